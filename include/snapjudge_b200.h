@@ -1,0 +1,168 @@
+/*
+ * snapjudge_b200.h — C ABI of the B200 (sm_100a) encoder forward for snapjudge.
+ *
+ * Two layers, both plain C: pointers, sizes, int status.
+ *
+ *  1. Kernel entry points — the five extern "C" launchers of the reference's
+ *     cuda/kernels.cu, in packed variable-length form (cu_seqlens instead of a
+ *     padded [B, L] batch) and returning a status instead of void.  Buffers are
+ *     caller-owned DEVICE memory; the call is asynchronous on `stream`
+ *     (a cudaStream_t passed as void*, NULL = legacy default stream).
+ *
+ *  2. The encoder engine (sj_fast_*) — what the reference's FastSnapjudge
+ *     (include/snapjudge/fast.hpp:15-31, cuda/fast.cpp) does: weights resident
+ *     on one GPU, the whole DecisionModel encoder (src/model.cpp:222-307) on
+ *     device, results back in host memory.  One engine per GPU; an engine is
+ *     not re-entrant (calls on one engine must not overlap; use one engine per
+ *     host thread, or serialise).
+ *
+ * bf16 values cross the ABI as their 16-bit patterns (sj_bf16).
+ * Status: SJ_OK (0) or a negative SJ_ERR_*; the message of the last failure on
+ * the calling thread is returned by sj_last_error(), and the engine's own by
+ * sj_fast_last_error(e).
+ */
+#ifndef SNAPJUDGE_B200_H
+#define SNAPJUDGE_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SJ_OK 0
+#define SJ_ERR_INVALID (-1)     /* bad argument, shape or input (message says which) */
+#define SJ_ERR_CUDA (-2)        /* a CUDA runtime call failed */
+#define SJ_ERR_UNSUPPORTED (-3) /* shape or option this build does not implement */
+#define SJ_ERR_TIMEOUT (-4)     /* a bounded device-side wait ran out (kernel returned early) */
+#define SJ_ERR_STATE (-5)       /* call out of order (e.g. forward before sj_fast_commit) */
+
+#define SJ_PREC_BF16 0 /* bf16 activations/weights, fp32 accumulation, fp32 residual stream */
+#define SJ_PREC_FP32 1 /* fp32 everywhere (parity mode: 1e-4 relative to the CPU forward) */
+
+#define SJ_HEAD_SOFTMAX 0
+#define SJ_HEAD_SIGMOID 1
+
+typedef uint16_t sj_bf16;
+
+/* Version of this ABI, major * 10000 + minor * 100 + patch. */
+int sj_b200_version(void);
+
+/* Message of the last failing call on this thread ("" if none). */
+const char* sj_last_error(void);
+
+/* ------------------------------------------------------------------------- */
+/* 1. Kernel entry points (device pointers, async on `stream`).              */
+/* ------------------------------------------------------------------------- */
+
+/* C[M,N] = act(A[M,K] W[N,K]^T + bias); act 0 none, 1 erf-GELU, 2 ReLU.
+ * bias (fp32 [N]) is read only when has_bias != 0.
+ * Replaces sj_gemm (cuda/kernels.cu:88-108). */
+int sj_gemm(const sj_bf16* A, const sj_bf16* W, const float* bias, sj_bf16* C, int M, int N,
+            int K, int has_bias, int act, void* stream);
+
+/* C[M,F] = gelu(A Wi[0:F]^T) * (A Wi[F:2F]^T), Wi [2F, K] in the checkpoint layout.
+ * Replaces sj_gemm_geglu (cuda/kernels.cu:168-174). */
+int sj_gemm_geglu(const sj_bf16* A, const sj_bf16* Wi, sj_bf16* C, int M, int F, int K,
+                  void* stream);
+
+/* X[M,D] (fp32) += R (bf16, when residual != 0); Y = LN(X) * w (+ b when has_bias).
+ * Replaces sj_add_ln (cuda/kernels.cu:243-254). */
+int sj_add_ln(float* X, const sj_bf16* R, const float* w, const float* b, sj_bf16* Y, int M,
+              int D, float eps, int residual, int has_bias, void* stream);
+
+/* In-place rotate-half RoPE on the q and k heads of packed qkv [T, 3*H*Dh];
+ * row r of segment b has position r - cu_seqlens[b]; cos/sin are fp32
+ * [max_pos, Dh/2] tables.  T = cu_seqlens[B] (read on the host from
+ * cu_seqlens_host, which must equal the device array).
+ * Replaces sj_rope (cuda/kernels.cu:282-288; position r % L there). */
+int sj_rope(sj_bf16* qkv, const float* cos_t, const float* sin_t, const int32_t* cu_seqlens,
+            const int32_t* cu_seqlens_host, int B, int H, int Dh, void* stream);
+
+/* Bidirectional attention over packed qkv [T, 3*H*Dh] -> O [T, H*Dh].
+ * Segment b = rows [cu_seqlens[b], cu_seqlens[b+1]); its queries attend keys
+ * j < kv_lens[b] of the same segment (kv_lens NULL: the whole segment) and,
+ * when window > 0, only |i - j| <= window.  softmax scale 1/sqrt(Dh), fp32
+ * accumulation.  cu_seqlens_host mirrors cu_seqlens for the tile schedule.
+ * Replaces sj_attn (cuda/kernels.cu:351-357; lens + padded L there). */
+int sj_attn(const sj_bf16* qkv, const int32_t* cu_seqlens, const int32_t* cu_seqlens_host,
+            const int32_t* kv_lens, sj_bf16* O, int B, int H, int Dh, int window, void* stream);
+
+/* ------------------------------------------------------------------------- */
+/* 2. Encoder engine (replaces FastSnapjudge, include/snapjudge/fast.hpp).    */
+/* ------------------------------------------------------------------------- */
+typedef struct sj_fast sj_fast;
+
+typedef struct sj_fast_config {
+  /* encoder/config.json, parsed as DecisionModel::load does (src/model.cpp:59-111) */
+  int hidden_size;
+  int num_hidden_layers;
+  int num_attention_heads;
+  int intermediate_size;
+  int vocab_size;
+  int max_position_embeddings;
+  float norm_eps;
+  int local_attention;          /* window = local_attention / 2 on sliding layers */
+  const int* layer_sliding;     /* [num_hidden_layers] 1 = sliding_attention; NULL = all full */
+  double rope_theta_full;
+  double rope_theta_sliding;
+  /* engine options */
+  int precision;                /* SJ_PREC_BF16 or SJ_PREC_FP32 */
+  int device;                   /* CUDA device ordinal */
+  int max_tokens;               /* tokens per device pass (workspace size); 0 = default */
+} sj_fast_config;
+
+/* Create an engine on cfg->device.  Weights are then given by name with
+ * sj_fast_set_tensor and uploaded by sj_fast_commit. */
+int sj_fast_create(const sj_fast_config* cfg, sj_fast** out);
+
+/* Stage one fp32 host tensor, named as in model.safetensors
+ * ("encoder.layers.3.attn.Wqkv.weight", ...).  The shape is checked against
+ * the config (the strict checks of src/model.cpp:17-33).  Decision heads on
+ * [CLS] are named "task_heads.<i>.weight" [n_out, D] / ".bias" [n_out]. */
+int sj_fast_set_tensor(sj_fast* e, const char* name, const float* host, const int64_t* shape,
+                       int ndim);
+
+/* Declare the [CLS] decision heads (n_heads <= 8, sum of n_out <= 64); kinds
+ * SJ_HEAD_SOFTMAX / SJ_HEAD_SIGMOID.  Call before sj_fast_commit. */
+int sj_fast_set_heads(sj_fast* e, int n_heads, const int* n_out, const int* kind);
+
+/* Check that every required tensor is present, convert and upload. */
+int sj_fast_commit(sj_fast* e);
+
+/* Encoder forward on packed sequences, host buffers in and out (synchronous).
+ * ids int64 [T], cu_seqlens int32 [B+1] (cu[0] = 0, non-decreasing,
+ * T = cu[B]); kv_lens int32 [B] or NULL (see sj_attn).  hidden fp32 [T, D] =
+ * final-norm hidden states, as DecisionModel::encode (src/model.cpp:222-307). */
+int sj_fast_encode(sj_fast* e, const int64_t* ids, const int32_t* cu_seqlens,
+                   const int32_t* kv_lens, int B, float* hidden);
+
+/* Encoder + [CLS] decision heads, host buffers (synchronous):
+ * probs fp32 [B, sum n_out] (heads in declaration order). */
+int sj_fast_decide(sj_fast* e, const int64_t* ids, const int32_t* cu_seqlens, int B,
+                   float* probs);
+
+/* Device-buffer variants, asynchronous on `stream` (NULL = the engine's
+ * stream).  T = cu_seqlens_host[B] must not exceed the engine's max_tokens.
+ * cu_seqlens_host mirrors the device array (it sizes the launches).
+ * hidden / cls may be NULL; probs may be NULL when no heads are set. */
+int sj_fast_encode_device(sj_fast* e, const int64_t* ids, const int32_t* cu_seqlens,
+                          const int32_t* cu_seqlens_host, const int32_t* kv_lens, int B,
+                          float* hidden, float* probs, void* stream);
+
+/* Wait for the engine's device work; reports device-side errors (an
+ * out-of-vocabulary id, a bounded wait that ran out) raised since the last
+ * check. */
+int sj_fast_sync(sj_fast* e, void* stream);
+
+/* Number of device kernel launches issued by the last forward (for audits). */
+int sj_fast_launch_count(const sj_fast* e);
+
+const char* sj_fast_last_error(const sj_fast* e);
+void sj_fast_destroy(sj_fast* e);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SNAPJUDGE_B200_H */

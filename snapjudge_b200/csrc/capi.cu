@@ -1,0 +1,130 @@
+// capi.cu — kernel-level C entry points (include/snapjudge_b200.h, part 1).
+//
+// The five launchers of the reference's cuda/kernels.cu (sj_gemm :88,
+// sj_gemm_geglu :168, sj_add_ln :243, sj_rope :282, sj_attn :351) with the
+// same argument meaning, in packed varlen form, returning a status.  They
+// allocate nothing: every buffer is the caller's.  Shapes the tcgen05 kernels
+// take go to them; the rest run on the CUDA-core kernels (never on the host).
+#include <string>
+
+#include "../../include/snapjudge_b200.h"
+#include "common.cuh"
+#include "kernels.h"
+
+using sjb::bf16;
+
+namespace {
+thread_local std::string g_err;
+
+int fail(int code, const std::string& m) {
+  g_err = m;
+  return code;
+}
+int launched(cudaError_t rc, const char* what) {
+  if (rc == cudaSuccess) return SJ_OK;
+  g_err = std::string("snapjudge CUDA: ") + what + ": " + cudaGetErrorString(rc);
+  return SJ_ERR_CUDA;
+}
+int check_cu(const int32_t* cu_host, int B, int* T, int* max_len) {
+  if (!cu_host) return fail(SJ_ERR_INVALID, "cu_seqlens_host is null");
+  if (B < 0) return fail(SJ_ERR_INVALID, "negative batch");
+  if (B > 0 && cu_host[0] != 0) return fail(SJ_ERR_INVALID, "cu_seqlens[0] must be 0");
+  int ml = 0;
+  for (int b = 0; b < B; ++b) {
+    int n = cu_host[b + 1] - cu_host[b];
+    if (n < 0) return fail(SJ_ERR_INVALID, "cu_seqlens must be non-decreasing");
+    ml = n > ml ? n : ml;
+  }
+  *T = B > 0 ? cu_host[B] : 0;
+  *max_len = ml;
+  return SJ_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int sj_b200_version(void) { return 100; }
+
+const char* sj_last_error(void) { return g_err.c_str(); }
+
+int sj_gemm(const sj_bf16* A, const sj_bf16* W, const float* bias, sj_bf16* C, int M, int N,
+            int K, int has_bias, int act, void* stream) {
+  if (M < 0 || N < 0 || K < 0) return fail(SJ_ERR_INVALID, "negative GEMM size");
+  if (act < 0 || act > 2) return fail(SJ_ERR_INVALID, "act must be 0, 1 or 2");
+  if ((M && K && !A) || (N && K && !W) || (M && N && !C) || (has_bias && !bias))
+    return fail(SJ_ERR_INVALID, "null GEMM operand");
+  auto st = static_cast<cudaStream_t>(stream);
+  const bf16* a = reinterpret_cast<const bf16*>(A);
+  const bf16* w = reinterpret_cast<const bf16*>(W);
+  bf16* c = reinterpret_cast<bf16*>(C);
+  const float* b = has_bias ? bias : nullptr;
+  if (sjb::gemm_tc_supported(M, N, K, false))
+    return launched(sjb::gemm_tc(a, w, b, c, nullptr, M, N, K, sjb::TC_STORE, act,
+                                 sjb::TcRope{}, nullptr, st),
+                    "gemm_tc");
+  return launched(sjb::gemm_simt<bf16, bf16>(a, w, b, c, nullptr, M, N, K, act, false, st),
+                  "gemm_simt");
+}
+
+int sj_gemm_geglu(const sj_bf16* A, const sj_bf16* Wi, sj_bf16* C, int M, int F, int K,
+                  void* stream) {
+  if (M < 0 || F < 0 || K < 0) return fail(SJ_ERR_INVALID, "negative GEMM size");
+  if ((M && K && !A) || (F && K && !Wi) || (M && F && !C))
+    return fail(SJ_ERR_INVALID, "null GEMM operand");
+  auto st = static_cast<cudaStream_t>(stream);
+  const bf16* a = reinterpret_cast<const bf16*>(A);
+  const bf16* w = reinterpret_cast<const bf16*>(Wi);
+  bf16* c = reinterpret_cast<bf16*>(C);
+  if (sjb::gemm_tc_supported(M, F, K, true))
+    return launched(sjb::gemm_tc(a, w, nullptr, c, nullptr, M, F, K, sjb::TC_GEGLU, 0,
+                                 sjb::TcRope{}, nullptr, st),
+                    "gemm_tc");
+  return launched(sjb::gemm_simt<bf16, bf16>(a, w, nullptr, c, nullptr, M, F, K, 0, true, st),
+                  "gemm_simt");
+}
+
+int sj_add_ln(float* X, const sj_bf16* R, const float* w, const float* b, sj_bf16* Y, int M,
+              int D, float eps, int residual, int has_bias, void* stream) {
+  if (M < 0 || D <= 0) return fail(SJ_ERR_INVALID, "bad LayerNorm size");
+  if (M && (!X || !w || !Y || (residual && !R) || (has_bias && !b)))
+    return fail(SJ_ERR_INVALID, "null LayerNorm operand");
+  return launched(sjb::add_ln<bf16, bf16>(X, residual ? reinterpret_cast<const bf16*>(R) : nullptr,
+                                          w, has_bias ? b : nullptr, reinterpret_cast<bf16*>(Y),
+                                          M, D, eps, nullptr, static_cast<cudaStream_t>(stream)),
+                  "add_ln");
+}
+
+int sj_rope(sj_bf16* qkv, const float* cos_t, const float* sin_t, const int32_t* cu_seqlens,
+            const int32_t* cu_seqlens_host, int B, int H, int Dh, void* stream) {
+  int T = 0, ml = 0, s;
+  if ((s = check_cu(cu_seqlens_host, B, &T, &ml))) return s;
+  if (H <= 0 || Dh <= 0 || Dh % 2) return fail(SJ_ERR_INVALID, "bad head shape");
+  if (T && (!qkv || !cos_t || !sin_t || !cu_seqlens))
+    return fail(SJ_ERR_INVALID, "null RoPE operand");
+  return launched(sjb::rope_cu(reinterpret_cast<bf16*>(qkv), cos_t, sin_t, cu_seqlens, B, T, H,
+                               Dh, static_cast<cudaStream_t>(stream)),
+                  "rope");
+}
+
+int sj_attn(const sj_bf16* qkv, const int32_t* cu_seqlens, const int32_t* cu_seqlens_host,
+            const int32_t* kv_lens, sj_bf16* O, int B, int H, int Dh, int window, void* stream) {
+  int T = 0, ml = 0, s;
+  if ((s = check_cu(cu_seqlens_host, B, &T, &ml))) return s;
+  if (H <= 0 || window < 0) return fail(SJ_ERR_INVALID, "bad attention shape");
+  if (T && (!qkv || !O || !cu_seqlens)) return fail(SJ_ERR_INVALID, "null attention operand");
+  if (T == 0) return SJ_OK;
+  auto st = static_cast<cudaStream_t>(stream);
+  const bf16* q = reinterpret_cast<const bf16*>(qkv);
+  bf16* o = reinterpret_cast<bf16*>(O);
+  if (sjb::attn_tc_supported(Dh))
+    return launched(sjb::attn_tc(q, cu_seqlens, kv_lens, o, T, H, window, nullptr, 0, B, ml,
+                                 nullptr, st),
+                    "attn_tc");
+  if (Dh != 8 && Dh != 16 && Dh != 32 && Dh != 64 && Dh != 128)
+    return fail(SJ_ERR_UNSUPPORTED, "head_dim must be 8, 16, 32, 64 or 128");
+  return launched(sjb::attn_simt<bf16>(q, cu_seqlens, kv_lens, o, H, Dh, window, nullptr, 0, B, ml,
+                                       st),
+                  "attn_simt");
+}
+
+}  // extern "C"

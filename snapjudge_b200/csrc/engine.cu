@@ -1,0 +1,614 @@
+// engine.cu — the encoder engine behind sj_fast_* (include/snapjudge_b200.h).
+//
+// Device-resident replacement of the reference FastSnapjudge
+// (include/snapjudge/fast.hpp:15-31, cuda/fast.cpp) running the encoder half
+// of DecisionModel (src/model.cpp:222-307) on packed variable-length batches:
+//
+//   pos  = position of each packed row (rope.cu)
+//   X    = LN(emb[ids]) (fp32 residual stream), Y = act(X)       (norm.cu)
+//   per layer:
+//     Y    = LN(X) * attn_norm            (identity when absent, layer 0)
+//     QKV  = Y Wqkv^T, RoPE on q,k        (tcgen05 GEMM, RoPE epilogue)
+//     O    = attention(QKV)               (tcgen05 flash attention)
+//     X   += O Wo^T                       (GEMM, fp32 residual epilogue)
+//     Y    = LN(X) * mlp_norm
+//     G    = gelu(Y Wg^T) * (Y Wu^T)      (GEMM, GEGLU epilogue)
+//     X   += G Wo2^T
+//   hidden = LN(X) * final_norm (+ LoRA); heads on the [CLS] rows
+//
+// bf16 mode: bf16 weights/activations, fp32 accumulation, fp32 residual and
+// norms.  fp32 mode: every tensor fp32, CUDA-core GEMM and attention.
+// Workspace is allocated once for `max_tokens` rows; host calls split larger
+// batches into passes of whole sequences.
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <string>
+#include <type_traits>
+#include <vector>
+
+#include "../../include/snapjudge_b200.h"
+#include "common.cuh"
+#include "kernels.h"
+
+using sjb::bf16;
+
+namespace {
+
+struct HostTensor {
+  std::vector<float> data;
+  std::vector<int64_t> shape;
+};
+
+std::string shape_str(const std::vector<int64_t>& s) {
+  std::string o = "[";
+  for (size_t i = 0; i < s.size(); ++i) o += (i ? "," : "") + std::to_string(s[i]);
+  return o + "]";
+}
+
+struct LayerDev {
+  float* attn_norm = nullptr;  // null: identity (reference layer 0)
+  float* mlp_norm = nullptr;
+  void* wqkv = nullptr;        // [3D, D]
+  void* wo = nullptr;          // [D, D]
+  void* wi = nullptr;          // [2F, D]  (gate rows, then up rows)
+  void* wo2 = nullptr;         // [D, F]
+  int window = 0;
+  bool sliding = false;
+};
+
+}  // namespace
+
+struct sj_fast {
+  sj_fast_config cfg{};
+  std::vector<int> sliding;
+  int D = 0, H = 0, Dh = 0, F = 0, V = 0, NL = 0;
+  int max_tokens = 0;
+  bool bf16_mode = true;
+  bool committed = false;
+  cudaStream_t stream = nullptr;
+  std::string err;
+  int launches = 0;
+
+  std::map<std::string, HostTensor> staged;
+  std::vector<void*> allocs;
+
+  // weights
+  float* emb = nullptr;
+  float* emb_norm = nullptr;
+  float* final_norm = nullptr;
+  std::vector<LayerDev> layers;
+  float *cos_f = nullptr, *sin_f = nullptr, *cos_s = nullptr, *sin_s = nullptr;
+  int lora_r = 0;
+  float *lora_a = nullptr, *lora_b = nullptr;
+  sjb::HeadSpec spec{};
+  bool has_heads = false;
+  float *head_w = nullptr, *head_b = nullptr;
+
+  // workspace
+  float* X = nullptr;
+  void *Y = nullptr, *QKV = nullptr, *O = nullptr, *G = nullptr;
+  int32_t* pos = nullptr;
+  int64_t* ids = nullptr;
+  int32_t* cu = nullptr;
+  int32_t* kvl = nullptr;
+  int2* tiles = nullptr;
+  int max_tiles = 0;
+  float* Hc = nullptr;    // [max_tokens, D] normalised [CLS] rows
+  float* probs = nullptr; // [max_tokens, n_total]
+  float* hid = nullptr;   // [max_tokens, D] fp32 hidden (host-API staging)
+  float* z = nullptr;     // LoRA [max_tokens, r]
+  int* dflags = nullptr;  // device error flags: [0] bad id, [1] gemm wait, [2] attn wait
+  // pinned host staging
+  int2* h_tiles = nullptr;
+  int32_t* h_cu = nullptr;
+  int32_t* h_kvl = nullptr;
+  cudaEvent_t staged_ev = nullptr;
+
+  int fail(int code, const std::string& m) {
+    err = m;
+    return code;
+  }
+  int cuda_fail(cudaError_t rc, const char* what) {
+    err = std::string("snapjudge CUDA: ") + what + ": " + cudaGetErrorString(rc);
+    return SJ_ERR_CUDA;
+  }
+  template <typename T>
+  cudaError_t dalloc(T** p, size_t n) {
+    void* q = nullptr;
+    cudaError_t rc = cudaMalloc(&q, n * sizeof(T) > 0 ? n * sizeof(T) : 16);
+    if (rc == cudaSuccess) allocs.push_back(q);
+    *p = static_cast<T*>(q);
+    return rc;
+  }
+  ~sj_fast() {
+    cudaSetDevice(cfg.device);
+    if (stream) cudaStreamSynchronize(stream);
+    for (void* p : allocs) cudaFree(p);
+    if (h_tiles) cudaFreeHost(h_tiles);
+    if (h_cu) cudaFreeHost(h_cu);
+    if (h_kvl) cudaFreeHost(h_kvl);
+    if (staged_ev) cudaEventDestroy(staged_ev);
+    if (stream) cudaStreamDestroy(stream);
+  }
+
+  const HostTensor* get(const std::string& n) const {
+    auto it = staged.find(n);
+    return it == staged.end() ? nullptr : &it->second;
+  }
+  int require(const std::string& n, std::vector<int64_t> want, const HostTensor** out) {
+    const HostTensor* t = get(n);
+    if (!t) return fail(SJ_ERR_INVALID, "Model weights incomplete: missing tensor " + n);
+    if (t->shape != want)
+      return fail(SJ_ERR_INVALID, "Model architecture mismatch: " + n + " expected " +
+                                      shape_str(want) + " but checkpoint has " + shape_str(t->shape));
+    *out = t;
+    return SJ_OK;
+  }
+  int upload_f32(const HostTensor* t, float** dst) {
+    cudaError_t rc = dalloc(dst, t->data.size());
+    if (rc != cudaSuccess) return cuda_fail(rc, "cudaMalloc");
+    rc = cudaMemcpy(*dst, t->data.data(), t->data.size() * sizeof(float), cudaMemcpyHostToDevice);
+    return rc == cudaSuccess ? SJ_OK : cuda_fail(rc, "cudaMemcpy");
+  }
+  // GEMM weight in the activation precision (bf16 round-to-nearest-even or fp32)
+  int upload_w(const HostTensor* t, void** dst) {
+    if (!bf16_mode) return upload_f32(t, reinterpret_cast<float**>(dst));
+    std::vector<bf16> tmp(t->data.size());
+    for (size_t i = 0; i < tmp.size(); ++i) tmp[i] = __float2bfloat16_rn(t->data[i]);
+    bf16* p = nullptr;
+    cudaError_t rc = dalloc(&p, tmp.size());
+    if (rc != cudaSuccess) return cuda_fail(rc, "cudaMalloc");
+    rc = cudaMemcpy(p, tmp.data(), tmp.size() * sizeof(bf16), cudaMemcpyHostToDevice);
+    *dst = p;
+    return rc == cudaSuccess ? SJ_OK : cuda_fail(rc, "cudaMemcpy");
+  }
+
+  int commit();
+  template <typename T>
+  int forward(const int64_t* d_ids, const int32_t* d_cu, const int32_t* hcu,
+              const int32_t* d_kvl, int B, int ntok, float* d_hidden, float* d_probs,
+              cudaStream_t st);
+  int run(const int64_t* d_ids, const int32_t* d_cu, const int32_t* hcu, const int32_t* d_kvl,
+          int B, float* d_hidden, float* d_probs, cudaStream_t st);
+  int check_flags(cudaStream_t st);
+  int host_call(const int64_t* ids_h, const int32_t* cu_h, const int32_t* kvl_h, int B,
+                float* hidden_h, float* probs_h);
+};
+
+// ------------------------------------------------------------------ commit
+int sj_fast::commit() {
+  if (committed) return fail(SJ_ERR_STATE, "sj_fast_commit: already committed");
+  cudaError_t rc = cudaSetDevice(cfg.device);
+  if (rc != cudaSuccess) return cuda_fail(rc, "cudaSetDevice");
+  const HostTensor* t = nullptr;
+  int s;
+  if ((s = require("encoder.embeddings.tok_embeddings.weight", {V, D}, &t))) return s;
+  if ((s = upload_f32(t, &emb))) return s;
+  if ((s = require("encoder.embeddings.norm.weight", {D}, &t))) return s;
+  if ((s = upload_f32(t, &emb_norm))) return s;
+  if ((s = require("encoder.final_norm.weight", {D}, &t))) return s;
+  if ((s = upload_f32(t, &final_norm))) return s;
+  layers.resize(NL);
+  const int win = cfg.local_attention > 0 ? cfg.local_attention / 2 : 0;
+  for (int i = 0; i < NL; ++i) {
+    LayerDev& ly = layers[i];
+    std::string p = "encoder.layers." + std::to_string(i) + ".";
+    ly.sliding = sliding[i] != 0;
+    ly.window = ly.sliding ? win : 0;
+    if (get(p + "attn_norm.weight")) {
+      if ((s = require(p + "attn_norm.weight", {D}, &t))) return s;
+      if ((s = upload_f32(t, &ly.attn_norm))) return s;
+    }
+    if ((s = require(p + "attn.Wqkv.weight", {3 * (int64_t)D, D}, &t))) return s;
+    if ((s = upload_w(t, &ly.wqkv))) return s;
+    if ((s = require(p + "attn.Wo.weight", {D, D}, &t))) return s;
+    if ((s = upload_w(t, &ly.wo))) return s;
+    if ((s = require(p + "mlp_norm.weight", {D}, &t))) return s;
+    if ((s = upload_f32(t, &ly.mlp_norm))) return s;
+    if ((s = require(p + "mlp.Wi.weight", {2 * (int64_t)F, D}, &t))) return s;
+    if ((s = upload_w(t, &ly.wi))) return s;
+    if ((s = require(p + "mlp.Wo.weight", {D, F}, &t))) return s;
+    if ((s = upload_w(t, &ly.wo2))) return s;
+  }
+  // optional encoder-output LoRA (src/model.cpp:192-203)
+  const HostTensor* la = get("lora_A.weight");
+  const HostTensor* lb = get("lora_B.weight");
+  if (la && lb) {
+    if (la->shape.size() != 2 || lb->shape.size() != 2 || la->shape[0] != lb->shape[1] ||
+        la->shape[1] != D || lb->shape[0] != D)
+      return fail(SJ_ERR_INVALID, "Model 'lora_A.weight'/'lora_B.weight' must be [r,D] and [D,r]");
+    lora_r = (int)la->shape[0];
+    if ((s = upload_f32(la, &lora_a))) return s;
+    if ((s = upload_f32(lb, &lora_b))) return s;
+  }
+  // RoPE tables: fp64 angles cast to fp32, as src/model.cpp:173-190
+  {
+    const int64_t half = Dh / 2, L = cfg.max_position_embeddings;
+    HostTensor c, sn;
+    c.data.resize(L * half);
+    sn.data.resize(L * half);
+    for (int which = 0; which < 2; ++which) {
+      double theta = which == 0 ? cfg.rope_theta_full : cfg.rope_theta_sliding;
+      for (int64_t p = 0; p < L; ++p)
+        for (int64_t d = 0; d < half; ++d) {
+          double inv = 1.0 / std::pow(theta, 2.0 * (double)d / Dh);
+          double fr = (double)p * inv;
+          c.data[p * half + d] = (float)std::cos(fr);
+          sn.data[p * half + d] = (float)std::sin(fr);
+        }
+      if ((s = upload_f32(&c, which == 0 ? &cos_f : &cos_s))) return s;
+      if ((s = upload_f32(&sn, which == 0 ? &sin_f : &sin_s))) return s;
+    }
+  }
+  // decision heads
+  if (has_heads) {
+    HostTensor w, b;
+    for (int h = 0; h < spec.n_heads; ++h) {
+      std::string p = "task_heads." + std::to_string(h) + ".";
+      if ((s = require(p + "weight", {spec.n_out[h], D}, &t))) return s;
+      w.data.insert(w.data.end(), t->data.begin(), t->data.end());
+      if ((s = require(p + "bias", {spec.n_out[h]}, &t))) return s;
+      b.data.insert(b.data.end(), t->data.begin(), t->data.end());
+    }
+    if ((s = upload_f32(&w, &head_w))) return s;
+    if ((s = upload_f32(&b, &head_b))) return s;
+  }
+  // workspace
+  const size_t T = (size_t)max_tokens, es = bf16_mode ? 2 : 4;
+  max_tiles = max_tokens / 64 + max_tokens + 1;
+  if ((rc = dalloc(&X, T * D)) || (rc = dalloc((char**)&Y, T * D * es)) ||
+      (rc = dalloc((char**)&QKV, T * 3 * D * es)) || (rc = dalloc((char**)&O, T * D * es)) ||
+      (rc = dalloc((char**)&G, T * F * es)) || (rc = dalloc(&pos, T)) || (rc = dalloc(&ids, T)) ||
+      (rc = dalloc(&cu, T + 1)) || (rc = dalloc(&kvl, T)) || (rc = dalloc(&tiles, max_tiles)) ||
+      (rc = dalloc(&Hc, T * D)) || (rc = dalloc(&probs, T * (size_t)std::max(1, spec.n_total))) ||
+      (rc = dalloc(&hid, T * D)) || (rc = dalloc(&z, T * (size_t)std::max(1, lora_r))) ||
+      (rc = dalloc(&dflags, 8)))
+    return cuda_fail(rc, "cudaMalloc (workspace)");
+  if ((rc = cudaMemset(dflags, 0, 8 * sizeof(int)))) return cuda_fail(rc, "cudaMemset");
+  if ((rc = cudaMallocHost(&h_tiles, max_tiles * sizeof(int2))) ||
+      (rc = cudaMallocHost(&h_cu, (T + 1) * sizeof(int32_t))) ||
+      (rc = cudaMallocHost(&h_kvl, T * sizeof(int32_t))))
+    return cuda_fail(rc, "cudaMallocHost");
+  if ((rc = cudaEventCreateWithFlags(&staged_ev, cudaEventDisableTiming)))
+    return cuda_fail(rc, "cudaEventCreate");
+  if ((rc = cudaEventRecord(staged_ev, stream))) return cuda_fail(rc, "cudaEventRecord");
+  staged.clear();
+  committed = true;
+  return SJ_OK;
+}
+
+// ------------------------------------------------------------------ forward
+#define SJ_LAUNCH(expr)                                    \
+  do {                                                     \
+    cudaError_t rc_ = (expr);                              \
+    ++launches;                                            \
+    if (rc_ != cudaSuccess) return cuda_fail(rc_, #expr);  \
+  } while (0)
+
+template <typename T>
+int sj_fast::forward(const int64_t* d_ids, const int32_t* d_cu, const int32_t* hcu,
+                     const int32_t* d_kvl, int B, int ntok, float* d_hidden, float* d_probs,
+                     cudaStream_t st) {
+  constexpr bool kBf16 = std::is_same<T, bf16>::value;
+  const bool tc_attn = kBf16 && sjb::attn_tc_supported(Dh);
+  const int qt = tc_attn ? 128 : 64;
+  // query-tile schedule, longest segments first (they take the longest)
+  cudaError_t rc = cudaEventSynchronize(staged_ev);  // previous upload of h_tiles done
+  if (rc != cudaSuccess) return cuda_fail(rc, "cudaEventSynchronize");
+  std::vector<int> order(B);
+  for (int b = 0; b < B; ++b) order[b] = b;
+  std::stable_sort(order.begin(), order.end(), [&](int a, int b) {
+    return hcu[a + 1] - hcu[a] > hcu[b + 1] - hcu[b];
+  });
+  int nt = 0;
+  for (int b : order) {
+    const int n = hcu[b + 1] - hcu[b];
+    for (int q0 = 0; q0 < n; q0 += qt) {
+      if (nt >= max_tiles) return fail(SJ_ERR_INVALID, "too many query tiles");
+      h_tiles[nt++] = make_int2(b, q0);
+    }
+  }
+  if (nt > 0) {
+    rc = cudaMemcpyAsync(tiles, h_tiles, nt * sizeof(int2), cudaMemcpyHostToDevice, st);
+    if (rc != cudaSuccess) return cuda_fail(rc, "cudaMemcpyAsync (tiles)");
+  }
+  if ((rc = cudaEventRecord(staged_ev, st))) return cuda_fail(rc, "cudaEventRecord");
+
+  T* Yt = static_cast<T*>(Y);
+  T* Qt = static_cast<T*>(QKV);
+  T* Ot = static_cast<T*>(O);
+  T* Gt = static_cast<T*>(G);
+  const float eps = cfg.norm_eps;
+  SJ_LAUNCH(sjb::positions(d_cu, B, ntok, pos, nullptr, st));
+  const bool y0 = !layers.empty() && !layers[0].attn_norm;
+  SJ_LAUNCH(sjb::embed_ln<T>(d_ids, ntok, emb, V, D, emb_norm, eps, X, y0 ? Yt : nullptr, dflags, st));
+
+  auto gemm = [&](const T* A, const void* W, T* C, float* resid, int N, int K, int epi,
+                  const float* ct, const float* stb) -> int {
+    if constexpr (kBf16) {
+      const bool geglu = epi == sjb::TC_GEGLU;
+      if (sjb::gemm_tc_supported(ntok, N, K, geglu) &&
+          (epi != sjb::TC_ROPE || Dh == 64)) {
+        sjb::TcRope rp{ct, stb, pos, H};
+        SJ_LAUNCH(sjb::gemm_tc(A, static_cast<const bf16*>(W), nullptr, C, resid, ntok, N, K, epi,
+                               0, rp, dflags + 1, st));
+        return SJ_OK;
+      }
+    }
+    SJ_LAUNCH((sjb::gemm_simt<T, T>(A, static_cast<const T*>(W), nullptr, C, resid, ntok, N, K, 0,
+                                    epi == sjb::TC_GEGLU, st)));
+    if (epi == sjb::TC_ROPE) SJ_LAUNCH(sjb::rope<T>(C, ct, stb, pos, ntok, H, Dh, st));
+    return SJ_OK;
+  };
+
+  int s;
+  for (int li = 0; li < NL; ++li) {
+    const LayerDev& ly = layers[li];
+    const T* Yin = Yt;
+    if (ly.attn_norm) {
+      SJ_LAUNCH((sjb::add_ln<T, T>(X, nullptr, ly.attn_norm, nullptr, Yt, ntok, D, eps, nullptr, st)));
+    } else if (li > 0) {
+      if constexpr (kBf16) SJ_LAUNCH(sjb::cast_bf16(X, Yt, (int64_t)ntok * D, st));
+      else Yin = reinterpret_cast<const T*>(X);
+    }
+    const float* ct = ly.sliding ? cos_s : cos_f;
+    const float* stb = ly.sliding ? sin_s : sin_f;
+    if ((s = gemm(Yin, ly.wqkv, Qt, nullptr, 3 * D, D, sjb::TC_ROPE, ct, stb))) return s;
+    if (tc_attn) {
+      if constexpr (kBf16)
+        SJ_LAUNCH(sjb::attn_tc(Qt, d_cu, d_kvl, Ot, ntok, H, ly.window, tiles, nt, B, 0, dflags + 2,
+                               st));
+    } else {
+      SJ_LAUNCH(sjb::attn_simt<T>(Qt, d_cu, d_kvl, Ot, H, Dh, ly.window, tiles, nt, B, 0, st));
+    }
+    if ((s = gemm(Ot, ly.wo, nullptr, X, D, D, sjb::TC_RESID, nullptr, nullptr))) return s;
+    SJ_LAUNCH((sjb::add_ln<T, T>(X, nullptr, ly.mlp_norm, nullptr, Yt, ntok, D, eps, nullptr, st)));
+    if ((s = gemm(Yt, ly.wi, Gt, nullptr, F, D, sjb::TC_GEGLU, nullptr, nullptr))) return s;
+    if ((s = gemm(Gt, ly.wo2, nullptr, X, D, F, sjb::TC_RESID, nullptr, nullptr))) return s;
+  }
+  // final norm (+ LoRA): all rows -> d_hidden, [CLS] rows -> heads
+  if (d_hidden) {
+    SJ_LAUNCH((sjb::add_ln<float, float>(X, nullptr, final_norm, nullptr, d_hidden, ntok, D, eps,
+                                         nullptr, st)));
+    if (lora_r > 0) {
+      SJ_LAUNCH((sjb::gemm_simt<float, float>(d_hidden, lora_a, nullptr, z, nullptr, ntok, lora_r, D,
+                                              0, false, st)));
+      SJ_LAUNCH((sjb::gemm_simt<float, float>(z, lora_b, nullptr, nullptr, d_hidden, ntok, D,
+                                              lora_r, 0, false, st)));
+    }
+  }
+  if (d_probs && has_heads) {
+    SJ_LAUNCH((sjb::add_ln<float, float>(X, nullptr, final_norm, nullptr, Hc, B, D, eps, d_cu, st)));
+    if (lora_r > 0) {
+      SJ_LAUNCH((sjb::gemm_simt<float, float>(Hc, lora_a, nullptr, z, nullptr, B, lora_r, D, 0,
+                                              false, st)));
+      SJ_LAUNCH((sjb::gemm_simt<float, float>(z, lora_b, nullptr, nullptr, Hc, B, D, lora_r, 0,
+                                              false, st)));
+    }
+    SJ_LAUNCH(sjb::dec_heads(Hc, B, D, head_w, head_b, spec, d_probs, st));
+  }
+  return SJ_OK;
+}
+
+int sj_fast::run(const int64_t* d_ids, const int32_t* d_cu, const int32_t* hcu,
+                 const int32_t* d_kvl, int B, float* d_hidden, float* d_probs, cudaStream_t st) {
+  if (!committed) return fail(SJ_ERR_STATE, "forward before sj_fast_commit");
+  if (B < 0) return fail(SJ_ERR_INVALID, "negative batch");
+  if (B == 0) return SJ_OK;
+  if (hcu[0] != 0) return fail(SJ_ERR_INVALID, "cu_seqlens[0] must be 0");
+  for (int b = 0; b < B; ++b) {
+    const int n = hcu[b + 1] - hcu[b];
+    if (n < 0) return fail(SJ_ERR_INVALID, "cu_seqlens must be non-decreasing");
+    if (n > cfg.max_position_embeddings)
+      return fail(SJ_ERR_INVALID, "sequence " + std::to_string(b) + " has " + std::to_string(n) +
+                                      " tokens > max_position_embeddings " +
+                                      std::to_string(cfg.max_position_embeddings));
+    if (d_probs && has_heads && n == 0)
+      return fail(SJ_ERR_INVALID, "sequence " + std::to_string(b) + " is empty (no [CLS] row)");
+  }
+  const int T = hcu[B];
+  if (T > max_tokens)
+    return fail(SJ_ERR_INVALID, "batch of " + std::to_string(T) + " tokens exceeds max_tokens " +
+                                    std::to_string(max_tokens));
+  if (T == 0) return SJ_OK;
+  launches = 0;
+  cudaError_t rc = cudaSetDevice(cfg.device);
+  if (rc != cudaSuccess) return cuda_fail(rc, "cudaSetDevice");
+  return bf16_mode ? forward<bf16>(d_ids, d_cu, hcu, d_kvl, B, T, d_hidden, d_probs, st)
+                   : forward<float>(d_ids, d_cu, hcu, d_kvl, B, T, d_hidden, d_probs, st);
+}
+
+int sj_fast::check_flags(cudaStream_t st) {
+  int h[8];
+  cudaError_t rc = cudaMemcpyAsync(h, dflags, sizeof(h), cudaMemcpyDeviceToHost, st);
+  if (rc == cudaSuccess) rc = cudaStreamSynchronize(st);
+  if (rc != cudaSuccess) return cuda_fail(rc, "device sync");
+  if (h[0] || h[1] || h[2]) {
+    cudaMemsetAsync(dflags, 0, sizeof(h), st);
+    cudaStreamSynchronize(st);
+    if (h[0]) return fail(SJ_ERR_INVALID, "input id out of vocabulary range");
+    return fail(SJ_ERR_TIMEOUT, std::string("a bounded device wait ran out in the ") +
+                                    (h[1] ? "GEMM" : "attention") + " kernel (code " +
+                                    std::to_string(h[1] ? h[1] : h[2]) + ")");
+  }
+  return SJ_OK;
+}
+
+int sj_fast::host_call(const int64_t* ids_h, const int32_t* cu_h, const int32_t* kvl_h, int B,
+                       float* hidden_h, float* probs_h) {
+  if (!committed) return fail(SJ_ERR_STATE, "forward before sj_fast_commit");
+  if (B <= 0) return B == 0 ? SJ_OK : fail(SJ_ERR_INVALID, "negative batch");
+  if (!cu_h || (!ids_h && cu_h[B] > 0)) return fail(SJ_ERR_INVALID, "null input");
+  if (probs_h && !has_heads) return fail(SJ_ERR_STATE, "no decision heads set");
+  if (cu_h[0] != 0) return fail(SJ_ERR_INVALID, "cu_seqlens[0] must be 0");
+  for (int b = 0; b < B; ++b) {
+    if (cu_h[b + 1] < cu_h[b]) return fail(SJ_ERR_INVALID, "cu_seqlens must be non-decreasing");
+    if (kvl_h && (kvl_h[b] < 0 || kvl_h[b] > cu_h[b + 1] - cu_h[b]))
+      return fail(SJ_ERR_INVALID, "kv_lens[b] must lie in [0, length of segment b]");
+  }
+  for (int64_t r = 0; r < cu_h[B]; ++r)
+    if (ids_h[r] < 0 || ids_h[r] >= V)
+      return fail(SJ_ERR_INVALID, "input id " + std::to_string(ids_h[r]) + " at row " +
+                                      std::to_string(r) + " outside [0, vocab_size)");
+  cudaError_t rc = cudaSetDevice(cfg.device);
+  if (rc != cudaSuccess) return cuda_fail(rc, "cudaSetDevice");
+  const int nout = std::max(1, spec.n_total);
+  int b0 = 0;
+  while (b0 < B) {
+    // largest run of whole sequences that fits the workspace
+    int b1 = b0;
+    while (b1 < B && cu_h[b1 + 1] - cu_h[b0] <= max_tokens) ++b1;
+    if (b1 == b0)
+      return fail(SJ_ERR_INVALID, "sequence longer than max_tokens");
+    const int nb = b1 - b0, base = cu_h[b0], T = cu_h[b1] - base;
+    rc = cudaEventSynchronize(staged_ev);
+    if (rc != cudaSuccess) return cuda_fail(rc, "cudaEventSynchronize");
+    for (int b = 0; b <= nb; ++b) h_cu[b] = cu_h[b0 + b] - base;
+    if (kvl_h) for (int b = 0; b < nb; ++b) h_kvl[b] = kvl_h[b0 + b];
+    if ((rc = cudaMemcpyAsync(ids, ids_h + base, T * sizeof(int64_t), cudaMemcpyHostToDevice,
+                              stream)) ||
+        (rc = cudaMemcpyAsync(cu, h_cu, (nb + 1) * sizeof(int32_t), cudaMemcpyHostToDevice,
+                              stream)) ||
+        (kvl_h && (rc = cudaMemcpyAsync(kvl, h_kvl, nb * sizeof(int32_t),
+                                        cudaMemcpyHostToDevice, stream))))
+      return cuda_fail(rc, "cudaMemcpyAsync (inputs)");
+    // h_cu is read by run() for the schedule; it is pinned host memory that
+    // stays untouched until the next pass's event wait above.
+    int s = run(ids, cu, h_cu, kvl_h ? kvl : nullptr, nb, hidden_h ? hid : nullptr,
+                probs_h ? probs : nullptr, stream);
+    if (s) return s;
+    if (hidden_h && (rc = cudaMemcpyAsync(hidden_h + (int64_t)base * D, hid,
+                                          (size_t)T * D * sizeof(float), cudaMemcpyDeviceToHost,
+                                          stream)))
+      return cuda_fail(rc, "cudaMemcpyAsync (hidden)");
+    if (probs_h && (rc = cudaMemcpyAsync(probs_h + (int64_t)b0 * nout, probs,
+                                         (size_t)nb * nout * sizeof(float),
+                                         cudaMemcpyDeviceToHost, stream)))
+      return cuda_fail(rc, "cudaMemcpyAsync (probs)");
+    if ((rc = cudaEventRecord(staged_ev, stream))) return cuda_fail(rc, "cudaEventRecord");
+    b0 = b1;
+  }
+  return check_flags(stream);
+}
+
+// ------------------------------------------------------------------ C ABI
+extern "C" {
+
+int sj_fast_create(const sj_fast_config* cfg, sj_fast** out) {
+  if (!cfg || !out) return SJ_ERR_INVALID;
+  *out = nullptr;
+  std::unique_ptr<sj_fast> e(new sj_fast());
+  e->cfg = *cfg;
+  const sj_fast_config& c = *cfg;
+  if (c.hidden_size <= 0 || c.num_attention_heads <= 0 || c.num_hidden_layers < 0 ||
+      c.intermediate_size <= 0 || c.vocab_size <= 0 || c.max_position_embeddings <= 0 ||
+      c.hidden_size % c.num_attention_heads != 0 ||
+      (c.hidden_size / c.num_attention_heads) % 2 != 0)
+    return SJ_ERR_INVALID;
+  if (c.precision != SJ_PREC_BF16 && c.precision != SJ_PREC_FP32) return SJ_ERR_UNSUPPORTED;
+  e->D = c.hidden_size;
+  e->H = c.num_attention_heads;
+  e->Dh = e->D / e->H;
+  e->F = c.intermediate_size;
+  e->V = c.vocab_size;
+  e->NL = c.num_hidden_layers;
+  e->bf16_mode = c.precision == SJ_PREC_BF16;
+  e->max_tokens = c.max_tokens > 0 ? c.max_tokens : (e->bf16_mode ? 262144 : 65536);
+  e->max_tokens = std::max(e->max_tokens, 128);
+  e->sliding.assign(e->NL, 0);
+  if (c.layer_sliding)
+    for (int i = 0; i < e->NL; ++i) e->sliding[i] = c.layer_sliding[i];
+  e->cfg.layer_sliding = nullptr;  // not retained
+  if (e->bf16_mode && (e->D % 8 != 0 || e->F % 8 != 0)) return SJ_ERR_UNSUPPORTED;
+  cudaError_t rc = cudaSetDevice(c.device);
+  if (rc == cudaSuccess) rc = cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking);
+  if (rc != cudaSuccess) return SJ_ERR_CUDA;
+  *out = e.release();
+  return SJ_OK;
+}
+
+int sj_fast_set_tensor(sj_fast* e, const char* name, const float* host, const int64_t* shape,
+                       int ndim) {
+  if (!e || !name || !host || (ndim > 0 && !shape) || ndim < 0 || ndim > 8)
+    return SJ_ERR_INVALID;
+  if (e->committed) return e->fail(SJ_ERR_STATE, "sj_fast_set_tensor after sj_fast_commit");
+  HostTensor t;
+  int64_t n = 1;
+  for (int i = 0; i < ndim; ++i) {
+    if (shape[i] < 0) return e->fail(SJ_ERR_INVALID, std::string("negative dim in ") + name);
+    t.shape.push_back(shape[i]);
+    n *= shape[i];
+  }
+  t.data.assign(host, host + n);
+  e->staged[name] = std::move(t);
+  return SJ_OK;
+}
+
+int sj_fast_set_heads(sj_fast* e, int n_heads, const int* n_out, const int* kind) {
+  if (!e) return SJ_ERR_INVALID;
+  if (e->committed) return e->fail(SJ_ERR_STATE, "sj_fast_set_heads after sj_fast_commit");
+  if (n_heads < 0 || n_heads > 8 || (n_heads > 0 && (!n_out || !kind)))
+    return e->fail(SJ_ERR_INVALID, "n_heads must be in [0, 8]");
+  sjb::HeadSpec s{};
+  s.n_heads = n_heads;
+  int off = 0;
+  for (int h = 0; h < n_heads; ++h) {
+    if (n_out[h] <= 0 || (kind[h] != SJ_HEAD_SOFTMAX && kind[h] != SJ_HEAD_SIGMOID))
+      return e->fail(SJ_ERR_INVALID, "bad head " + std::to_string(h));
+    s.off[h] = off;
+    s.n_out[h] = n_out[h];
+    s.kind[h] = kind[h];
+    off += n_out[h];
+  }
+  if (off > 64) return e->fail(SJ_ERR_INVALID, "at most 64 head outputs in total");
+  s.n_total = off;
+  e->spec = s;
+  e->has_heads = n_heads > 0;
+  return SJ_OK;
+}
+
+int sj_fast_commit(sj_fast* e) { return e ? e->commit() : SJ_ERR_INVALID; }
+
+int sj_fast_encode(sj_fast* e, const int64_t* ids, const int32_t* cu_seqlens,
+                   const int32_t* kv_lens, int B, float* hidden) {
+  if (!e) return SJ_ERR_INVALID;
+  if (!hidden && B > 0) return e->fail(SJ_ERR_INVALID, "null hidden output");
+  return e->host_call(ids, cu_seqlens, kv_lens, B, hidden, nullptr);
+}
+
+int sj_fast_decide(sj_fast* e, const int64_t* ids, const int32_t* cu_seqlens, int B,
+                   float* probs) {
+  if (!e) return SJ_ERR_INVALID;
+  if (!probs && B > 0) return e->fail(SJ_ERR_INVALID, "null probs output");
+  return e->host_call(ids, cu_seqlens, nullptr, B, nullptr, probs);
+}
+
+int sj_fast_encode_device(sj_fast* e, const int64_t* ids, const int32_t* cu_seqlens,
+                          const int32_t* cu_seqlens_host, const int32_t* kv_lens, int B,
+                          float* hidden, float* probs, void* stream) {
+  if (!e) return SJ_ERR_INVALID;
+  if (!cu_seqlens_host || (B > 0 && (!ids || !cu_seqlens)))
+    return e->fail(SJ_ERR_INVALID, "null input");
+  if (probs && !e->has_heads) return e->fail(SJ_ERR_STATE, "no decision heads set");
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : e->stream;
+  return e->run(ids, cu_seqlens, cu_seqlens_host, kv_lens, B, hidden, probs, st);
+}
+
+int sj_fast_sync(sj_fast* e, void* stream) {
+  if (!e) return SJ_ERR_INVALID;
+  cudaError_t rc = cudaSetDevice(e->cfg.device);
+  if (rc != cudaSuccess) return e->cuda_fail(rc, "cudaSetDevice");
+  return e->check_flags(stream ? static_cast<cudaStream_t>(stream) : e->stream);
+}
+
+int sj_fast_launch_count(const sj_fast* e) { return e ? e->launches : 0; }
+
+const char* sj_fast_last_error(const sj_fast* e) { return e ? e->err.c_str() : "null engine"; }
+
+void sj_fast_destroy(sj_fast* e) { delete e; }
+
+}  // extern "C"

@@ -1,0 +1,103 @@
+// kernels.h — internal launchers of the snapjudge B200 kernels (C++ only).
+//
+// Every launcher is asynchronous on `st` and returns the launch status.  The
+// C-ABI (capi.cu) and the encoder engine (engine.cu) are the only callers.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace sjb {
+
+using bf16 = __nv_bfloat16;
+
+enum Act { ACT_NONE = 0, ACT_GELU = 1, ACT_RELU = 2 };
+
+// ---- norms (norm.cu) ------------------------------------------------------
+// X[T, D] (fp32) = LN(emb[ids]) * w ; Y = cast(X) when Y != null.
+// Out-of-vocabulary ids produce a zero row and set *bad = 1.
+template <typename TY>
+cudaError_t embed_ln(const int64_t* ids, int T, const float* emb, int V, int D,
+                     const float* w, float eps, float* X, TY* Y, int* bad, cudaStream_t st);
+
+// Optional residual add (X += R), then Y = LN(X) * w (+ b).  With `rows`
+// (length M), output row i normalises X[rows[i]] and no residual is applied.
+template <typename TR, typename TY>
+cudaError_t add_ln(float* X, const TR* R, const float* w, const float* b, TY* Y, int M, int D,
+                   float eps, const int32_t* rows, cudaStream_t st);
+
+// ---- GEMM on CUDA cores (gemm_simt.cu) --------------------------------------
+// C[M, N] = act(A[M, K] W[N, K]^T + bias)           (resid == null, geglu == false)
+// resid[M, N] += A W^T (+ bias)  (fp32 residual)     (resid != null)
+// C[M, N] = gelu(A Wg^T) * (A Wu^T), W = [Wg; Wu]   (geglu == true, N = F)
+template <typename TA, typename TC>
+cudaError_t gemm_simt(const TA* A, const TA* W, const float* bias, TC* C, float* resid, int M,
+                      int N, int K, int act, bool geglu, cudaStream_t st);
+
+// ---- RoPE (rope.cu) -------------------------------------------------------------
+// In-place rotate-half on the q and k parts of qkv [M, 3*H*Dh]; row r has
+// position pos[r]; cos/sin tables [max_pos, Dh/2].
+template <typename T>
+cudaError_t rope(T* qkv, const float* cos_t, const float* sin_t, const int32_t* pos, int M, int H,
+                 int Dh, cudaStream_t st);
+
+// Same, with the position of row r found from cu_seqlens (no position array).
+cudaError_t rope_cu(bf16* qkv, const float* cos_t, const float* sin_t, const int32_t* cu, int B,
+                    int M, int H, int Dh, cudaStream_t st);
+
+// pos[r] = r - cu[b] for the sequence b owning row r; seq[r] = b (seq may be null).
+cudaError_t positions(const int32_t* cu, int B, int T, int32_t* pos, int32_t* seq, cudaStream_t st);
+
+// ---- attention on CUDA cores (attn_simt.cu) ---------------------------------
+// Packed varlen bidirectional attention over qkv [T, 3*H*Dh]; O [T, H*Dh].
+// Segment b = rows [cu[b], cu[b+1]); its queries attend keys j < kv_len[b]
+// (kv_lens null: the whole segment), |i - j| <= window when window > 0.
+// tiles: list of (b, q0) query tiles of 64 rows, n_tiles entries; or null,
+// then the grid covers B x ceil(max_seqlen / 64) tiles and idle ones exit.
+template <typename T>
+cudaError_t attn_simt(const T* qkv, const int32_t* cu, const int32_t* kv_lens, T* O, int H, int Dh,
+                      int window, const int2* tiles, int n_tiles, int B, int max_seqlen,
+                      cudaStream_t st);
+
+// ---- decision heads on [CLS] (heads.cu) ---------------------------------------
+struct HeadSpec {
+  int n_heads;
+  int off[8];   // first output column of head h in W/bias/probs
+  int n_out[8];
+  int kind[8];  // 0 softmax, 1 sigmoid
+  int n_total;
+};
+// probs[b] = heads(Hc[b]) for already-normalised rows Hc [B, D].
+cudaError_t dec_heads(const float* Hc, int B, int D, const float* W, const float* bias,
+                      HeadSpec spec, float* probs, cudaStream_t st);
+
+// Y[i] = bf16(X[i]) (identity attn_norm in bf16 mode).
+cudaError_t cast_bf16(const float* X, bf16* Y, int64_t n, cudaStream_t st);
+
+// ---- tcgen05 GEMM (gemm_tc.cu) ------------------------------------------------
+// True when the tensor-core GEMM takes this shape (K % 64 == 0, N tiles of 256
+// or, for geglu, F % 128 == 0, 16-byte aligned rows).
+bool gemm_tc_supported(int M, int N, int K, bool geglu);
+
+enum TcEpi { TC_STORE = 0, TC_RESID = 1, TC_GEGLU = 2, TC_ROPE = 3 };
+struct TcRope {
+  const float* cos_t;
+  const float* sin_t;
+  const int32_t* pos;
+  int H;  // q and k heads of 64 columns rotate; v columns pass through
+};
+// bf16 A[M, K], W[N, K] (for TC_GEGLU W = [Wg; Wu], 2N rows, N = F), fp32 accum.
+// TC_STORE: C = acc (+bias, act); TC_RESID: resid += acc; TC_ROPE: C = rope(acc).
+cudaError_t gemm_tc(const bf16* A, const bf16* W, const float* bias, bf16* C, float* resid,
+                    int M, int N, int K, int epi, int act, TcRope rope, int* err,
+                    cudaStream_t st);
+
+// ---- tcgen05 flash attention (attn_tc.cu) -----------------------------------
+bool attn_tc_supported(int Dh);
+// tiles: list of (b, q0) query tiles of 128 rows (or null: B x ceil(max_seqlen/128)).
+cudaError_t attn_tc(const bf16* qkv, const int32_t* cu, const int32_t* kv_lens, bf16* O, int T,
+                    int H, int window, const int2* tiles, int n_tiles, int B, int max_seqlen,
+                    int* err, cudaStream_t st);
+
+}  // namespace sjb

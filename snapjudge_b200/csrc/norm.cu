@@ -1,0 +1,266 @@
+// norm.cu — embedding gather + LayerNorm, and residual add + LayerNorm.
+//
+// Follows the reference layer_norm (src/tensor.cpp:54-79): population
+// variance, eps inside the square root, weight then optional bias; the
+// residual stream X stays fp32 (src/model.cpp:333-397).  Statistics are
+// two-pass fp32 over the row held in registers (the reference accumulates in
+// fp64; the difference is far below every tolerance used here).
+//
+// One warp per row, 16-byte loads: each lane owns D/128 float4 chunks
+// (D <= 1024 in registers).  Rows of other widths use a block-per-row kernel.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace sjb {
+namespace {
+
+constexpr int kMaxChunks = 8;  // float4 chunks per lane -> D <= 1024
+
+template <typename TY>
+__device__ __forceinline__ void store4(TY* p, float4 v);
+template <>
+__device__ __forceinline__ void store4<float>(float* p, float4 v) {
+  *reinterpret_cast<float4*>(p) = v;
+}
+template <>
+__device__ __forceinline__ void store4<bf16>(bf16* p, float4 v) {
+  __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y);
+  __nv_bfloat162 b = __floats2bfloat162_rn(v.z, v.w);
+  uint2 u;
+  u.x = *reinterpret_cast<uint32_t*>(&a);
+  u.y = *reinterpret_cast<uint32_t*>(&b);
+  *reinterpret_cast<uint2*>(p) = u;
+}
+
+template <typename TR>
+__device__ __forceinline__ float4 load4(const TR* p);
+template <>
+__device__ __forceinline__ float4 load4<float>(const float* p) {
+  return *reinterpret_cast<const float4*>(p);
+}
+template <>
+__device__ __forceinline__ float4 load4<bf16>(const bf16* p) {
+  uint2 u = *reinterpret_cast<const uint2*>(p);
+  __nv_bfloat162 a = *reinterpret_cast<__nv_bfloat162*>(&u.x);
+  __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162*>(&u.y);
+  float2 fa = __bfloat1622float2(a), fb = __bfloat1622float2(b);
+  return make_float4(fa.x, fa.y, fb.x, fb.y);
+}
+
+// Normalise the lane-held chunks v[0..nc) of a D-wide row; returns inv std.
+// Chunk c of a lane is float4 index lane + 32 c; chunks past the row end are
+// zero and excluded from the variance.
+__device__ __forceinline__ void row_stats(const float4 (&v)[kMaxChunks], int lane, int nc4, int D,
+                                          float eps, float& mean, float& inv) {
+  float s = 0.f;
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c) s += (v[c].x + v[c].y) + (v[c].z + v[c].w);
+  mean = warp_sum(s) / (float)D;
+  float q = 0.f;
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c) {
+    if (lane + 32 * c >= nc4) break;
+    float a = v[c].x - mean, b = v[c].y - mean, cc = v[c].z - mean, d = v[c].w - mean;
+    q += (a * a + b * b) + (cc * cc + d * d);
+  }
+  float var = warp_sum(q) / (float)D;
+  inv = 1.0f / sqrtf(var + eps);
+}
+
+template <typename TY>
+__global__ void __launch_bounds__(256) embed_ln_warp(const int64_t* __restrict__ ids, int T,
+                                                     const float* __restrict__ emb, int V, int D,
+                                                     const float* __restrict__ w, float eps,
+                                                     float* __restrict__ X, TY* __restrict__ Y,
+                                                     int* __restrict__ bad) {
+  const int lane = threadIdx.x & 31;
+  const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (r >= T) return;
+  const int nc4 = D >> 2;  // float4 chunks in the row
+  int64_t id = ids[r];
+  bool ok = id >= 0 && id < V;
+  if (!ok && lane == 0) *bad = 1;
+  float4 v[kMaxChunks];
+#pragma unroll
+  for (int k = 0; k < kMaxChunks; ++k) {
+    const int c = lane + 32 * k;
+    v[k] = (ok && c < nc4) ? load4<float>(emb + id * (int64_t)D + 4 * c)
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  float mean, inv;
+  row_stats(v, lane, nc4, D, eps, mean, inv);
+#pragma unroll
+  for (int k = 0; k < kMaxChunks; ++k) {
+    const int c = lane + 32 * k;
+    if (c >= nc4) break;
+    float4 g = load4<float>(w + 4 * c);
+    float4 o = make_float4((v[k].x - mean) * inv * g.x, (v[k].y - mean) * inv * g.y,
+                           (v[k].z - mean) * inv * g.z, (v[k].w - mean) * inv * g.w);
+    store4<float>(X + (int64_t)r * D + 4 * c, o);
+    if (Y) store4<TY>(Y + (int64_t)r * D + 4 * c, o);
+  }
+}
+
+template <typename TR, typename TY>
+__global__ void __launch_bounds__(256) add_ln_warp(float* __restrict__ X, const TR* __restrict__ R,
+                                                   const float* __restrict__ w,
+                                                   const float* __restrict__ b,
+                                                   TY* __restrict__ Y, int M, int D, float eps,
+                                                   const int32_t* __restrict__ rows) {
+  const int lane = threadIdx.x & 31;
+  const int i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (i >= M) return;
+  const int src = rows ? rows[i] : i;
+  const int nc4 = D >> 2;
+  float4 v[kMaxChunks];
+#pragma unroll
+  for (int k = 0; k < kMaxChunks; ++k) {
+    const int c = lane + 32 * k;
+    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (c < nc4) {
+      x = load4<float>(X + (int64_t)src * D + 4 * c);
+      if (R && !rows) {
+        float4 rr = load4<TR>(R + (int64_t)src * D + 4 * c);
+        x.x += rr.x; x.y += rr.y; x.z += rr.z; x.w += rr.w;
+        store4<float>(X + (int64_t)src * D + 4 * c, x);
+      }
+    }
+    v[k] = x;
+  }
+  float mean, inv;
+  row_stats(v, lane, nc4, D, eps, mean, inv);
+#pragma unroll
+  for (int k = 0; k < kMaxChunks; ++k) {
+    const int c = lane + 32 * k;
+    if (c >= nc4) break;
+    float4 g = load4<float>(w + 4 * c);
+    float4 o = make_float4((v[k].x - mean) * inv * g.x, (v[k].y - mean) * inv * g.y,
+                           (v[k].z - mean) * inv * g.z, (v[k].w - mean) * inv * g.w);
+    if (b) {
+      float4 bb = load4<float>(b + 4 * c);
+      o.x += bb.x; o.y += bb.y; o.z += bb.z; o.w += bb.w;
+    }
+    store4<TY>(Y + (int64_t)i * D + 4 * c, o);
+  }
+}
+
+// ---- generic widths: one block per row, row staged in shared memory ----
+__device__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (lane == 0) red[wid] = v;
+  __syncthreads();
+  float t = 0.f;
+  for (int k = 0; k < nw; ++k) t += red[k];
+  return t;
+}
+
+template <typename TR, typename TY>
+__global__ void add_ln_block(float* __restrict__ X, const TR* __restrict__ R,
+                             const float* __restrict__ w, const float* __restrict__ b,
+                             TY* __restrict__ Y, int M, int D, float eps,
+                             const int32_t* __restrict__ rows, const int64_t* __restrict__ ids,
+                             const float* __restrict__ emb, int V, int* __restrict__ bad) {
+  extern __shared__ float srow[];
+  __shared__ float red[32];
+  const int i = blockIdx.x;
+  if (i >= M) return;
+  const int src = rows ? rows[i] : i;
+  int64_t id = 0;
+  bool ok = true;
+  if (ids) {
+    id = ids[i];
+    ok = id >= 0 && id < V;
+    if (!ok && threadIdx.x == 0) *bad = 1;
+  }
+  for (int j = threadIdx.x; j < D; j += blockDim.x) {
+    float x;
+    if (ids) {
+      x = ok ? emb[id * (int64_t)D + j] : 0.f;
+    } else {
+      x = X[(int64_t)src * D + j];
+      if (R && !rows) {
+        x += io<TR>::to_f(R[(int64_t)src * D + j]);
+        X[(int64_t)src * D + j] = x;
+      }
+    }
+    srow[j] = x;
+  }
+  __syncthreads();
+  float s = 0.f;
+  for (int j = threadIdx.x; j < D; j += blockDim.x) s += srow[j];
+  float mean = block_sum(s, red) / (float)D;
+  float q = 0.f;
+  for (int j = threadIdx.x; j < D; j += blockDim.x) {
+    float d = srow[j] - mean;
+    q += d * d;
+  }
+  float inv = 1.0f / sqrtf(block_sum(q, red) / (float)D + eps);
+  for (int j = threadIdx.x; j < D; j += blockDim.x) {
+    float o = (srow[j] - mean) * inv * w[j];
+    if (b) o += b[j];
+    if (ids) {
+      X[(int64_t)i * D + j] = o;
+      if (Y) Y[(int64_t)i * D + j] = io<TY>::cvt(o);
+    } else {
+      Y[(int64_t)i * D + j] = io<TY>::cvt(o);
+    }
+  }
+}
+
+__global__ void cast_bf16_kernel(const float* __restrict__ X, bf16* __restrict__ Y, int64_t n) {
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) Y[i] = __float2bfloat16(X[i]);
+}
+
+bool warp_path(int D) { return D % 4 == 0 && D <= 4 * 32 * kMaxChunks; }
+
+}  // namespace
+
+template <typename TY>
+cudaError_t embed_ln(const int64_t* ids, int T, const float* emb, int V, int D, const float* w,
+                     float eps, float* X, TY* Y, int* bad, cudaStream_t st) {
+  if (T <= 0) return cudaSuccess;
+  if (warp_path(D)) {
+    embed_ln_warp<TY><<<(T + 7) / 8, 256, 0, st>>>(ids, T, emb, V, D, w, eps, X, Y, bad);
+  } else {
+    add_ln_block<float, TY><<<T, 128, D * sizeof(float), st>>>(X, nullptr, w, nullptr, Y, T, D,
+                                                               eps, nullptr, ids, emb, V, bad);
+  }
+  return cudaGetLastError();
+}
+
+template <typename TR, typename TY>
+cudaError_t add_ln(float* X, const TR* R, const float* w, const float* b, TY* Y, int M, int D,
+                   float eps, const int32_t* rows, cudaStream_t st) {
+  if (M <= 0) return cudaSuccess;
+  if (warp_path(D)) {
+    add_ln_warp<TR, TY><<<(M + 7) / 8, 256, 0, st>>>(X, R, w, b, Y, M, D, eps, rows);
+  } else {
+    add_ln_block<TR, TY><<<M, 128, D * sizeof(float), st>>>(X, R, w, b, Y, M, D, eps, rows,
+                                                            nullptr, nullptr, 0, nullptr);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t cast_bf16(const float* X, bf16* Y, int64_t n, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  cast_bf16_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(X, Y, n);
+  return cudaGetLastError();
+}
+
+template cudaError_t embed_ln<float>(const int64_t*, int, const float*, int, int, const float*,
+                                     float, float*, float*, int*, cudaStream_t);
+template cudaError_t embed_ln<bf16>(const int64_t*, int, const float*, int, int, const float*,
+                                    float, float*, bf16*, int*, cudaStream_t);
+template cudaError_t add_ln<float, float>(float*, const float*, const float*, const float*,
+                                          float*, int, int, float, const int32_t*, cudaStream_t);
+template cudaError_t add_ln<bf16, bf16>(float*, const bf16*, const float*, const float*, bf16*,
+                                        int, int, float, const int32_t*, cudaStream_t);
+template cudaError_t add_ln<float, bf16>(float*, const float*, const float*, const float*, bf16*,
+                                         int, int, float, const int32_t*, cudaStream_t);
+template cudaError_t add_ln<bf16, float>(float*, const bf16*, const float*, const float*, float*,
+                                         int, int, float, const int32_t*, cudaStream_t);
+
+}  // namespace sjb

@@ -1,0 +1,144 @@
+"""FastSnapjudge — host-side mirror of the reference's CUDA fast path.
+
+Mirrors ``snapjudge::FastSnapjudge`` (include/snapjudge/fast.hpp:15-31) and the
+encoder entry point it accelerates, ``DecisionModel::encode``
+(src/model.cpp:222-307), over the C ABI of ``libsnapjudge_b200.so``:
+
+* ``encode(input_ids, attention_mask)`` — the reference signature: a
+  right-padded ``[B, L]`` batch in, ``[B, L, D]`` final-norm hidden states out,
+  padded rows included (they attend the valid keys, as in the reference).
+* ``encode_packed(ids, lengths)`` — packed variable-length form: only valid
+  rows are computed.
+* ``decide(ids, lengths)`` — encoder + decision heads on the [CLS] rows.
+* ``encode_device(...)`` — the same on caller-owned device buffers (torch
+  tensors), asynchronous on a CUDA stream.
+
+Errors raise :class:`SnapjudgeError` carrying the library's message, the way
+the reference throws ``std::runtime_error("snapjudge CUDA: ...")``.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from . import _lib
+from ._lib import SnapjudgeError, check  # noqa: F401  (re-exported)
+from .checkpoint import EncoderConfig, load_checkpoint
+
+_I64P = C.POINTER(C.c_int64)
+
+
+def _ptr(a: np.ndarray):
+    return C.c_void_p(a.ctypes.data) if a is not None else None
+
+
+class FastSnapjudge:
+    """One encoder engine resident on one GPU."""
+
+    def __init__(self, cfg: EncoderConfig, tensors: dict[str, np.ndarray], *,
+                 precision: str = "bf16", heads=None, device: int = 0, max_tokens: int = 0):
+        L = _lib.lib()
+        self.cfg = cfg
+        self.precision = precision
+        self.D = cfg.hidden_size
+        sl = (C.c_int * max(1, cfg.num_hidden_layers))(
+            *[int(cfg.layer_sliding(i)) for i in range(cfg.num_hidden_layers)])
+        c = _lib.FastConfig(cfg.hidden_size, cfg.num_hidden_layers, cfg.num_attention_heads,
+                            cfg.intermediate_size, cfg.vocab_size, cfg.max_position_embeddings,
+                            cfg.norm_eps, cfg.local_attention, sl, cfg.rope_theta_full,
+                            cfg.rope_theta_sliding,
+                            _lib.SJ_PREC_BF16 if precision == "bf16" else _lib.SJ_PREC_FP32,
+                            device, max_tokens)
+        if precision not in ("bf16", "fp32"):
+            raise ValueError(f"precision must be 'bf16' or 'fp32', got {precision!r}")
+        h = C.c_void_p()
+        rc = L.sj_fast_create(C.byref(c), C.byref(h))
+        if rc != 0:
+            raise SnapjudgeError(rc, "sj_fast_create failed (invalid config or CUDA error)")
+        self._h = h
+        self.heads = list(heads or [])
+        self.n_out = sum(hd.n_out for hd in self.heads)
+        try:
+            for name, t in tensors.items():
+                a = np.ascontiguousarray(t, dtype=np.float32)
+                shape = (C.c_int64 * max(1, a.ndim))(*a.shape)
+                check(L.sj_fast_set_tensor(h, name.encode(), _ptr(a), shape, a.ndim), h)
+            if self.heads:
+                n = (C.c_int * len(self.heads))(*[hd.n_out for hd in self.heads])
+                k = (C.c_int * len(self.heads))(*[hd.kind for hd in self.heads])
+                check(L.sj_fast_set_heads(h, len(self.heads), n, k), h)
+            check(L.sj_fast_commit(h), h)
+        except Exception:
+            self.close()
+            raise
+
+    @classmethod
+    def from_checkpoint(cls, path: str, **kw) -> "FastSnapjudge":
+        cfg, tensors = load_checkpoint(path)
+        return cls(cfg, tensors, **kw)
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            _lib.lib().sj_fast_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    # -- host buffers ------------------------------------------------------
+    def encode_packed(self, ids, lengths, kv_lens=None) -> np.ndarray:
+        ids = np.ascontiguousarray(ids, dtype=np.int64)
+        lengths = np.asarray(lengths, dtype=np.int64)
+        cu = np.zeros(len(lengths) + 1, np.int32)
+        np.cumsum(lengths, out=cu[1:])
+        out = np.empty((int(cu[-1]), self.D), np.float32)
+        kvl = None if kv_lens is None else np.ascontiguousarray(kv_lens, np.int32)
+        check(_lib.lib().sj_fast_encode(self._h, _ptr(ids), _ptr(cu), _ptr(kvl), len(lengths),
+                                        _ptr(out)), self._h)
+        return out
+
+    def encode(self, input_ids, attention_mask) -> np.ndarray:
+        """DecisionModel::encode: padded [B, L] ids + mask -> [B, L, D]."""
+        ids = np.ascontiguousarray(input_ids, dtype=np.int64)
+        mask = np.asarray(attention_mask, dtype=np.int64)
+        B, L = ids.shape
+        lens = mask.sum(axis=1).astype(np.int32)
+        out = self.encode_packed(ids.reshape(-1), np.full(B, L, np.int64), kv_lens=lens)
+        return out.reshape(B, L, self.D)
+
+    def decide(self, ids, lengths) -> np.ndarray:
+        ids = np.ascontiguousarray(ids, dtype=np.int64)
+        lengths = np.asarray(lengths, dtype=np.int64)
+        cu = np.zeros(len(lengths) + 1, np.int32)
+        np.cumsum(lengths, out=cu[1:])
+        out = np.empty((len(lengths), max(1, self.n_out)), np.float32)
+        check(_lib.lib().sj_fast_decide(self._h, _ptr(ids), _ptr(cu), len(lengths), _ptr(out)),
+              self._h)
+        return out
+
+    def split_heads(self, probs: np.ndarray) -> list[np.ndarray]:
+        out, off = [], 0
+        for hd in self.heads:
+            out.append(probs[:, off:off + hd.n_out])
+            off += hd.n_out
+        return out
+
+    # -- device buffers (torch tensors) --------------------------------------
+    def encode_device(self, ids, cu, cu_host: np.ndarray, *, kv_lens=None, hidden=None,
+                      probs=None, stream=None) -> None:
+        """Asynchronous forward on device tensors (int64 ids, int32 cu/kv_lens)."""
+        cu_host = np.ascontiguousarray(cu_host, np.int32)
+        self._cu_host = cu_host  # must outlive the launch (the schedule reads it now)
+        dp = lambda t: None if t is None else C.c_void_p(t.data_ptr())  # noqa: E731
+        st = None if stream is None else C.c_void_p(stream.cuda_stream)
+        check(_lib.lib().sj_fast_encode_device(self._h, dp(ids), dp(cu), _ptr(cu_host),
+                                               dp(kv_lens), len(cu_host) - 1, dp(hidden),
+                                               dp(probs), st), self._h)
+
+    def sync(self, stream=None) -> None:
+        st = None if stream is None else C.c_void_p(stream.cuda_stream)
+        check(_lib.lib().sj_fast_sync(self._h, st), self._h)
+
+    def launch_count(self) -> int:
+        return _lib.lib().sj_fast_launch_count(self._h)

@@ -127,8 +127,9 @@ def make_weights(spec: SynthSpec, std: float = 0.02) -> dict[str, np.ndarray]:
     t["act_head.2.weight"] = n(c.n_act, 256)
     t["act_head.2.bias"] = n(c.n_act)
     for i, h in enumerate(spec.heads):
-        # task heads use a larger scale so the probabilities are not all uniform
-        t[f"task_heads.{i}.weight"] = rng.standard_normal((h.n_out, D), dtype=np.float32)
+        # task heads: std 1/sqrt(D) so the [CLS] logits are O(1), as in a trained head
+        t[f"task_heads.{i}.weight"] = (rng.standard_normal((h.n_out, D), dtype=np.float32)
+                                       * np.float32(1.0 / np.sqrt(D)))
         t[f"task_heads.{i}.bias"] = rng.standard_normal((h.n_out,), dtype=np.float32) * s
     return t
 
