@@ -453,7 +453,7 @@ int sj_fast::host_call(const int64_t* ids_h, const int32_t* cu_h, const int32_t*
   for (int64_t r = 0; r < cu_h[B]; ++r)
     if (ids_h[r] < 0 || ids_h[r] >= V)
       return fail(SJ_ERR_INVALID, "input id " + std::to_string(ids_h[r]) + " at row " +
-                                      std::to_string(r) + " outside [0, vocab_size)");
+                                      std::to_string(r) + " outside the vocabulary [0, vocab_size)");
   cudaError_t rc = cudaSetDevice(cfg.device);
   if (rc != cudaSuccess) return cuda_fail(rc, "cudaSetDevice");
   const int nout = std::max(1, spec.n_total);

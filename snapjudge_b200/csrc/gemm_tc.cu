@@ -1,10 +1,369 @@
-// gemm_tc.cu — tcgen05 GEMM (placeholder until the tensor-core kernel lands).
+// gemm_tc.cu — persistent warp-specialised tcgen05 GEMM for the encoder projections.
+//
+// C = A W^T with A [M, K] bf16 activations and W [N, K] bf16 weights in the
+// checkpoint layout (both K-major), fp32 accumulation in TMEM — the
+// contraction of the reference gemm_nt / gemm_geglu (src/tensor.cpp:108-151).
+//
+// CTA (192 threads, one per SM, persistent over output tiles of 128 x BN):
+//   warp 0      TMA producer: A 128x64 and W BNx64 boxes, 128-byte swizzle,
+//               STAGES-deep ring of shared-memory stages (full/empty mbarriers)
+//   warp 1      TMEM owner + MMA issuer: 4 x tcgen05.mma (K = 16) per stage
+//               into one of two TMEM accumulators (2 x BN fp32 columns)
+//   warps 2-5   epilogue: tcgen05.ld of the accumulator (warp w reads TMEM
+//               lanes 32*(w%4)..+31 = tile rows), then one of
+//                 STORE  C = bf16(acc + bias, act)           (act: GELU-erf / ReLU)
+//                 RESID  X += acc                            (fp32 residual stream)
+//                 GEGLU  G = bf16(gelu(acc_g) * acc_u)        (W tile = 128 gate rows
+//                                                             + 128 up rows of [Wg; Wu])
+//                 ROPE   QKV = bf16(rotate-half(acc)) on q/k heads of 64, v as is
+// The epilogue of tile i overlaps the MMAs of tile i+1 (double-buffered TMEM).
+// Every mbarrier wait is bounded; a wait that runs out records an error code
+// and the CTA winds down (no trap).
+#include <algorithm>
+
+#include "common.cuh"
 #include "kernels.h"
+#include "tc_common.cuh"
+#include "tc_host.h"
 
 namespace sjb {
-bool gemm_tc_supported(int, int, int, bool) { return false; }
-cudaError_t gemm_tc(const bf16*, const bf16*, const float*, bf16*, float*, int, int, int, int,
-                    int, TcRope, int*, cudaStream_t) {
-  return cudaErrorNotSupported;
+
+__device__ int g_gemm_tc_err;  // error sink when the caller passes no flag
+
+namespace {
+using namespace tc;
+
+constexpr int BM = 128, BK = 64;
+constexpr int kThreads = 192;
+
+struct EpiArgs {
+  const float* bias;
+  int act;
+  bf16* C;
+  int ldc;               // output row pitch in elements
+  float* resid;          // fp32 [M, ldr]
+  int ldr;
+  const float* cos_t;    // [max_pos, 32]
+  const float* sin_t;
+  const int32_t* pos;    // [M]
+  int rope_cols;         // columns [0, rope_cols) are rotated q/k heads
+  int* err;
+};
+
+template <int BN>
+__host__ __device__ constexpr int stages_for() { return BN >= 256 ? 4 : 6; }
+
+__device__ __forceinline__ void record_err(int* err, int code) {
+  atomicCAS(err ? err : &g_gemm_tc_err, 0, code);
 }
+
+__device__ __forceinline__ float act_fn(float v, int act) {
+  if (act == ACT_GELU) return gelu_erf(v);
+  if (act == ACT_RELU) return fmaxf(v, 0.f);
+  return v;
+}
+
+__device__ __forceinline__ void store_bf16x32(bf16* dst, const float* v) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint32_t w[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      __nv_bfloat162 h = __floats2bfloat162_rn(v[q * 8 + 2 * e], v[q * 8 + 2 * e + 1]);
+      w[e] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    d[q] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
+                   int M, int n_tiles, int K, int up_row0, EpiArgs ep) {
+  constexpr int STAGES = stages_for<BN>();
+  constexpr int A_BYTES = BM * BK * 2;
+  constexpr int B_BYTES = BN * BK * 2;
+  constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  constexpr uint32_t TMEM_COLS = 2 * BN;
+  constexpr uint32_t IDESC = idesc_bf16(BM, BN, false, false);
+
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint64_t full_bar[STAGES], empty_bar[STAGES], tfull_bar[2], tempty_bar[2], drain_bar;
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ volatile int abort_sh;
+
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m_tiles = (M + BM - 1) / BM;
+  const int num_tiles = m_tiles * n_tiles;
+  const int k_blocks = K / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull_bar[b], 1);
+      mbar_init(&tempty_bar[b], 4);
+    }
+    mbar_init(&drain_bar, 1);
+    abort_sh = 0;
+    fence_barrier_init();
+    tma_prefetch(&mapA);
+    tma_prefetch(&mapB);
+  }
+  if (warp == 1) tmem_alloc(&tmem_base_sh, TMEM_COLS);
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tmem_base = tmem_base_sh;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer ----------------
+    int stage = 0;
+    uint32_t phase = 0;
+    int issued = 0;
+    for (int t = blockIdx.x; t < num_tiles && !abort_sh; t += gridDim.x) {
+      const int m0 = (t / n_tiles) * BM, nb = t % n_tiles;
+      for (int kb = 0; kb < k_blocks; ++kb) {
+        if (!mbar_wait(&empty_bar[stage], phase ^ 1)) {
+          record_err(ep.err, 1);
+          abort_sh = 1;
+          break;
+        }
+        uint8_t* sa = smem + stage * STAGE_BYTES;
+        uint8_t* sb = sa + A_BYTES;
+        mbar_expect_tx(&full_bar[stage], STAGE_BYTES);
+        tma_load_2d(sa, &mapA, &full_bar[stage], kb * BK, m0);
+        if (EPI == TC_GEGLU) {
+          tma_load_2d(sb, &mapB, &full_bar[stage], kb * BK, nb * (BN / 2));
+          tma_load_2d(sb + B_BYTES / 2, &mapB, &full_bar[stage], kb * BK, up_row0 + nb * (BN / 2));
+        } else {
+          tma_load_2d(sb, &mapB, &full_bar[stage], kb * BK, nb * BN);
+        }
+        ++issued;
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+    }
+    // drain: every issued copy has landed before the CTA can exit
+    for (int i = 0; i < STAGES && i < issued; ++i) {
+      if (--stage < 0) { stage = STAGES - 1; phase ^= 1; }
+      if (!mbar_wait(&full_bar[stage], phase)) record_err(ep.err, 2);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer ----------------
+    int stage = 0;
+    uint32_t phase = 0;
+    int local = 0;
+    for (int t = blockIdx.x; t < num_tiles && !abort_sh; t += gridDim.x, ++local) {
+      const int b = local & 1;
+      const uint32_t aphase = (local >> 1) & 1;
+      if (!mbar_wait(&tempty_bar[b], aphase ^ 1)) {
+        record_err(ep.err, 3);
+        abort_sh = 1;
+        break;
+      }
+      fence_after_sync();
+      const uint32_t d = tmem_base + b * BN;
+      for (int kb = 0; kb < k_blocks; ++kb) {
+        if (!mbar_wait(&full_bar[stage], phase)) {
+          record_err(ep.err, 4);
+          abort_sh = 1;
+          break;
+        }
+        fence_after_sync();
+        const uint32_t a_addr = smem_u32(smem + stage * STAGE_BYTES);
+        const uint32_t b_addr = a_addr + A_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk)
+          mma_bf16(d, desc_kmajor_sw128(a_addr + kk * 32), desc_kmajor_sw128(b_addr + kk * 32),
+                   IDESC, (kb | kk) != 0);
+        mma_commit(&empty_bar[stage]);
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+      mma_commit(&tfull_bar[b]);
+    }
+    mma_commit(&drain_bar);
+    if (!mbar_wait(&drain_bar, 0)) record_err(ep.err, 5);
+  } else if (warp >= 2) {
+    // ---------------- epilogue ----------------
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int local = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+      const int b = local & 1;
+      const uint32_t aphase = (local >> 1) & 1;
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait(&tfull_bar[b], aphase) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok || abort_sh) {
+        if (lane == 0 && !ok) { record_err(ep.err, 6); abort_sh = 1; }
+        break;
+      }
+      fence_after_sync();
+      const int m0 = (t / n_tiles) * BM, nb = t % n_tiles;
+      const int row = m0 + q * 32 + lane;
+      const bool live = row < M;
+      const uint32_t tacc = tmem_base + ((uint32_t)(q * 32) << 16) + b * BN;
+      uint32_t r0[32], r1[32];
+      if (EPI == TC_GEGLU) {
+        constexpr int HALF = BN / 2;
+        const int col_base = nb * HALF;
+#pragma unroll 1
+        for (int c = 0; c < HALF; c += 32) {
+          tmem_ld32(tacc + c, r0);
+          tmem_ld32(tacc + HALF + c, r1);
+          tmem_ld_wait();
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            v[j] = gelu_erf(__uint_as_float(r0[j])) * __uint_as_float(r1[j]);
+          if (live) store_bf16x32(ep.C + (int64_t)row * ep.ldc + col_base + c, v);
+        }
+      } else if (EPI == TC_ROPE) {
+        const int col_base = nb * BN;
+        const int p = live ? ep.pos[row] : 0;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 64) {
+          tmem_ld32(tacc + c, r0);
+          tmem_ld32(tacc + c + 32, r1);
+          tmem_ld_wait();
+          float v[64];
+          if (col_base + c < ep.rope_cols) {
+            const float* cs = ep.cos_t + (int64_t)p * 32;
+            const float* sn = ep.sin_t + (int64_t)p * 32;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float x0 = __uint_as_float(r0[j]), x1 = __uint_as_float(r1[j]);
+              const float cj = live ? cs[j] : 0.f, sj = live ? sn[j] : 0.f;
+              v[j] = x0 * cj - x1 * sj;
+              v[32 + j] = x1 * cj + x0 * sj;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              v[j] = __uint_as_float(r0[j]);
+              v[32 + j] = __uint_as_float(r1[j]);
+            }
+          }
+          if (live) {
+            store_bf16x32(ep.C + (int64_t)row * ep.ldc + col_base + c, v);
+            store_bf16x32(ep.C + (int64_t)row * ep.ldc + col_base + c + 32, v + 32);
+          }
+        }
+      } else {
+        const int col_base = nb * BN;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          tmem_ld32(tacc + c, r0);
+          tmem_ld_wait();
+          if (!live) continue;
+          if (EPI == TC_RESID) {
+            float4* x = reinterpret_cast<float4*>(ep.resid + (int64_t)row * ep.ldr + col_base + c);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              float4 o = x[j];
+              o.x += __uint_as_float(r0[4 * j]);
+              o.y += __uint_as_float(r0[4 * j + 1]);
+              o.z += __uint_as_float(r0[4 * j + 2]);
+              o.w += __uint_as_float(r0[4 * j + 3]);
+              x[j] = o;
+            }
+          } else {
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              float a = __uint_as_float(r0[j]);
+              if (ep.bias) a += ep.bias[col_base + c + j];
+              v[j] = act_fn(a, ep.act);
+            }
+            store_bf16x32(ep.C + (int64_t)row * ep.ldc + col_base + c, v);
+          }
+        }
+      }
+      fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty_bar[b]);
+    }
+  }
+
+  fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    fence_after_sync();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+template <int BN, int EPI>
+cudaError_t launch(const bf16* A, const bf16* W, int M, int N_out, int K, int w_rows, EpiArgs ep,
+                   cudaStream_t st) {
+  constexpr int STAGES = stages_for<BN>();
+  constexpr int SMEM = STAGES * (BM * BK * 2 + BN * BK * 2) + 1024;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t rc = cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    if (rc != cudaSuccess) return rc;
+    attr_set = true;
+  }
+  CUtensorMap ma, mb;
+  const int b_box = EPI == TC_GEGLU ? BN / 2 : BN;
+  if (!make_map_bf16(&ma, A, K, M, (uint64_t)K * 2, BK, BM) ||
+      !make_map_bf16(&mb, W, K, w_rows, (uint64_t)K * 2, BK, b_box))
+    return cudaErrorInvalidValue;
+  const int out_tile = EPI == TC_GEGLU ? BN / 2 : BN;
+  const int n_tiles = N_out / out_tile;
+  const int tiles = ((M + BM - 1) / BM) * n_tiles;
+  const int grid = std::min(tiles, sm_count());
+  const int up_row0 = EPI == TC_GEGLU ? N_out : 0;
+  gemm_tc_kernel<BN, EPI><<<grid, kThreads, SMEM, st>>>(ma, mb, M, n_tiles, K, up_row0, ep);
+  return cudaGetLastError();
+}
+
+template <int EPI>
+cudaError_t dispatch_bn(const bf16* A, const bf16* W, int M, int N, int K, int w_rows, EpiArgs ep,
+                        cudaStream_t st) {
+  if (EPI == TC_GEGLU) {
+    if (N % 128 == 0) return launch<256, EPI>(A, W, M, N, K, w_rows, ep, st);
+    return launch<128, EPI>(A, W, M, N, K, w_rows, ep, st);
+  }
+  if (N % 256 == 0) return launch<256, EPI>(A, W, M, N, K, w_rows, ep, st);
+  if (N % 128 == 0) return launch<128, EPI>(A, W, M, N, K, w_rows, ep, st);
+  return launch<64, EPI>(A, W, M, N, K, w_rows, ep, st);
+}
+
+}  // namespace
+
+bool gemm_tc_supported(int M, int N, int K, bool geglu) {
+  if (M <= 0 || K < BK || K % BK != 0) return false;
+  return geglu ? (N % 64 == 0) : (N % 64 == 0);
+}
+
+cudaError_t gemm_tc(const bf16* A, const bf16* W, const float* bias, bf16* C, float* resid, int M,
+                    int N, int K, int epi, int act, TcRope rope, int* err, cudaStream_t st) {
+  if (!gemm_tc_supported(M, N, K, epi == TC_GEGLU)) return cudaErrorInvalidValue;
+  EpiArgs ep{};
+  ep.bias = bias;
+  ep.act = act;
+  ep.C = C;
+  ep.ldc = N;
+  ep.resid = resid;
+  ep.ldr = N;
+  ep.cos_t = rope.cos_t;
+  ep.sin_t = rope.sin_t;
+  ep.pos = rope.pos;
+  ep.rope_cols = 2 * rope.H * 64;
+  ep.err = err;
+  switch (epi) {
+    case TC_STORE: return dispatch_bn<TC_STORE>(A, W, M, N, K, N, ep, st);
+    case TC_RESID: return dispatch_bn<TC_RESID>(A, W, M, N, K, N, ep, st);
+    case TC_GEGLU: return dispatch_bn<TC_GEGLU>(A, W, M, N, K, 2 * N, ep, st);
+    case TC_ROPE: return dispatch_bn<TC_ROPE>(A, W, M, N, K, N, ep, st);
+  }
+  return cudaErrorInvalidValue;
+}
+
 }  // namespace sjb
