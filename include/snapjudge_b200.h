@@ -158,6 +158,24 @@ int sj_fast_sync(sj_fast* e, void* stream);
 /* Number of device kernel launches issued by the last forward (for audits). */
 int sj_fast_launch_count(const sj_fast* e);
 
+/* Per-kernel timing with CUDA events recorded around every launch (off by
+ * default; the reference has no tracing, bench/bench.cpp times whole calls).
+ * Kernel classes, in this order: */
+#define SJ_K_EMBED 0      /* embedding gather + LayerNorm */
+#define SJ_K_LN 1         /* attn_norm / mlp_norm LayerNorm */
+#define SJ_K_QKV 2        /* QKV projection (+ RoPE) */
+#define SJ_K_ATTN 3       /* attention */
+#define SJ_K_WO 4         /* attention output projection + residual */
+#define SJ_K_GEGLU 5      /* Wi projection + GEGLU gate */
+#define SJ_K_WO2 6        /* FFN output projection + residual */
+#define SJ_K_FINAL 7      /* final norm, LoRA, decision heads, positions */
+#define SJ_K_COUNT 8
+int sj_fast_set_profiling(sj_fast* e, int enable);
+/* Accumulated since the last reset (synchronises the engine's work first):
+ * ms[k] total milliseconds and launches[k] count of class k (arrays of
+ * SJ_K_COUNT); reset != 0 clears the accumulators afterwards. */
+int sj_fast_profile(sj_fast* e, double* ms, int64_t* launches, int reset);
+
 const char* sj_fast_last_error(const sj_fast* e);
 void sj_fast_destroy(sj_fast* e);
 

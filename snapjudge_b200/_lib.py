@@ -25,7 +25,11 @@ SJ_PREC_FP32 = 1
 EXPORTS = ["sj_b200_version", "sj_last_error", "sj_gemm", "sj_gemm_geglu", "sj_add_ln", "sj_rope",
            "sj_attn", "sj_fast_create", "sj_fast_set_tensor", "sj_fast_set_heads",
            "sj_fast_commit", "sj_fast_encode", "sj_fast_decide", "sj_fast_encode_device",
-           "sj_fast_sync", "sj_fast_launch_count", "sj_fast_last_error", "sj_fast_destroy"]
+           "sj_fast_sync", "sj_fast_launch_count", "sj_fast_set_profiling", "sj_fast_profile",
+           "sj_fast_last_error", "sj_fast_destroy"]
+
+# kernel classes of sj_fast_profile (SJ_K_* in the header)
+KERNEL_CLASSES = ["embed", "ln", "qkv", "attn", "wo", "geglu", "wo2", "final"]
 
 
 class SnapjudgeError(RuntimeError):
@@ -73,6 +77,8 @@ def lib() -> C.CDLL:
         L.sj_fast_encode_device.argtypes = [_P, _P, _P, _P, _P, _I, _P, _P, _P]
         L.sj_fast_sync.argtypes = [_P, _P]
         L.sj_fast_launch_count.argtypes = [_P]
+        L.sj_fast_set_profiling.argtypes = [_P, _I]
+        L.sj_fast_profile.argtypes = [_P, C.POINTER(C.c_double), C.POINTER(C.c_int64), _I]
         L.sj_fast_destroy.argtypes = [_P]
         _LIB = L
     return _LIB

@@ -107,6 +107,51 @@ struct sj_fast {
   int32_t* h_cu = nullptr;
   int32_t* h_kvl = nullptr;
   cudaEvent_t staged_ev = nullptr;
+  // per-kernel CUDA-event timing (sj_fast_set_profiling)
+  bool profiling = false;
+  struct Mark { int cls; cudaEvent_t a, b; };
+  std::vector<Mark> marks;
+  std::vector<cudaEvent_t> ev_pool;
+  double prof_ms[SJ_K_COUNT] = {};
+  int64_t prof_n[SJ_K_COUNT] = {};
+
+  cudaEvent_t take_event() {
+    if (!ev_pool.empty()) {
+      cudaEvent_t e = ev_pool.back();
+      ev_pool.pop_back();
+      return e;
+    }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+  }
+  // Record a start event before a launch of class `cls` (returns null when off).
+  cudaEvent_t mark_begin(cudaStream_t st) {
+    if (!profiling) return nullptr;
+    cudaEvent_t a = take_event();
+    cudaEventRecord(a, st);
+    return a;
+  }
+  void mark_end(int cls, cudaEvent_t a, cudaStream_t st) {
+    if (!a) return;
+    cudaEvent_t b = take_event();
+    cudaEventRecord(b, st);
+    marks.push_back({cls, a, b});
+  }
+  int collect_profile() {
+    for (const Mark& m : marks) {
+      float ms = 0.f;
+      cudaError_t rc = cudaEventSynchronize(m.b);
+      if (rc == cudaSuccess) rc = cudaEventElapsedTime(&ms, m.a, m.b);
+      if (rc != cudaSuccess) return cuda_fail(rc, "profile events");
+      prof_ms[m.cls] += ms;
+      prof_n[m.cls] += 1;
+      ev_pool.push_back(m.a);
+      ev_pool.push_back(m.b);
+    }
+    marks.clear();
+    return SJ_OK;
+  }
 
   int fail(int code, const std::string& m) {
     err = m;
@@ -132,6 +177,11 @@ struct sj_fast {
     if (h_cu) cudaFreeHost(h_cu);
     if (h_kvl) cudaFreeHost(h_kvl);
     if (staged_ev) cudaEventDestroy(staged_ev);
+    for (const Mark& m : marks) {
+      cudaEventDestroy(m.a);
+      cudaEventDestroy(m.b);
+    }
+    for (cudaEvent_t e : ev_pool) cudaEventDestroy(e);
     if (stream) cudaStreamDestroy(stream);
   }
 
@@ -282,9 +332,11 @@ int sj_fast::commit() {
 }
 
 // ------------------------------------------------------------------ forward
-#define SJ_LAUNCH(expr)                                    \
+#define SJ_LAUNCH(cls, expr)                               \
   do {                                                     \
+    cudaEvent_t ev_ = mark_begin(st);                      \
     cudaError_t rc_ = (expr);                              \
+    mark_end(cls, ev_, st);                                \
     ++launches;                                            \
     if (rc_ != cudaSuccess) return cuda_fail(rc_, #expr);  \
   } while (0)
@@ -323,25 +375,25 @@ int sj_fast::forward(const int64_t* d_ids, const int32_t* d_cu, const int32_t* h
   T* Ot = static_cast<T*>(O);
   T* Gt = static_cast<T*>(G);
   const float eps = cfg.norm_eps;
-  SJ_LAUNCH(sjb::positions(d_cu, B, ntok, pos, nullptr, st));
+  SJ_LAUNCH(SJ_K_FINAL, sjb::positions(d_cu, B, ntok, pos, nullptr, st));
   const bool y0 = !layers.empty() && !layers[0].attn_norm;
-  SJ_LAUNCH(sjb::embed_ln<T>(d_ids, ntok, emb, V, D, emb_norm, eps, X, y0 ? Yt : nullptr, dflags, st));
+  SJ_LAUNCH(SJ_K_EMBED, sjb::embed_ln<T>(d_ids, ntok, emb, V, D, emb_norm, eps, X, y0 ? Yt : nullptr, dflags, st));
 
-  auto gemm = [&](const T* A, const void* W, T* C, float* resid, int N, int K, int epi,
+  auto gemm = [&](int cls, const T* A, const void* W, T* C, float* resid, int N, int K, int epi,
                   const float* ct, const float* stb) -> int {
     if constexpr (kBf16) {
       const bool geglu = epi == sjb::TC_GEGLU;
       if (sjb::gemm_tc_supported(ntok, N, K, geglu) &&
           (epi != sjb::TC_ROPE || Dh == 64)) {
         sjb::TcRope rp{ct, stb, pos, H};
-        SJ_LAUNCH(sjb::gemm_tc(A, static_cast<const bf16*>(W), nullptr, C, resid, ntok, N, K, epi,
+        SJ_LAUNCH(cls, sjb::gemm_tc(A, static_cast<const bf16*>(W), nullptr, C, resid, ntok, N, K, epi,
                                0, rp, dflags + 1, st));
         return SJ_OK;
       }
     }
-    SJ_LAUNCH((sjb::gemm_simt<T, T>(A, static_cast<const T*>(W), nullptr, C, resid, ntok, N, K, 0,
+    SJ_LAUNCH(cls, (sjb::gemm_simt<T, T>(A, static_cast<const T*>(W), nullptr, C, resid, ntok, N, K, 0,
                                     epi == sjb::TC_GEGLU, st)));
-    if (epi == sjb::TC_ROPE) SJ_LAUNCH(sjb::rope<T>(C, ct, stb, pos, ntok, H, Dh, st));
+    if (epi == sjb::TC_ROPE) SJ_LAUNCH(cls, sjb::rope<T>(C, ct, stb, pos, ntok, H, Dh, st));
     return SJ_OK;
   };
 
@@ -350,46 +402,46 @@ int sj_fast::forward(const int64_t* d_ids, const int32_t* d_cu, const int32_t* h
     const LayerDev& ly = layers[li];
     const T* Yin = Yt;
     if (ly.attn_norm) {
-      SJ_LAUNCH((sjb::add_ln<T, T>(X, nullptr, ly.attn_norm, nullptr, Yt, ntok, D, eps, nullptr, st)));
+      SJ_LAUNCH(SJ_K_LN, (sjb::add_ln<T, T>(X, nullptr, ly.attn_norm, nullptr, Yt, ntok, D, eps, nullptr, st)));
     } else if (li > 0) {
-      if constexpr (kBf16) SJ_LAUNCH(sjb::cast_bf16(X, Yt, (int64_t)ntok * D, st));
+      if constexpr (kBf16) SJ_LAUNCH(SJ_K_LN, sjb::cast_bf16(X, Yt, (int64_t)ntok * D, st));
       else Yin = reinterpret_cast<const T*>(X);
     }
     const float* ct = ly.sliding ? cos_s : cos_f;
     const float* stb = ly.sliding ? sin_s : sin_f;
-    if ((s = gemm(Yin, ly.wqkv, Qt, nullptr, 3 * D, D, sjb::TC_ROPE, ct, stb))) return s;
+    if ((s = gemm(SJ_K_QKV, Yin, ly.wqkv, Qt, nullptr, 3 * D, D, sjb::TC_ROPE, ct, stb))) return s;
     if (tc_attn) {
       if constexpr (kBf16)
-        SJ_LAUNCH(sjb::attn_tc(Qt, d_cu, d_kvl, Ot, ntok, H, ly.window, tiles, nt, B, 0, dflags + 2,
+        SJ_LAUNCH(SJ_K_ATTN, sjb::attn_tc(Qt, d_cu, d_kvl, Ot, ntok, H, ly.window, tiles, nt, B, 0, dflags + 2,
                                st));
     } else {
-      SJ_LAUNCH(sjb::attn_simt<T>(Qt, d_cu, d_kvl, Ot, H, Dh, ly.window, tiles, nt, B, 0, st));
+      SJ_LAUNCH(SJ_K_ATTN, sjb::attn_simt<T>(Qt, d_cu, d_kvl, Ot, H, Dh, ly.window, tiles, nt, B, 0, st));
     }
-    if ((s = gemm(Ot, ly.wo, nullptr, X, D, D, sjb::TC_RESID, nullptr, nullptr))) return s;
-    SJ_LAUNCH((sjb::add_ln<T, T>(X, nullptr, ly.mlp_norm, nullptr, Yt, ntok, D, eps, nullptr, st)));
-    if ((s = gemm(Yt, ly.wi, Gt, nullptr, F, D, sjb::TC_GEGLU, nullptr, nullptr))) return s;
-    if ((s = gemm(Gt, ly.wo2, nullptr, X, D, F, sjb::TC_RESID, nullptr, nullptr))) return s;
+    if ((s = gemm(SJ_K_WO, Ot, ly.wo, nullptr, X, D, D, sjb::TC_RESID, nullptr, nullptr))) return s;
+    SJ_LAUNCH(SJ_K_LN, (sjb::add_ln<T, T>(X, nullptr, ly.mlp_norm, nullptr, Yt, ntok, D, eps, nullptr, st)));
+    if ((s = gemm(SJ_K_GEGLU, Yt, ly.wi, Gt, nullptr, F, D, sjb::TC_GEGLU, nullptr, nullptr))) return s;
+    if ((s = gemm(SJ_K_WO2, Gt, ly.wo2, nullptr, X, D, F, sjb::TC_RESID, nullptr, nullptr))) return s;
   }
   // final norm (+ LoRA): all rows -> d_hidden, [CLS] rows -> heads
   if (d_hidden) {
-    SJ_LAUNCH((sjb::add_ln<float, float>(X, nullptr, final_norm, nullptr, d_hidden, ntok, D, eps,
+    SJ_LAUNCH(SJ_K_FINAL, (sjb::add_ln<float, float>(X, nullptr, final_norm, nullptr, d_hidden, ntok, D, eps,
                                          nullptr, st)));
     if (lora_r > 0) {
-      SJ_LAUNCH((sjb::gemm_simt<float, float>(d_hidden, lora_a, nullptr, z, nullptr, ntok, lora_r, D,
+      SJ_LAUNCH(SJ_K_FINAL, (sjb::gemm_simt<float, float>(d_hidden, lora_a, nullptr, z, nullptr, ntok, lora_r, D,
                                               0, false, st)));
-      SJ_LAUNCH((sjb::gemm_simt<float, float>(z, lora_b, nullptr, nullptr, d_hidden, ntok, D,
+      SJ_LAUNCH(SJ_K_FINAL, (sjb::gemm_simt<float, float>(z, lora_b, nullptr, nullptr, d_hidden, ntok, D,
                                               lora_r, 0, false, st)));
     }
   }
   if (d_probs && has_heads) {
-    SJ_LAUNCH((sjb::add_ln<float, float>(X, nullptr, final_norm, nullptr, Hc, B, D, eps, d_cu, st)));
+    SJ_LAUNCH(SJ_K_FINAL, (sjb::add_ln<float, float>(X, nullptr, final_norm, nullptr, Hc, B, D, eps, d_cu, st)));
     if (lora_r > 0) {
-      SJ_LAUNCH((sjb::gemm_simt<float, float>(Hc, lora_a, nullptr, z, nullptr, B, lora_r, D, 0,
+      SJ_LAUNCH(SJ_K_FINAL, (sjb::gemm_simt<float, float>(Hc, lora_a, nullptr, z, nullptr, B, lora_r, D, 0,
                                               false, st)));
-      SJ_LAUNCH((sjb::gemm_simt<float, float>(z, lora_b, nullptr, nullptr, Hc, B, D, lora_r, 0,
+      SJ_LAUNCH(SJ_K_FINAL, (sjb::gemm_simt<float, float>(z, lora_b, nullptr, nullptr, Hc, B, D, lora_r, 0,
                                               false, st)));
     }
-    SJ_LAUNCH(sjb::dec_heads(Hc, B, D, head_w, head_b, spec, d_probs, st));
+    SJ_LAUNCH(SJ_K_FINAL, sjb::dec_heads(Hc, B, D, head_w, head_b, spec, d_probs, st));
   }
   return SJ_OK;
 }
@@ -606,6 +658,29 @@ int sj_fast_sync(sj_fast* e, void* stream) {
 }
 
 int sj_fast_launch_count(const sj_fast* e) { return e ? e->launches : 0; }
+
+int sj_fast_set_profiling(sj_fast* e, int enable) {
+  if (!e) return SJ_ERR_INVALID;
+  e->profiling = enable != 0;
+  return SJ_OK;
+}
+
+int sj_fast_profile(sj_fast* e, double* ms, int64_t* launches, int reset) {
+  if (!e) return SJ_ERR_INVALID;
+  cudaError_t rc = cudaSetDevice(e->cfg.device);
+  if (rc != cudaSuccess) return e->cuda_fail(rc, "cudaSetDevice");
+  int s = e->collect_profile();
+  if (s) return s;
+  for (int k = 0; k < SJ_K_COUNT; ++k) {
+    if (ms) ms[k] = e->prof_ms[k];
+    if (launches) launches[k] = e->prof_n[k];
+    if (reset) {
+      e->prof_ms[k] = 0;
+      e->prof_n[k] = 0;
+    }
+  }
+  return SJ_OK;
+}
 
 const char* sj_fast_last_error(const sj_fast* e) { return e ? e->err.c_str() : "null engine"; }
 

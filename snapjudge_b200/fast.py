@@ -142,3 +142,14 @@ class FastSnapjudge:
 
     def launch_count(self) -> int:
         return _lib.lib().sj_fast_launch_count(self._h)
+
+    def set_profiling(self, enable: bool) -> None:
+        check(_lib.lib().sj_fast_set_profiling(self._h, int(enable)), self._h)
+
+    def profile(self, reset: bool = True) -> dict[str, tuple[float, int]]:
+        """{kernel class: (total ms, launches)} accumulated since the last reset."""
+        n = len(_lib.KERNEL_CLASSES)
+        ms = (C.c_double * n)()
+        cnt = (C.c_int64 * n)()
+        check(_lib.lib().sj_fast_profile(self._h, ms, cnt, int(reset)), self._h)
+        return {k: (ms[i], cnt[i]) for i, k in enumerate(_lib.KERNEL_CLASSES)}
