@@ -1,0 +1,379 @@
+#!/usr/bin/env python3
+"""Encoder tokens/sec on B200 for snapjudge's serving batch; prints one JSON line.
+
+Workload: the base-encoder architecture (12 pre-LN layers,
+d_model 768, 12 heads x 64, GEGLU FFN 2048, vocab 32768, RoPE), seeded
+synthetic N(0, 0.02) weights, 32768 requests per GPU packed varlen with
+lengths log-normal(median 48, sigma 0.8) clipped to [4, 512], uniform token
+ids, and four linear decision heads on [CLS] (choice-3, choice-8, score-5,
+noul).  One step = the whole batch of this rank through the encoder and the
+heads.  Per-GPU work is fixed (weak scaling); ranks share nothing on the data
+path (no collective); the max over ranks of the device time is reported.
+
+* value  — device-resident inputs, CUDA events on the launch stream.
+* e2e    — the public C ABI call sj_fast_decide with pinned host buffers:
+           host->device ids, device->host probabilities inside the timed region.
+* roofline — the dominant kernel (Wi projection + GEGLU gate), its launches
+           timed live with CUDA events inside the timed steps.
+* cpu_baseline — the reference's own CPU forward (src/model.cpp, compiled
+           unchanged into oracle/_ref with OpenBLAS) on a bounded sample.
+* attention — C2 (64 x 12 heads x 64, lengths U[32, 512]) attention TFLOP/s.
+
+`--impl reference` times only the reference CPU forward (rank 0).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+# the reference CPU path reads its thread counts at load time
+_NPROC = os.cpu_count() or 1
+os.environ.setdefault("OPENBLAS_NUM_THREADS", str(_NPROC))
+os.environ.setdefault("SNAPJUDGE_THREADS", str(_NPROC))
+
+import numpy as np  # noqa: E402
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from snapjudge_b200 import synth  # noqa: E402
+
+PEAKS = os.path.join(ROOT, "MEASURED_PEAKS.json")
+FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# DRAM traffic per token of the Wi+GEGLU launch, from the committed ncu capture
+# (profiles/gemm_geglu_c5.md); None until a capture exists.
+GEGLU_DRAM_BYTES_PER_TOKEN = None
+
+
+def peaks():
+    try:
+        with open(PEAKS) as f:
+            p = json.load(f)
+        return p, "measured"
+    except (OSError, ValueError):
+        return FALLBACK, "fallback"
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi samples (200 ms) of SM clock and throttle reasons during a region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.gpu)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ workload
+def workload(rank: int, requests: int):
+    spec = synth.SPECS["c5"]
+    lengths = synth.make_lengths(spec, batch=requests, seed=spec.seed + 1000 + 7919 * rank)
+    ids = synth.make_ids(spec, lengths, seed=spec.seed + 2000 + 7919 * rank)
+    return spec, lengths, ids
+
+
+def passes(lengths: np.ndarray, max_tokens: int):
+    """Split requests into consecutive passes of at most max_tokens tokens."""
+    out, b0, tok = [], 0, 0
+    for b, n in enumerate(lengths):
+        if tok + n > max_tokens and b > b0:
+            out.append((b0, b))
+            b0, tok = b, 0
+        tok += int(n)
+    out.append((b0, len(lengths)))
+    return out
+
+
+# ------------------------------------------------------------------ CPU reference
+def reference_sample(spec, weights, seconds: float, min_req: int, max_req: int, seed: int):
+    """Time the reference CPU forward (+ the same heads) request by request.
+
+    Returns (tokens, seconds, n_requests, kind, cores)."""
+    from oracle import oracle
+    from snapjudge_b200.checkpoint import save_checkpoint
+    lengths = synth.make_lengths(spec, batch=max_req, seed=seed)
+    ids = synth.make_ids(spec, lengths, seed=seed + 1)
+    cu = synth.cu_seqlens(lengths)
+    D = spec.cfg.hidden_size
+    if oracle.ref_available():
+        d = tempfile.mkdtemp(prefix="sjref_")
+        save_checkpoint(d, spec.cfg, weights)
+        model = oracle.RefModel(d)
+        enc = lambda x: model.encode(x[None], np.ones_like(x)[None], D)[0]  # noqa: E731
+        kind = "reference"
+    else:
+        oracle.set_blas()
+        orc = oracle.Oracle(spec.cfg, weights)
+        enc = lambda x: orc.encode_padded(x[None], np.ones_like(x)[None])[0]  # noqa: E731
+        kind = "port"
+    enc(ids[:8])  # warm the BLAS threads
+    tok, n, t0 = 0, 0, time.perf_counter()
+    while n < max_req and (n < min_req or time.perf_counter() - t0 < seconds):
+        h = enc(ids[cu[n]:cu[n + 1]])
+        oracle.task_heads(h[:1], weights, spec.heads)
+        tok += int(lengths[n])
+        n += 1
+    return tok, time.perf_counter() - t0, n, kind, _NPROC
+
+
+# ------------------------------------------------------------------ main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--requests", type=int, default=32768, help="requests per GPU per step")
+    ap.add_argument("--max-tokens", type=int, default=262144, help="tokens per device pass")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    a = ap.parse_args()
+
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    spec = synth.SPECS["c5"]
+    cfgd = {"workload": "c5 serving batch: base encoder 12x768 (12 heads x 64, GEGLU 2048, "
+                        "vocab 32768), requests packed varlen, lengths lognormal(48, 0.8) "
+                        "clipped to [4, 512], 4 [CLS] heads (choice-3/8, score-5, noul)",
+            "requests_per_gpu": a.requests, "parallelism": f"request-sharded x{world}",
+            "l2": "inputs larger than L2 (bf16 weights 0.17 GB + ~4 GB activations per pass)"}
+
+    if a.impl == "reference":
+        if rank != 0:
+            return 0
+        weights = synth.make_weights(spec)
+        steps = []
+        for s in range(a.warmup + a.steps):
+            tok, sec, n, kind, cores = reference_sample(spec, weights, 8.0, 4, 64,
+                                                        seed=spec.seed + 50000 + s)
+            if s >= a.warmup:
+                steps.append((tok, sec, n))
+        tok = sum(x[0] for x in steps)
+        sec = sum(x[1] for x in steps)
+        v = tok / sec
+        line = {"metric": "encoder tokens/sec", "value": v, "unit": "tokens/s", "n_gpus": world,
+                "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1e3 * sec / a.steps,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "f32", "data": "synthetic", "impl": "reference", "config": cfgd,
+                "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": kind,
+                                 "sample": f"{sum(x[2] for x in steps)} c5 requests "
+                                           f"({tok} tokens), one request per encode call"},
+                "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return 0
+
+    import torch
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    from snapjudge_b200.fast import FastSnapjudge
+
+    weights = synth.make_weights(spec)
+    _, lengths, ids = workload(rank, a.requests)
+    T = int(lengths.sum())
+    eng = FastSnapjudge(spec.cfg, weights, precision="bf16", heads=spec.heads, device=local,
+                        max_tokens=a.max_tokens)
+    nout = eng.n_out
+    dev = torch.device("cuda", local)
+    st = torch.cuda.Stream(device=dev)
+    P = passes(lengths, a.max_tokens)
+    cu_all = synth.cu_seqlens(lengths)
+    ids_d = torch.from_numpy(ids).to(dev)
+    probs_d = torch.empty(len(lengths), nout, dtype=torch.float32, device=dev)
+    pass_args = []
+    for b0, b1 in P:
+        cu_h = (cu_all[b0:b1 + 1] - cu_all[b0]).astype(np.int32)
+        pass_args.append((ids_d[int(cu_all[b0]):int(cu_all[b1])], torch.from_numpy(cu_h).to(dev),
+                          cu_h, probs_d[b0:b1]))
+    torch.cuda.synchronize()
+
+    def step():
+        for x_ids, x_cu, x_cuh, x_p in pass_args:
+            eng.encode_device(x_ids, x_cu, x_cuh, probs=x_p, stream=st)
+
+    def barrier():
+        if dist:
+            dist.barrier()
+
+    with torch.cuda.stream(st):
+        for _ in range(a.warmup):
+            step()
+    eng.sync(st)
+    eng.profile(reset=True)
+    eng.set_profiling(True)
+    barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(a.steps):
+        step()
+    e1.record(st)
+    eng.sync(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    clk = clocks.stop()
+    prof = eng.profile(reset=True)
+    eng.set_profiling(False)
+    gpu_launches = int(sum(n for _, n in prof.values()))
+    if dist:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = T * world * a.steps / (ms / 1e3)
+
+    # roofline of the dominant kernel (Wi projection + GEGLU gate)
+    pk, pk_kind = peaks()
+    D, F, L = spec.cfg.hidden_size, spec.cfg.intermediate_size, spec.cfg.num_hidden_layers
+    g_ms, g_n = prof["geglu"]
+    flops_per_launch = 2.0 * T / len(P) * 2 * F * D  # average pass size
+    dur = g_ms / max(1, g_n)
+    achieved = flops_per_launch / (dur / 1e3) / 1e12
+    peak = pk.get("bf16_tflops_sustained", FALLBACK["bf16_tflops_sustained"])
+    traffic = (GEGLU_DRAM_BYTES_PER_TOKEN * T / len(P)
+               if GEGLU_DRAM_BYTES_PER_TOKEN is not None else None)
+    roofline = {"kernel": "gemm_tc<GEGLU> (Wi projection + GEGLU gate)", "bound": "tensor",
+                "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                "peak_kind": f"{pk_kind} sustained bf16", "traffic": traffic,
+                "flops_per_launch": flops_per_launch, "launch_ms": dur,
+                "share_of_step": g_ms / ms if ms > 0 else None}
+    kernels = {k: {"ms_per_step": v[0] / a.steps, "launches_per_step": v[1] // max(1, a.steps)}
+               for k, v in prof.items()}
+
+    # end to end through the public C ABI with pinned host buffers
+    ids_pin = torch.from_numpy(ids).pin_memory()
+    cu_pin = torch.from_numpy(cu_all.astype(np.int32)).pin_memory()
+    out_pin = torch.empty(len(lengths), nout, dtype=torch.float32).pin_memory()
+    ids_np, cu_np, out_np = ids_pin.numpy(), cu_pin.numpy(), out_pin.numpy()
+    for _ in range(max(1, a.warmup)):
+        eng.decide(ids_np, lengths, out=out_np, cu=cu_np)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        eng.decide(ids_np, lengths, out=out_np, cu=cu_np)
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e = {"value": T * world * a.steps / e2e_s, "unit": "tokens/s",
+           "h2d_bytes_per_step": int(ids.nbytes + cu_np.nbytes),
+           "d2h_bytes_per_step": int(out_np.nbytes), "ms_per_step": 1e3 * e2e_s / a.steps}
+    # the device-resident and host-API results agree
+    assert np.array_equal(out_np, probs_d.cpu().numpy()), "e2e and device results differ"
+
+    line = {"metric": "encoder tokens/sec", "value": value, "unit": "tokens/s",
+            "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+            "ms_per_step": ms / a.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,0.02) weights)",
+            "config": dict(cfgd, tokens_per_gpu=T, passes=len(P), max_tokens_per_pass=a.max_tokens),
+            "clocks": clk, "e2e": e2e, "gpu_launches": gpu_launches, "roofline": roofline,
+            "kernels": kernels}
+
+    if rank == 0:
+        # attention-only C2 (second half of the metric): TFLOP/s vs the bf16 peak
+        from snapjudge_b200 import ops
+        lens2, q, k, v = synth.attention_inputs()
+        cu2 = synth.cu_seqlens(lens2)
+        T2, H2, Dh2 = q.shape
+        qkv = torch.from_numpy(np.concatenate([q, k, v], 1).reshape(T2, -1)).to(dev).to(
+            torch.bfloat16)
+        fl = float(sum(4 * int(n) ** 2 * Dh2 * H2 for n in lens2))
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # > L2 (126 MB)
+        reps, ams = 20, 0.0
+        with torch.cuda.stream(st):
+            for _ in range(5):
+                ops.attn(qkv, cu2, H2, Dh2)
+            for _ in range(reps):
+                flush.zero_()
+                a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a0.record(st)
+                ops.attn(qkv, cu2, H2, Dh2)
+                a1.record(st)
+                a1.synchronize()
+                ams += a0.elapsed_time(a1) / reps
+        burst = pk.get("bf16_tflops", FALLBACK["bf16_tflops"])
+        line["attention"] = {"config": "c2: 64 seqs x 12 heads x 64, lengths U[32,512], bf16",
+                             "ms": ams, "tflops": fl / (ams / 1e3) / 1e12,
+                             "frac_of_peak": fl / (ams / 1e3) / 1e12 / burst,
+                             "peak": burst, "peak_kind": f"{pk_kind} burst bf16",
+                             "l2": "L2 flushed (256 MB write) before every timed launch"}
+        if world == 1 and not a.no_cpu_baseline:
+            tok, sec, n, kind, cores = reference_sample(spec, weights, a.cpu_seconds, 8, 4096,
+                                                        seed=spec.seed + 40000)
+            line["cpu_baseline"] = {"value": tok / sec, "unit": "tokens/s", "cores": cores,
+                                    "kind": kind,
+                                    "sample": f"{n} c5 requests ({tok} tokens), one request per "
+                                              f"encode call, {sec:.1f} s"}
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    eng.close()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

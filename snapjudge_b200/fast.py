@@ -107,12 +107,16 @@ class FastSnapjudge:
         out = self.encode_packed(ids.reshape(-1), np.full(B, L, np.int64), kv_lens=lens)
         return out.reshape(B, L, self.D)
 
-    def decide(self, ids, lengths) -> np.ndarray:
+    def decide(self, ids, lengths, out: np.ndarray | None = None, cu=None) -> np.ndarray:
+        """Encoder + heads; probs [B, sum n_out].  `out` / `cu` may be preallocated
+        (e.g. pinned) host arrays: float32 [B, n_out] and int32 [B + 1]."""
         ids = np.ascontiguousarray(ids, dtype=np.int64)
         lengths = np.asarray(lengths, dtype=np.int64)
-        cu = np.zeros(len(lengths) + 1, np.int32)
-        np.cumsum(lengths, out=cu[1:])
-        out = np.empty((len(lengths), max(1, self.n_out)), np.float32)
+        if cu is None:
+            cu = np.zeros(len(lengths) + 1, np.int32)
+            np.cumsum(lengths, out=cu[1:])
+        if out is None:
+            out = np.empty((len(lengths), max(1, self.n_out)), np.float32)
         check(_lib.lib().sj_fast_decide(self._h, _ptr(ids), _ptr(cu), len(lengths), _ptr(out)),
               self._h)
         return out
