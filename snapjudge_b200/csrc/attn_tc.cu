@@ -47,7 +47,13 @@ __device__ __forceinline__ void record_err(int* err, int code) {
   atomicCAS(err ? err : &g_attn_tc_err, 0, code);
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+__device__ __forceinline__ float ex2(float x) {  // 2^x on the MUFU (ex2.approx, flush-to-zero)
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__global__ void __launch_bounds__(kThreads, 2)
     attn_tc_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapKV,
                    const int32_t* __restrict__ cu, const int32_t* __restrict__ kv_lens,
                    bf16* __restrict__ O, int H, int window, const int2* __restrict__ tiles,
@@ -214,7 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld32(tO + (i & 1) * DH + lane_off, ra);
       tmem_ld32(tO + (i & 1) * DH + 32 + lane_off, rb);
       tmem_ld_wait();
-      const float c = (m_acc == -INFINITY) ? 0.f : exp2f(m_acc - m_i);
+      const float c = (m_acc == -INFINITY) ? 0.f : ex2(m_acc - m_i);
 #pragma unroll
       for (int d = 0; d < 32; ++d) {
         o[d] = o[d] * c + __uint_as_float(ra[d]);
@@ -241,18 +247,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_empty[j & 1]);
       const int kbase = (t_lo + j) * KT;
-      float s[KT];
+      // scores in place: ra/rb hold S_j row (keys kbase..+63) as fp32 bits
       float tmax = -INFINITY;
 #pragma unroll
       for (int c = 0; c < KT; ++c) {
         const int key = kbase + c;
-        const float v = __uint_as_float(c < 32 ? ra[c] : rb[c - 32]) * scale;
-        s[c] = (key >= lo && key < hi) ? v : -INFINITY;
-        tmax = fmaxf(tmax, s[c]);
+        uint32_t& cell = c < 32 ? ra[c] : rb[c - 32];
+        const float v = (key >= lo && key < hi) ? __uint_as_float(cell) * scale : -INFINITY;
+        cell = __float_as_uint(v);
+        tmax = fmaxf(tmax, v);
       }
       const float m_new = fmaxf(m, tmax);
       const float m_use = m_new == -INFINITY ? 0.f : m_new;
-      const float corr = m == -INFINITY ? 0.f : exp2f(m - m_use);
+      const float corr = m == -INFINITY ? 0.f : ex2(m - m_use);
       float rs = 0.f;
       // P_j = 2^(s - m_new) -> bf16, written in the 128-byte-swizzled K-major layout
       uint8_t* prow = sP + (j & 1) * P_BYTES + r * 128;
@@ -261,8 +268,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t w[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float p0 = exp2f(s[ch * 8 + 2 * e] - m_use);
-          const float p1 = exp2f(s[ch * 8 + 2 * e + 1] - m_use);
+          const int c0 = ch * 8 + 2 * e;
+          const float p0 = ex2(__uint_as_float(c0 < 32 ? ra[c0] : rb[c0 - 32]) - m_use);
+          const float p1 = ex2(__uint_as_float(c0 + 1 < 32 ? ra[c0 + 1] : rb[c0 - 31]) - m_use);
           __nv_bfloat162 pb = __floats2bfloat162_rn(p0, p1);
           const float2 pr = __bfloat1622float2(pb);
           rs += pr.x + pr.y;  // normaliser from the rounded P the MMA sees
@@ -283,7 +291,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) { record_err(err, 18); abort_sh = 1; }
     } else if (live) {
       // o is relative to m_acc (= final running max); l to m
-      const float c = (m_acc == -INFINITY || m == -INFINITY) ? 0.f : exp2f(m_acc - (m == -INFINITY ? 0.f : m));
+      const float c = (m_acc == -INFINITY || m == -INFINITY) ? 0.f : ex2(m_acc - m);
       const float inv = l > 0.f ? c / l : 0.f;
       float v[DH];
 #pragma unroll
