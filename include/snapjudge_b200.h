@@ -88,6 +88,19 @@ int sj_rope(sj_bf16* qkv, const float* cos_t, const float* sin_t, const int32_t*
 int sj_attn(const sj_bf16* qkv, const int32_t* cu_seqlens, const int32_t* cu_seqlens_host,
             const int32_t* kv_lens, sj_bf16* O, int B, int H, int Dh, int window, void* stream);
 
+/* sj_attn with the engine's longest-first query-tile schedule, for callers
+ * that cannot allocate device memory (their device memory belongs to their own
+ * pool allocator, or allocation is not allowed on their inference path).  No
+ * counterpart in the reference.  The schedule lives in a static device array
+ * of the library (512 KiB per GPU, resident until exit): at most 65536 query
+ * tiles per call (tiles of 128 rows at head_dim 64, else 64 rows), larger
+ * batches return SJ_ERR_INVALID.  The first call on a device looks the array
+ * up (make it before any stream capture); calls whose launches overlap on the
+ * GPU share the array and race.  Arguments as sj_attn. */
+int sj_attn_noalloc(const sj_bf16* qkv, const int32_t* cu_seqlens, const int32_t* cu_seqlens_host,
+                    const int32_t* kv_lens, sj_bf16* O, int B, int H, int Dh, int window,
+                    void* stream);
+
 /* ------------------------------------------------------------------------- */
 /* 2. Encoder engine (replaces FastSnapjudge, include/snapjudge/fast.hpp).    */
 /* ------------------------------------------------------------------------- */

@@ -23,7 +23,7 @@ SJ_PREC_FP32 = 1
 
 # every symbol declared in include/snapjudge_b200.h
 EXPORTS = ["sj_b200_version", "sj_last_error", "sj_gemm", "sj_gemm_geglu", "sj_add_ln", "sj_rope",
-           "sj_attn", "sj_fast_create", "sj_fast_set_tensor", "sj_fast_set_heads",
+           "sj_attn", "sj_attn_noalloc", "sj_fast_create", "sj_fast_set_tensor", "sj_fast_set_heads",
            "sj_fast_commit", "sj_fast_encode", "sj_fast_decide", "sj_fast_encode_device",
            "sj_fast_sync", "sj_fast_launch_count", "sj_fast_set_profiling", "sj_fast_profile",
            "sj_fast_last_error", "sj_fast_destroy"]
@@ -68,6 +68,7 @@ def lib() -> C.CDLL:
         L.sj_add_ln.argtypes = [_P, _P, _P, _P, _P, _I, _I, C.c_float, _I, _I, _P]
         L.sj_rope.argtypes = [_P, _P, _P, _P, _P, _I, _I, _I, _P]
         L.sj_attn.argtypes = [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P]
+        L.sj_attn_noalloc.argtypes = [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P]
         L.sj_fast_create.argtypes = [C.POINTER(FastConfig), C.POINTER(_P)]
         L.sj_fast_set_tensor.argtypes = [_P, C.c_char_p, _P, C.POINTER(C.c_int64), _I]
         L.sj_fast_set_heads.argtypes = [_P, _I, C.POINTER(_I), C.POINTER(_I)]

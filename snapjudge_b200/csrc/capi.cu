@@ -41,6 +41,11 @@ int check_cu(const int32_t* cu_host, int B, int* T, int* max_len) {
 }
 }  // namespace
 
+namespace sjb {
+// Message returned by sj_last_error() on this thread (for entry points in other files).
+void set_last_error(const std::string& m) { g_err = m; }
+}  // namespace sjb
+
 extern "C" {
 
 int sj_b200_version(void) { return 100; }

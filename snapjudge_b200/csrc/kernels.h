@@ -8,7 +8,12 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <string>
+
 namespace sjb {
+
+// Set the message sj_last_error() returns on the calling thread (capi.cu).
+void set_last_error(const std::string& m);
 
 using bf16 = __nv_bfloat16;
 
