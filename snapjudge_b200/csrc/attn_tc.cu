@@ -3,19 +3,26 @@
 // Semantics of the reference attention (src/tensor.cpp:156-228): query i of
 // segment b attends keys j in [max(0, i - w), min(kv_len, i + w + 1))
 // (w = 0: all j < kv_len), scale 1/sqrt(64), max-subtracted softmax.  bf16
-// q/k/v/o, fp32 scores and accumulation; P is rounded to bf16 for the P.V MMA.
+// q/k/v/o, fp32 scores and accumulation; P is rounded to bf16 for the P.V MMA
+// and the row normaliser is summed from the rounded P.
 //
-// One CTA = 128 queries of one (segment, head).  192 threads:
+// Persistent: 2 CTAs per SM walk a strided list of work items (128 queries of
+// one segment x one head), longest segments first.  192 threads per CTA:
 //   warps 0-3  softmax: thread = query row = TMEM lane; online softmax in
-//              registers; P (bf16) written to swizzled shared memory; the
-//              output accumulator o[64] lives in registers
-//   warp 4     TMA producer: Q once, then K/V tiles of 64 keys (3-stage ring)
-//   warp 5     MMA issuer: S_j = Q K_j^T into TMEM S[j%2] (M=128, N=64, K=64),
-//              O_j = P_j V_j into TMEM O[j%2] (V is the MN-major operand)
+//              registers; P (bf16) written to 128-byte-swizzled shared memory;
+//              the output accumulator o[64] lives in registers
+//   warp 4     TMA producer: Q of each item, then its K/V tiles of 64 keys
+//              through a 3-stage ring that runs on across items
+//   warp 5     MMA issuer: S_j = Q K_j^T into TMEM S[g%2] (M=128, N=64, K=64),
+//              O_j = P_j V_j into TMEM O[g%2] (V is the MN-major operand);
+//              g counts key tiles across items, so every buffer's phase runs
+//              on across items as well
 // The softmax warps fold O_{j-1} into o[] while the tensor core computes
-// S_{j+1} and O_j, so MMA and softmax overlap.  Keys past kv_len and outside
-// the window are masked with -inf; key tiles wholly outside the window are
-// skipped.  All mbarrier waits are bounded (error code, no trap).
+// S_{j+1} and O_j.  Q is reloaded for the next item as soon as the last S MMA
+// of the current one has been issued.  Keys past kv_len and outside the window
+// are masked with -inf (tiles wholly inside skip the mask); key tiles wholly
+// outside the window are skipped.  All mbarrier waits are bounded (error code,
+// no trap).
 #include <algorithm>
 
 #include "common.cuh"
@@ -30,7 +37,7 @@ __device__ int g_attn_tc_err;
 namespace {
 using namespace tc;
 
-constexpr int QT = 128;        // queries per CTA
+constexpr int QT = 128;        // queries per work item
 constexpr int KT = 64;         // keys per tile
 constexpr int DH = 64;
 constexpr int STAGES = 3;
@@ -53,41 +60,60 @@ __device__ __forceinline__ float ex2(float x) {  // 2^x on the MUFU (ex2.approx,
   return y;
 }
 
+struct Item {
+  int b, q0, h, s0, n, nk, t_lo, n_kv;
+};
+
+// Work item w: list form (tiles != null): tile w / H, head w % H; grid form:
+// w = ((b * nqt) + qtile) * H + h.  False for idle grid-form items.
+__device__ __forceinline__ bool decode(int w, const int2* tiles, int H, int nqt,
+                                       const int32_t* cu, const int32_t* kv_lens, int window,
+                                       Item& it) {
+  it.h = w % H;
+  const int rest = w / H;
+  if (tiles) {
+    const int2 t = tiles[rest];
+    it.b = t.x;
+    it.q0 = t.y;
+  } else {
+    it.b = rest / nqt;
+    it.q0 = (rest % nqt) * QT;
+  }
+  it.s0 = cu[it.b];
+  it.n = cu[it.b + 1] - it.s0;
+  if (it.q0 >= it.n) return false;
+  int nk = kv_lens ? kv_lens[it.b] : it.n;
+  it.nk = min(nk, it.n);
+  int k_lo = 0, k_hi = it.nk;
+  if (window > 0) {
+    k_lo = max(0, it.q0 - window);
+    k_hi = min(it.nk, it.q0 + QT - 1 + window + 1);
+  }
+  it.t_lo = k_lo / KT;
+  it.n_kv = k_hi > k_lo ? (k_hi - 1) / KT - it.t_lo + 1 : 0;
+  return true;
+}
+
 __global__ void __launch_bounds__(kThreads, 2)
     attn_tc_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapKV,
                    const int32_t* __restrict__ cu, const int32_t* __restrict__ kv_lens,
                    bf16* __restrict__ O, int H, int window, const int2* __restrict__ tiles,
-                   int* err) {
+                   int n_items, int nqt, int* err) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t q_full, kv_full[STAGES], kv_empty[STAGES], s_full[2], s_empty[2], p_full[2],
-      o_full[2], o_empty[2], drain;
+  __shared__ uint64_t q_full, q_empty, kv_full[STAGES], kv_empty[STAGES], s_full[2], s_empty[2],
+      p_full[2], o_full[2], o_empty[2], drain;
   __shared__ uint32_t tmem_sh;
   __shared__ volatile int abort_sh;
 
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t* sQ = smem;
-  uint8_t* sKV = smem + Q_BYTES;                       // stage s: K at s*2*KV, V at +KV
-  uint8_t* sP = smem + Q_BYTES + STAGES * 2 * KV_BYTES; // P[2]
-
+  uint8_t* sKV = smem + Q_BYTES;                        // stage s: K at s*2*KV, V at +KV
+  uint8_t* sP = smem + Q_BYTES + STAGES * 2 * KV_BYTES;  // P[2]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int2 tl = tiles ? tiles[blockIdx.x] : make_int2(blockIdx.z, blockIdx.x * QT);
-  const int b = tl.x, q0 = tl.y, h = blockIdx.y;
-  const int s0 = cu[b];
-  const int n = cu[b + 1] - s0;
-  if (q0 >= n) return;  // idle tile of the grid form (whole CTA exits before any setup)
-  int nk = kv_lens ? kv_lens[b] : n;
-  nk = min(nk, n);
-  // key range visible to any query of this tile, in whole key tiles
-  int k_lo = 0, k_hi = nk;
-  if (window > 0) {
-    k_lo = max(0, q0 - window);
-    k_hi = min(nk, q0 + QT - 1 + window + 1);
-  }
-  const int t_lo = k_lo / KT;
-  const int n_kv = k_hi > k_lo ? (k_hi - 1) / KT - t_lo + 1 : 0;
 
   if (threadIdx.x == 0) {
     mbar_init(&q_full, 1);
+    mbar_init(&q_empty, 1);
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
@@ -115,26 +141,36 @@ __global__ void __launch_bounds__(kThreads, 2)
       // ---------------- TMA producer ----------------
       tma_prefetch(&mapQ);
       tma_prefetch(&mapKV);
-      mbar_expect_tx(&q_full, Q_BYTES);
-      tma_load_2d(sQ, &mapQ, &q_full, h * DH, s0 + q0);
-      int stage = 0;
-      uint32_t phase = 0;
-      int issued = 0;
-      for (int j = 0; j < n_kv && !abort_sh; ++j) {
-        if (!mbar_wait(&kv_empty[stage], phase ^ 1)) {
-          record_err(err, 11);
+      int stage = 0, issued = 0;
+      uint32_t phase = 0, qi = 0;
+      for (int w = blockIdx.x; w < n_items && !abort_sh; w += gridDim.x) {
+        Item it;
+        if (!decode(w, tiles, H, nqt, cu, kv_lens, window, it) || it.n_kv == 0) continue;
+        if (!mbar_wait(&q_empty, (qi & 1) ^ 1)) {
+          record_err(err, 10);
           abort_sh = 1;
           break;
         }
-        const int row = s0 + (t_lo + j) * KT;
-        uint8_t* dst = sKV + stage * 2 * KV_BYTES;
-        mbar_expect_tx(&kv_full[stage], 2 * KV_BYTES);
-        tma_load_2d(dst, &mapKV, &kv_full[stage], (H + h) * DH, row);
-        tma_load_2d(dst + KV_BYTES, &mapKV, &kv_full[stage], (2 * H + h) * DH, row);
-        ++issued;
-        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        mbar_expect_tx(&q_full, Q_BYTES);
+        tma_load_2d(sQ, &mapQ, &q_full, it.h * DH, it.s0 + it.q0);
+        ++qi;
+        for (int j = 0; j < it.n_kv; ++j) {
+          if (!mbar_wait(&kv_empty[stage], phase ^ 1)) {
+            record_err(err, 11);
+            abort_sh = 1;
+            break;
+          }
+          const int row = it.s0 + (it.t_lo + j) * KT;
+          uint8_t* dst = sKV + stage * 2 * KV_BYTES;
+          mbar_expect_tx(&kv_full[stage], 2 * KV_BYTES);
+          tma_load_2d(dst, &mapKV, &kv_full[stage], (H + it.h) * DH, row);
+          tma_load_2d(dst + KV_BYTES, &mapKV, &kv_full[stage], (2 * H + it.h) * DH, row);
+          ++issued;
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
       }
-      if (!mbar_wait(&q_full, 0)) record_err(err, 12);
+      // drain: every issued copy has landed before the CTA can exit
+      if (qi > 0 && !mbar_wait(&q_full, (qi - 1) & 1)) record_err(err, 12);
       for (int i = 0; i < STAGES && i < issued; ++i) {
         if (--stage < 0) { stage = STAGES - 1; phase ^= 1; }
         if (!mbar_wait(&kv_full[stage], phase)) record_err(err, 13);
@@ -144,47 +180,61 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
       const uint32_t q_addr = smem_u32(sQ);
-      bool ok = n_kv == 0 || mbar_wait(&q_full, 0);
-      if (!ok) { record_err(err, 14); abort_sh = 1; }
       int stage = 0;
-      uint32_t phase = 0;
-      // S_j needs stage(j); O_j needs P_j and stage(j) (V); keep the stage of j-1
-      int prev_stage = 0;
-      for (int j = 0; j <= n_kv && ok && !abort_sh; ++j) {
-        if (j < n_kv) {
-          if (!mbar_wait(&kv_full[stage], phase) || !mbar_wait(&s_empty[j & 1], ((j >> 1) & 1) ^ 1)) {
-            record_err(err, 15);
-            abort_sh = 1;
-            break;
-          }
-          fence_after_sync();
-          const uint32_t k_addr = smem_u32(sKV + stage * 2 * KV_BYTES);
-#pragma unroll
-          for (int kk = 0; kk < DH / 16; ++kk)
-            mma_bf16(tS + (j & 1) * KT, desc_kmajor_sw128(q_addr + kk * 32),
-                     desc_kmajor_sw128(k_addr + kk * 32), IDESC_S, kk != 0);
-          mma_commit(&s_full[j & 1]);
+      uint32_t phase = 0, qi = 0, g = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; w < n_items && ok && !abort_sh; w += gridDim.x) {
+        Item it;
+        if (!decode(w, tiles, H, nqt, cu, kv_lens, window, it) || it.n_kv == 0) continue;
+        if (!mbar_wait(&q_full, qi & 1)) {
+          record_err(err, 14);
+          abort_sh = 1;
+          break;
         }
-        if (j >= 1) {
-          const int i = j - 1;
-          if (!mbar_wait(&p_full[i & 1], (i >> 1) & 1) ||
-              !mbar_wait(&o_empty[i & 1], ((i >> 1) & 1) ^ 1)) {
-            record_err(err, 16);
-            abort_sh = 1;
-            break;
-          }
-          fence_after_sync();
-          const uint32_t p_addr = smem_u32(sP + (i & 1) * P_BYTES);
-          const uint32_t v_addr = smem_u32(sKV + prev_stage * 2 * KV_BYTES + KV_BYTES);
+        int prev_stage = 0;
+        for (int j = 0; j <= it.n_kv; ++j) {
+          if (j < it.n_kv) {
+            const uint32_t gj = g + j;
+            if (!mbar_wait(&kv_full[stage], phase) ||
+                !mbar_wait(&s_empty[gj & 1], ((gj >> 1) & 1) ^ 1)) {
+              record_err(err, 15);
+              abort_sh = 1;
+              ok = false;
+              break;
+            }
+            fence_after_sync();
+            const uint32_t k_addr = smem_u32(sKV + stage * 2 * KV_BYTES);
 #pragma unroll
-          for (int kk = 0; kk < KT / 16; ++kk)
-            mma_bf16(tO + (i & 1) * DH, desc_kmajor_sw128(p_addr + kk * 32),
-                     desc_mnmajor_sw128(v_addr + kk * 16 * 128), IDESC_O, kk != 0);
-          mma_commit(&o_full[i & 1]);
-          mma_commit(&kv_empty[prev_stage]);
+            for (int kk = 0; kk < DH / 16; ++kk)
+              mma_bf16(tS + (gj & 1) * KT, desc_kmajor_sw128(q_addr + kk * 32),
+                       desc_kmajor_sw128(k_addr + kk * 32), IDESC_S, kk != 0);
+            mma_commit(&s_full[gj & 1]);
+            if (j == it.n_kv - 1) mma_commit(&q_empty);  // Q is free once its last S is done
+          }
+          if (j >= 1) {
+            const uint32_t i = g + j - 1;
+            if (!mbar_wait(&p_full[i & 1], (i >> 1) & 1) ||
+                !mbar_wait(&o_empty[i & 1], ((i >> 1) & 1) ^ 1)) {
+              record_err(err, 16);
+              abort_sh = 1;
+              ok = false;
+              break;
+            }
+            fence_after_sync();
+            const uint32_t p_addr = smem_u32(sP + (i & 1) * P_BYTES);
+            const uint32_t v_addr = smem_u32(sKV + prev_stage * 2 * KV_BYTES + KV_BYTES);
+#pragma unroll
+            for (int kk = 0; kk < KT / 16; ++kk)
+              mma_bf16(tO + (i & 1) * DH, desc_kmajor_sw128(p_addr + kk * 32),
+                       desc_mnmajor_sw128(v_addr + kk * 16 * 128), IDESC_O, kk != 0);
+            mma_commit(&o_full[i & 1]);
+            mma_commit(&kv_empty[prev_stage]);
+          }
+          prev_stage = stage;
+          if (j < it.n_kv && ++stage == STAGES) { stage = 0; phase ^= 1; }
         }
-        prev_stage = stage;
-        if (j < n_kv && ++stage == STAGES) { stage = 0; phase ^= 1; }
+        g += it.n_kv;
+        ++qi;
       }
       mma_commit(&drain);
       if (!mbar_wait(&drain, 0)) record_err(err, 17);
@@ -192,121 +242,144 @@ __global__ void __launch_bounds__(kThreads, 2)
   } else {
     // ---------------- softmax warps 0-3 ----------------
     const int r = warp * 32 + lane;  // query row in the tile = TMEM lane
-    const int i_q = q0 + r;
-    const bool live = i_q < n;
-    int lo = 0, hi = nk;
-    if (window > 0) {
-      lo = max(0, i_q - window);
-      hi = min(nk, i_q + window + 1);
-    }
     const float scale = 0.125f * 1.4426950408889634f;  // log2(e) / sqrt(64)
     const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-    float o[DH];
-#pragma unroll
-    for (int d = 0; d < DH; ++d) o[d] = 0.f;
-    float m = -INFINITY, l = 0.f;
-    float m_prev_tile = -INFINITY;  // running max used for P_{j-1}
-    float m_acc = -INFINITY;        // scale o[] currently refers to
+    uint32_t g = 0;
     bool failed = false;
-
-    auto fold = [&](int i, float m_i) -> bool {
-      // o = o * 2^(m_acc - m_i) + O_i  (O_i was computed against m_i)
-      int okw = 1;
-      if (lane == 0) okw = mbar_wait(&o_full[i & 1], (i >> 1) & 1) ? 1 : 0;
-      okw = __shfl_sync(0xffffffffu, okw, 0);
-      if (!okw) return false;
-      fence_after_sync();
-      uint32_t ra[32], rb[32];
-      tmem_ld32(tO + (i & 1) * DH + lane_off, ra);
-      tmem_ld32(tO + (i & 1) * DH + 32 + lane_off, rb);
-      tmem_ld_wait();
-      const float c = (m_acc == -INFINITY) ? 0.f : ex2(m_acc - m_i);
-#pragma unroll
-      for (int d = 0; d < 32; ++d) {
-        o[d] = o[d] * c + __uint_as_float(ra[d]);
-        o[32 + d] = o[32 + d] * c + __uint_as_float(rb[d]);
+    for (int w = blockIdx.x; w < n_items && !failed && !abort_sh; w += gridDim.x) {
+      Item it;
+      if (!decode(w, tiles, H, nqt, cu, kv_lens, window, it)) continue;
+      const int i_q = it.q0 + r;
+      const bool live = i_q < it.n;
+      bf16* orow = O + (int64_t)(it.s0 + i_q) * H * DH + it.h * DH;
+      if (it.n_kv == 0) {  // no visible key at all: the reference's empty sum gives 0
+        if (live)
+          for (int q = 0; q < 8; ++q) reinterpret_cast<uint4*>(orow)[q] = make_uint4(0, 0, 0, 0);
+        continue;
       }
-      m_acc = m_i;
-      fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&o_empty[i & 1]);
-      return true;
-    };
-
-    for (int j = 0; j < n_kv; ++j) {
-      int okw = 1;
-      if (lane == 0) okw = mbar_wait(&s_full[j & 1], (j >> 1) & 1) ? 1 : 0;
-      okw = __shfl_sync(0xffffffffu, okw, 0);
-      if (!okw || abort_sh) { failed = !okw; break; }
-      fence_after_sync();
-      uint32_t ra[32], rb[32];
-      tmem_ld32(tS + (j & 1) * KT + lane_off, ra);
-      tmem_ld32(tS + (j & 1) * KT + 32 + lane_off, rb);
-      tmem_ld_wait();
-      fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_empty[j & 1]);
-      const int kbase = (t_lo + j) * KT;
-      // scores in place: ra/rb hold S_j row (keys kbase..+63) as fp32 bits
-      float tmax = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < KT; ++c) {
-        const int key = kbase + c;
-        uint32_t& cell = c < 32 ? ra[c] : rb[c - 32];
-        const float v = (key >= lo && key < hi) ? __uint_as_float(cell) * scale : -INFINITY;
-        cell = __float_as_uint(v);
-        tmax = fmaxf(tmax, v);
+      int lo = 0, hi = it.nk;
+      if (window > 0) {
+        lo = max(0, i_q - window);
+        hi = min(it.nk, i_q + window + 1);
       }
-      const float m_new = fmaxf(m, tmax);
-      const float m_use = m_new == -INFINITY ? 0.f : m_new;
-      const float corr = m == -INFINITY ? 0.f : ex2(m - m_use);
-      float rs = 0.f;
-      // P_j = 2^(s - m_new) -> bf16, written in the 128-byte-swizzled K-major layout
-      uint8_t* prow = sP + (j & 1) * P_BYTES + r * 128;
+      float o[DH];
 #pragma unroll
-      for (int ch = 0; ch < KT / 8; ++ch) {
-        uint32_t w[4];
+      for (int d = 0; d < DH; ++d) o[d] = 0.f;
+      float m = -INFINITY, l = 0.f;
+      float m_prev_tile = -INFINITY;  // running max used for P_{j-1}
+      float m_acc = -INFINITY;        // scale o[] currently refers to
+
+      auto fold = [&](uint32_t i, float m_i) -> bool {
+        // o = o * 2^(m_acc - m_i) + O_i  (O_i was computed against m_i)
+        int okw = 1;
+        if (lane == 0) okw = mbar_wait(&o_full[i & 1], (i >> 1) & 1) ? 1 : 0;
+        okw = __shfl_sync(0xffffffffu, okw, 0);
+        if (!okw) return false;
+        fence_after_sync();
+        uint32_t ra[32], rb[32];
+        tmem_ld32(tO + (i & 1) * DH + lane_off, ra);
+        tmem_ld32(tO + (i & 1) * DH + 32 + lane_off, rb);
+        tmem_ld_wait();
+        const float c = (m_acc == -INFINITY) ? 0.f : ex2(m_acc - m_i);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int c0 = ch * 8 + 2 * e;
-          const float p0 = ex2(__uint_as_float(c0 < 32 ? ra[c0] : rb[c0 - 32]) - m_use);
-          const float p1 = ex2(__uint_as_float(c0 + 1 < 32 ? ra[c0 + 1] : rb[c0 - 31]) - m_use);
-          __nv_bfloat162 pb = __floats2bfloat162_rn(p0, p1);
-          const float2 pr = __bfloat1622float2(pb);
-          rs += pr.x + pr.y;  // normaliser from the rounded P the MMA sees
-          w[e] = *reinterpret_cast<uint32_t*>(&pb);
+        for (int d = 0; d < 32; ++d) {
+          o[d] = o[d] * c + __uint_as_float(ra[d]);
+          o[32 + d] = o[32 + d] * c + __uint_as_float(rb[d]);
         }
-        *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        m_acc = m_i;
+        fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&o_empty[i & 1]);
+        return true;
+      };
+
+      for (int j = 0; j < it.n_kv; ++j) {
+        const uint32_t gj = g + j;
+        int okw = 1;
+        if (lane == 0) okw = mbar_wait(&s_full[gj & 1], (gj >> 1) & 1) ? 1 : 0;
+        okw = __shfl_sync(0xffffffffu, okw, 0);
+        if (!okw || abort_sh) { failed = true; break; }
+        fence_after_sync();
+        uint32_t ra[32], rb[32];
+        tmem_ld32(tS + (gj & 1) * KT + lane_off, ra);
+        tmem_ld32(tS + (gj & 1) * KT + 32 + lane_off, rb);
+        tmem_ld_wait();
+        fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_empty[gj & 1]);
+        const int kbase = (it.t_lo + j) * KT;
+        // scores in place: ra/rb hold the S row (keys kbase..+63) as fp32 bits
+        float tmax = -INFINITY;
+        if (window == 0 && kbase + KT <= it.nk) {  // interior tile: every key visible
+#pragma unroll
+          for (int c = 0; c < KT; ++c) {
+            uint32_t& cell = c < 32 ? ra[c] : rb[c - 32];
+            const float v = __uint_as_float(cell) * scale;
+            cell = __float_as_uint(v);
+            tmax = fmaxf(tmax, v);
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < KT; ++c) {
+            const int key = kbase + c;
+            uint32_t& cell = c < 32 ? ra[c] : rb[c - 32];
+            const float v = (key >= lo && key < hi) ? __uint_as_float(cell) * scale : -INFINITY;
+            cell = __float_as_uint(v);
+            tmax = fmaxf(tmax, v);
+          }
+        }
+        const float m_new = fmaxf(m, tmax);
+        const float m_use = m_new == -INFINITY ? 0.f : m_new;
+        const float corr = m == -INFINITY ? 0.f : ex2(m - m_use);
+        float rs = 0.f;
+        // P_j = 2^(s - m_new) -> bf16, written in the 128-byte-swizzled K-major layout
+        uint8_t* prow = sP + (gj & 1) * P_BYTES + r * 128;
+#pragma unroll
+        for (int ch = 0; ch < KT / 8; ++ch) {
+          uint32_t wv[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int c0 = ch * 8 + 2 * e;
+            const float p0 = ex2(__uint_as_float(c0 < 32 ? ra[c0] : rb[c0 - 32]) - m_use);
+            const float p1 = ex2(__uint_as_float(c0 + 1 < 32 ? ra[c0 + 1] : rb[c0 - 31]) - m_use);
+            __nv_bfloat162 pb = __floats2bfloat162_rn(p0, p1);
+            const float2 pr = __bfloat1622float2(pb);
+            rs += pr.x + pr.y;  // normaliser from the rounded P the MMA sees
+            wv[e] = *reinterpret_cast<uint32_t*>(&pb);
+          }
+          *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) =
+              make_uint4(wv[0], wv[1], wv[2], wv[3]);
+        }
+        l = l * corr + rs;
+        m = m_new;
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // P visible to the MMA
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[gj & 1]);
+        if (j >= 1 && !fold(gj - 1, m_prev_tile)) { failed = true; break; }
+        m_prev_tile = m_use;
       }
-      l = l * corr + rs;
-      m = m_new;
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // P visible to the MMA
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[j & 1]);
-      if (j >= 1 && !fold(j - 1, m_prev_tile)) { failed = true; break; }
-      m_prev_tile = m_use;
+      if (failed || !fold(g + it.n_kv - 1, m_prev_tile)) { failed = true; break; }
+      g += it.n_kv;
+      if (live) {
+        // o is relative to m_acc (= the final running max); l to m
+        const float c = (m_acc == -INFINITY || m == -INFINITY) ? 0.f : ex2(m_acc - m);
+        const float inv = l > 0.f ? c / l : 0.f;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          uint32_t wv[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            __nv_bfloat162 hb =
+                __floats2bfloat162_rn(o[q * 8 + 2 * e] * inv, o[q * 8 + 2 * e + 1] * inv);
+            wv[e] = *reinterpret_cast<uint32_t*>(&hb);
+          }
+          reinterpret_cast<uint4*>(orow)[q] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+        }
+      }
     }
-    if (!failed && !abort_sh && n_kv > 0 && !fold(n_kv - 1, m_prev_tile)) failed = true;
-    if (failed) {
-      if (lane == 0) { record_err(err, 18); abort_sh = 1; }
-    } else if (live) {
-      // o is relative to m_acc (= final running max); l to m
-      const float c = (m_acc == -INFINITY || m == -INFINITY) ? 0.f : ex2(m_acc - m);
-      const float inv = l > 0.f ? c / l : 0.f;
-      float v[DH];
-#pragma unroll
-      for (int d = 0; d < DH; ++d) v[d] = o[d] * inv;
-      uint4* dst = reinterpret_cast<uint4*>(O + (int64_t)(s0 + i_q) * H * DH + h * DH);
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        uint32_t w[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          __nv_bfloat162 hb = __floats2bfloat162_rn(v[q * 8 + 2 * e], v[q * 8 + 2 * e + 1]);
-          w[e] = *reinterpret_cast<uint32_t*>(&hb);
-        }
-        dst[q] = make_uint4(w[0], w[1], w[2], w[3]);
-      }
+    if (failed && lane == 0) {
+      record_err(err, 18);
+      abort_sh = 1;
     }
   }
 
@@ -339,10 +412,13 @@ cudaError_t attn_tc(const bf16* qkv, const int32_t* cu, const int32_t* kv_lens, 
   if (!make_map_bf16(&mq, qkv, cols, T, cols * 2, DH, QT) ||
       !make_map_bf16(&mkv, qkv, cols, T, cols * 2, DH, KT))
     return cudaErrorInvalidValue;
-  dim3 grid(n_tiles, H, 1);
-  if (!tiles) grid = dim3((max_seqlen + QT - 1) / QT, H, B);
-  if (grid.x == 0 || grid.z == 0) return cudaSuccess;
-  attn_tc_kernel<<<grid, kThreads, SMEM_BYTES, st>>>(mq, mkv, cu, kv_lens, O, H, window, tiles, err);
+  const int nqt = tiles ? 0 : (max_seqlen + QT - 1) / QT;
+  const long long items = tiles ? (long long)n_tiles * H : (long long)B * nqt * H;
+  if (items <= 0) return cudaSuccess;
+  if (items > 0x7fffffff) return cudaErrorInvalidValue;
+  const int grid = (int)std::min<long long>(items, 2LL * sm_count());
+  attn_tc_kernel<<<grid, kThreads, SMEM_BYTES, st>>>(mq, mkv, cu, kv_lens, O, H, window, tiles,
+                                                      (int)items, nqt, err);
   return cudaGetLastError();
 }
 

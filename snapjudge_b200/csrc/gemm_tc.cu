@@ -4,13 +4,14 @@
 // checkpoint layout (both K-major), fp32 accumulation in TMEM — the
 // contraction of the reference gemm_nt / gemm_geglu (src/tensor.cpp:108-151).
 //
-// CTA (192 threads, one per SM, persistent over output tiles of 128 x BN):
+// CTA (320 threads, one per SM, persistent over output tiles of 128 x BN):
 //   warp 0      TMA producer: A 128x64 and W BNx64 boxes, 128-byte swizzle,
 //               STAGES-deep ring of shared-memory stages (full/empty mbarriers)
 //   warp 1      TMEM owner + MMA issuer: 4 x tcgen05.mma (K = 16) per stage
 //               into one of two TMEM accumulators (2 x BN fp32 columns)
-//   warps 2-5   epilogue: tcgen05.ld of the accumulator (warp w reads TMEM
-//               lanes 32*(w%4)..+31 = tile rows), then one of
+//   warps 2-9   epilogue: tcgen05.ld of the accumulator (warp w reads TMEM
+//               lanes 32*(w%4)..+31 = tile rows; warps 2-5 take the first half
+//               of the tile's columns, warps 6-9 the second), then one of
 //                 STORE  C = bf16(acc + bias, act)           (act: GELU-erf / ReLU)
 //                 RESID  X += acc                            (fp32 residual stream)
 //                 GEGLU  G = bf16(gelu(acc_g) * acc_u)        (W tile = 128 gate rows
@@ -34,7 +35,8 @@ namespace {
 using namespace tc;
 
 constexpr int BM = 128, BK = 64;
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 
 struct EpiArgs {
   const float* bias;
@@ -106,7 +108,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull_bar[b], 1);
-      mbar_init(&tempty_bar[b], 4);
+      mbar_init(&tempty_bar[b], kEpiWarps);
     }
     mbar_init(&drain_bar, 1);
     abort_sh = 0;
@@ -189,7 +191,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!mbar_wait(&drain_bar, 0)) record_err(ep.err, 5);
   } else if (warp >= 2) {
     // ---------------- epilogue ----------------
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int q = warp & 3;             // TMEM lane quarter this warp may access
+    const int hf = (warp - 2) >> 2;     // which half of the tile's columns
     int local = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
       const int b = local & 1;
@@ -208,10 +211,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t tacc = tmem_base + ((uint32_t)(q * 32) << 16) + b * BN;
       uint32_t r0[32], r1[32];
       if (EPI == TC_GEGLU) {
-        constexpr int HALF = BN / 2;
+        constexpr int HALF = BN / 2;    // output columns of the tile
         const int col_base = nb * HALF;
 #pragma unroll 1
-        for (int c = 0; c < HALF; c += 32) {
+        for (int c = hf * HALF / 2; c < (hf + 1) * HALF / 2; c += 32) {
           tmem_ld32(tacc + c, r0);
           tmem_ld32(tacc + HALF + c, r1);
           tmem_ld_wait();
@@ -222,30 +225,38 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (live) store_bf16x32(ep.C + (int64_t)row * ep.ldc + col_base + c, v);
         }
       } else if (EPI == TC_ROPE) {
+        constexpr int HEADS = BN / 64;
         const int col_base = nb * BN;
-        const int p = live ? ep.pos[row] : 0;
+        const int h0 = hf * ((HEADS + 1) / 2), h1 = min(HEADS, (hf + 1) * ((HEADS + 1) / 2));
+        // this row's cos/sin (32 each), loaded once per tile with 16-byte loads
+        float cs[32], sn[32];
+        if (live && col_base + h0 * 64 < ep.rope_cols && h0 < h1) {
+          const int p = ep.pos[row];
+          const float4* c4 = reinterpret_cast<const float4*>(ep.cos_t + (int64_t)p * 32);
+          const float4* s4 = reinterpret_cast<const float4*>(ep.sin_t + (int64_t)p * 32);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const float4 a = __ldg(c4 + k), z = __ldg(s4 + k);
+            cs[4 * k] = a.x; cs[4 * k + 1] = a.y; cs[4 * k + 2] = a.z; cs[4 * k + 3] = a.w;
+            sn[4 * k] = z.x; sn[4 * k + 1] = z.y; sn[4 * k + 2] = z.z; sn[4 * k + 3] = z.w;
+          }
+        } else {
+#pragma unroll
+          for (int k = 0; k < 32; ++k) { cs[k] = 1.f; sn[k] = 0.f; }
+        }
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 64) {
+        for (int hh = h0; hh < h1; ++hh) {
+          const int c = hh * 64;
           tmem_ld32(tacc + c, r0);
           tmem_ld32(tacc + c + 32, r1);
           tmem_ld_wait();
           float v[64];
-          if (col_base + c < ep.rope_cols) {
-            const float* cs = ep.cos_t + (int64_t)p * 32;
-            const float* sn = ep.sin_t + (int64_t)p * 32;
+          const bool rot = col_base + c < ep.rope_cols;
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const float x0 = __uint_as_float(r0[j]), x1 = __uint_as_float(r1[j]);
-              const float cj = live ? cs[j] : 0.f, sj = live ? sn[j] : 0.f;
-              v[j] = x0 * cj - x1 * sj;
-              v[32 + j] = x1 * cj + x0 * sj;
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              v[j] = __uint_as_float(r0[j]);
-              v[32 + j] = __uint_as_float(r1[j]);
-            }
+          for (int j = 0; j < 32; ++j) {
+            const float x0 = __uint_as_float(r0[j]), x1 = __uint_as_float(r1[j]);
+            v[j] = rot ? x0 * cs[j] - x1 * sn[j] : x0;
+            v[32 + j] = rot ? x1 * cs[j] + x0 * sn[j] : x1;
           }
           if (live) {
             store_bf16x32(ep.C + (int64_t)row * ep.ldc + col_base + c, v);
@@ -255,22 +266,32 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else {
         const int col_base = nb * BN;
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
-          tmem_ld32(tacc + c, r0);
-          tmem_ld_wait();
-          if (!live) continue;
+        for (int c = hf * BN / 2; c < (hf + 1) * BN / 2; c += 32) {
           if (EPI == TC_RESID) {
+            // issue the residual loads first so they overlap the TMEM load
             float4* x = reinterpret_cast<float4*>(ep.resid + (int64_t)row * ep.ldr + col_base + c);
+            float4 xv[8];
+            if (live) {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              float4 o = x[j];
-              o.x += __uint_as_float(r0[4 * j]);
-              o.y += __uint_as_float(r0[4 * j + 1]);
-              o.z += __uint_as_float(r0[4 * j + 2]);
-              o.w += __uint_as_float(r0[4 * j + 3]);
-              x[j] = o;
+              for (int j = 0; j < 8; ++j) xv[j] = x[j];
+            }
+            tmem_ld32(tacc + c, r0);
+            tmem_ld_wait();
+            if (live) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                float4 o = xv[j];
+                o.x += __uint_as_float(r0[4 * j]);
+                o.y += __uint_as_float(r0[4 * j + 1]);
+                o.z += __uint_as_float(r0[4 * j + 2]);
+                o.w += __uint_as_float(r0[4 * j + 3]);
+                x[j] = o;
+              }
             }
           } else {
+            tmem_ld32(tacc + c, r0);
+            tmem_ld_wait();
+            if (!live) continue;
             float v[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
