@@ -4,22 +4,23 @@
 // segment b attends keys j in [max(0, i - w), min(kv_len, i + w + 1))
 // (w = 0: all j < kv_len), scale 1/sqrt(64), max-subtracted softmax.  bf16
 // q/k/v/o, fp32 scores and accumulation; P is rounded to bf16 for the P.V MMA
-// and the row normaliser is summed from the rounded P.
+// (the row normaliser sums the fp32 probabilities).
 //
 // Persistent: 2 CTAs per SM walk a strided list of work items (128 queries of
 // one segment x one head), longest segments first.  192 threads per CTA:
 //   warps 0-3  softmax: thread = query row = TMEM lane; online softmax in
-//              registers; P (bf16) written to 128-byte-swizzled shared memory;
-//              the output accumulator o[64] lives in registers
-//   warp 4     TMA producer: Q of each item, then its K/V tiles of 64 keys
+//              registers; P (bf16) written to 128-byte-swizzled shared memory
+//              once O_{j-1} has been folded (one P buffer); the output
+//              accumulator o[64] lives in registers
+//   warp 4     TMA producer: Q of each item (2 buffers, so the next item's Q
+//              loads during the current one), then its K/V tiles of 64 keys
 //              through a 3-stage ring that runs on across items
 //   warp 5     MMA issuer: S_j = Q K_j^T into TMEM S[g%2] (M=128, N=64, K=64),
 //              O_j = P_j V_j into TMEM O[g%2] (V is the MN-major operand);
 //              g counts key tiles across items, so every buffer's phase runs
 //              on across items as well
 // The softmax warps fold O_{j-1} into o[] while the tensor core computes
-// S_{j+1} and O_j.  Q is reloaded for the next item as soon as the last S MMA
-// of the current one has been issued.  Keys past kv_len and outside the window
+// S_{j+1} and O_j.  Keys past kv_len and outside the window
 // are masked with -inf (tiles wholly inside skip the mask); key tiles wholly
 // outside the window are skipped.  All mbarrier waits are bounded (error code,
 // no trap).
@@ -45,7 +46,7 @@ constexpr int kThreads = 192;
 constexpr int Q_BYTES = QT * DH * 2;       // 16 KB
 constexpr int KV_BYTES = KT * DH * 2;      // 8 KB each for K and V
 constexpr int P_BYTES = QT * KT * 2;       // 16 KB
-constexpr int SMEM_BYTES = Q_BYTES + STAGES * 2 * KV_BYTES + 2 * P_BYTES + 1024;
+constexpr int SMEM_BYTES = 2 * Q_BYTES + STAGES * 2 * KV_BYTES + P_BYTES + 1024;
 constexpr uint32_t TMEM_COLS = 256;        // S[2] x 64 + O[2] x 64
 constexpr uint32_t IDESC_S = idesc_bf16(QT, KT, false, false);
 constexpr uint32_t IDESC_O = idesc_bf16(QT, DH, false, true);
@@ -100,20 +101,22 @@ __global__ void __launch_bounds__(kThreads, 2)
                    bf16* __restrict__ O, int H, int window, const int2* __restrict__ tiles,
                    int n_items, int nqt, int* err) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t q_full, q_empty, kv_full[STAGES], kv_empty[STAGES], s_full[2], s_empty[2],
-      p_full[2], o_full[2], o_empty[2], drain;
+  __shared__ uint64_t q_full[2], q_empty[2], kv_full[STAGES], kv_empty[STAGES], s_full[2],
+      s_empty[2], p_full[2], o_full[2], o_empty[2], drain;
   __shared__ uint32_t tmem_sh;
   __shared__ volatile int abort_sh;
 
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-  uint8_t* sQ = smem;
-  uint8_t* sKV = smem + Q_BYTES;                        // stage s: K at s*2*KV, V at +KV
-  uint8_t* sP = smem + Q_BYTES + STAGES * 2 * KV_BYTES;  // P[2]
+  uint8_t* sQ = smem;                                        // Q[2]
+  uint8_t* sKV = smem + 2 * Q_BYTES;                         // stage s: K at s*2*KV, V at +KV
+  uint8_t* sP = smem + 2 * Q_BYTES + STAGES * 2 * KV_BYTES;  // P
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    mbar_init(&q_full, 1);
-    mbar_init(&q_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+    }
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
@@ -146,13 +149,14 @@ __global__ void __launch_bounds__(kThreads, 2)
       for (int w = blockIdx.x; w < n_items && !abort_sh; w += gridDim.x) {
         Item it;
         if (!decode(w, tiles, H, nqt, cu, kv_lens, window, it) || it.n_kv == 0) continue;
-        if (!mbar_wait(&q_empty, (qi & 1) ^ 1)) {
+        const int qb = qi & 1;
+        if (!mbar_wait(&q_empty[qb], ((qi >> 1) & 1) ^ 1)) {
           record_err(err, 10);
           abort_sh = 1;
           break;
         }
-        mbar_expect_tx(&q_full, Q_BYTES);
-        tma_load_2d(sQ, &mapQ, &q_full, it.h * DH, it.s0 + it.q0);
+        mbar_expect_tx(&q_full[qb], Q_BYTES);
+        tma_load_2d(sQ + qb * Q_BYTES, &mapQ, &q_full[qb], it.h * DH, it.s0 + it.q0);
         ++qi;
         for (int j = 0; j < it.n_kv; ++j) {
           if (!mbar_wait(&kv_empty[stage], phase ^ 1)) {
@@ -170,7 +174,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
       }
       // drain: every issued copy has landed before the CTA can exit
-      if (qi > 0 && !mbar_wait(&q_full, (qi - 1) & 1)) record_err(err, 12);
+      for (uint32_t k = qi > 2 ? qi - 2 : 0; k < qi; ++k)
+        if (!mbar_wait(&q_full[k & 1], (k >> 1) & 1)) record_err(err, 12);
       for (int i = 0; i < STAGES && i < issued; ++i) {
         if (--stage < 0) { stage = STAGES - 1; phase ^= 1; }
         if (!mbar_wait(&kv_full[stage], phase)) record_err(err, 13);
@@ -179,18 +184,19 @@ __global__ void __launch_bounds__(kThreads, 2)
   } else if (warp == 5) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
-      const uint32_t q_addr = smem_u32(sQ);
       int stage = 0;
       uint32_t phase = 0, qi = 0, g = 0;
       bool ok = true;
       for (int w = blockIdx.x; w < n_items && ok && !abort_sh; w += gridDim.x) {
         Item it;
         if (!decode(w, tiles, H, nqt, cu, kv_lens, window, it) || it.n_kv == 0) continue;
-        if (!mbar_wait(&q_full, qi & 1)) {
+        const int qb = qi & 1;
+        if (!mbar_wait(&q_full[qb], (qi >> 1) & 1)) {
           record_err(err, 14);
           abort_sh = 1;
           break;
         }
+        const uint32_t q_addr = smem_u32(sQ + qb * Q_BYTES);
         int prev_stage = 0;
         for (int j = 0; j <= it.n_kv; ++j) {
           if (j < it.n_kv) {
@@ -209,7 +215,7 @@ __global__ void __launch_bounds__(kThreads, 2)
               mma_bf16(tS + (gj & 1) * KT, desc_kmajor_sw128(q_addr + kk * 32),
                        desc_kmajor_sw128(k_addr + kk * 32), IDESC_S, kk != 0);
             mma_commit(&s_full[gj & 1]);
-            if (j == it.n_kv - 1) mma_commit(&q_empty);  // Q is free once its last S is done
+            if (j == it.n_kv - 1) mma_commit(&q_empty[qb]);  // Q free once its last S is done
           }
           if (j >= 1) {
             const uint32_t i = g + j - 1;
@@ -221,7 +227,7 @@ __global__ void __launch_bounds__(kThreads, 2)
               break;
             }
             fence_after_sync();
-            const uint32_t p_addr = smem_u32(sP + (i & 1) * P_BYTES);
+            const uint32_t p_addr = smem_u32(sP);
             const uint32_t v_addr = smem_u32(sKV + prev_stage * 2 * KV_BYTES + KV_BYTES);
 #pragma unroll
             for (int kk = 0; kk < KT / 16; ++kk)
@@ -308,54 +314,49 @@ __global__ void __launch_bounds__(kThreads, 2)
         __syncwarp();
         if (lane == 0) mbar_arrive(&s_empty[gj & 1]);
         const int kbase = (it.t_lo + j) * KT;
-        // scores in place: ra/rb hold the S row (keys kbase..+63) as fp32 bits
+        // raw scores stay in ra/rb; masked keys become -inf
         float tmax = -INFINITY;
         if (window == 0 && kbase + KT <= it.nk) {  // interior tile: every key visible
 #pragma unroll
-          for (int c = 0; c < KT; ++c) {
-            uint32_t& cell = c < 32 ? ra[c] : rb[c - 32];
-            const float v = __uint_as_float(cell) * scale;
-            cell = __float_as_uint(v);
-            tmax = fmaxf(tmax, v);
-          }
+          for (int c = 0; c < KT; ++c) tmax = fmaxf(tmax, __uint_as_float(c < 32 ? ra[c] : rb[c - 32]));
         } else {
 #pragma unroll
           for (int c = 0; c < KT; ++c) {
             const int key = kbase + c;
             uint32_t& cell = c < 32 ? ra[c] : rb[c - 32];
-            const float v = (key >= lo && key < hi) ? __uint_as_float(cell) * scale : -INFINITY;
+            const float v = (key >= lo && key < hi) ? __uint_as_float(cell) : -INFINITY;
             cell = __float_as_uint(v);
             tmax = fmaxf(tmax, v);
           }
         }
-        const float m_new = fmaxf(m, tmax);
+        // running max in log2 units: m = max(m, tmax / sqrt(Dh) * log2 e)
+        const float m_new = fmaxf(m, tmax * scale);
         const float m_use = m_new == -INFINITY ? 0.f : m_new;
         const float corr = m == -INFINITY ? 0.f : ex2(m - m_use);
+        // P_j = 2^(s * scale - m_use) packed to bf16 pairs; fp32 row sum
         float rs = 0.f;
-        // P_j = 2^(s - m_new) -> bf16, written in the 128-byte-swizzled K-major layout
-        uint8_t* prow = sP + (gj & 1) * P_BYTES + r * 128;
+        uint32_t pk[KT / 2];
 #pragma unroll
-        for (int ch = 0; ch < KT / 8; ++ch) {
-          uint32_t wv[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int c0 = ch * 8 + 2 * e;
-            const float p0 = ex2(__uint_as_float(c0 < 32 ? ra[c0] : rb[c0 - 32]) - m_use);
-            const float p1 = ex2(__uint_as_float(c0 + 1 < 32 ? ra[c0 + 1] : rb[c0 - 31]) - m_use);
-            __nv_bfloat162 pb = __floats2bfloat162_rn(p0, p1);
-            const float2 pr = __bfloat1622float2(pb);
-            rs += pr.x + pr.y;  // normaliser from the rounded P the MMA sees
-            wv[e] = *reinterpret_cast<uint32_t*>(&pb);
-          }
-          *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) =
-              make_uint4(wv[0], wv[1], wv[2], wv[3]);
+        for (int c = 0; c < KT; c += 2) {
+          const float p0 = ex2(fmaf(__uint_as_float(c < 32 ? ra[c] : rb[c - 32]), scale, -m_use));
+          const float p1 =
+              ex2(fmaf(__uint_as_float(c + 1 < 32 ? ra[c + 1] : rb[c - 31]), scale, -m_use));
+          rs += p0 + p1;
+          __nv_bfloat162 pb = __floats2bfloat162_rn(p0, p1);
+          pk[c / 2] = *reinterpret_cast<uint32_t*>(&pb);
         }
         l = l * corr + rs;
         m = m_new;
+        // O_{j-1} first: its completion also frees the single P buffer
+        if (j >= 1 && !fold(gj - 1, m_prev_tile)) { failed = true; break; }
+        uint8_t* prow = sP + r * 128;  // 128-byte-swizzled K-major row
+#pragma unroll
+        for (int ch = 0; ch < KT / 8; ++ch)
+          *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) =
+              make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // P visible to the MMA
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[gj & 1]);
-        if (j >= 1 && !fold(gj - 1, m_prev_tile)) { failed = true; break; }
         m_prev_tile = m_use;
       }
       if (failed || !fold(g + it.n_kv - 1, m_prev_tile)) { failed = true; break; }

@@ -263,44 +263,53 @@ __global__ void __launch_bounds__(kThreads, 1)
             store_bf16x32(ep.C + (int64_t)row * ep.ldc + col_base + c + 32, v + 32);
           }
         }
+      } else if (EPI == TC_RESID) {
+        // X += acc, software-pipelined: the next chunk's residual loads are in
+        // flight while the current chunk is added and stored
+        constexpr int NCH = BN / 64;  // 32-column chunks in this warp's half
+        const int c0 = hf * BN / 2;
+        float* xrow = ep.resid + (int64_t)row * ep.ldr + nb * BN + c0;
+        float4 xv[2][8];
+        if (live) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) xv[0][j] = reinterpret_cast<const float4*>(xrow)[j];
+        }
+#pragma unroll
+        for (int k = 0; k < NCH; ++k) {
+          if (k + 1 < NCH && live) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              xv[(k + 1) & 1][j] = reinterpret_cast<const float4*>(xrow + 32 * (k + 1))[j];
+          }
+          tmem_ld32(tacc + c0 + 32 * k, r0);
+          tmem_ld_wait();
+          if (live) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              float4 o = xv[k & 1][j];
+              o.x += __uint_as_float(r0[4 * j]);
+              o.y += __uint_as_float(r0[4 * j + 1]);
+              o.z += __uint_as_float(r0[4 * j + 2]);
+              o.w += __uint_as_float(r0[4 * j + 3]);
+              reinterpret_cast<float4*>(xrow + 32 * k)[j] = o;
+            }
+          }
+        }
       } else {
         const int col_base = nb * BN;
 #pragma unroll 1
         for (int c = hf * BN / 2; c < (hf + 1) * BN / 2; c += 32) {
-          if (EPI == TC_RESID) {
-            // issue the residual loads first so they overlap the TMEM load
-            float4* x = reinterpret_cast<float4*>(ep.resid + (int64_t)row * ep.ldr + col_base + c);
-            float4 xv[8];
-            if (live) {
+          tmem_ld32(tacc + c, r0);
+          tmem_ld_wait();
+          if (!live) continue;
+          float v[32];
 #pragma unroll
-              for (int j = 0; j < 8; ++j) xv[j] = x[j];
-            }
-            tmem_ld32(tacc + c, r0);
-            tmem_ld_wait();
-            if (live) {
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                float4 o = xv[j];
-                o.x += __uint_as_float(r0[4 * j]);
-                o.y += __uint_as_float(r0[4 * j + 1]);
-                o.z += __uint_as_float(r0[4 * j + 2]);
-                o.w += __uint_as_float(r0[4 * j + 3]);
-                x[j] = o;
-              }
-            }
-          } else {
-            tmem_ld32(tacc + c, r0);
-            tmem_ld_wait();
-            if (!live) continue;
-            float v[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              float a = __uint_as_float(r0[j]);
-              if (ep.bias) a += ep.bias[col_base + c + j];
-              v[j] = act_fn(a, ep.act);
-            }
-            store_bf16x32(ep.C + (int64_t)row * ep.ldc + col_base + c, v);
+          for (int j = 0; j < 32; ++j) {
+            float a = __uint_as_float(r0[j]);
+            if (ep.bias) a += ep.bias[col_base + c + j];
+            v[j] = act_fn(a, ep.act);
           }
+          store_bf16x32(ep.C + (int64_t)row * ep.ldc + col_base + c, v);
         }
       }
       fence_before_sync();
