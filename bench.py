@@ -345,23 +345,36 @@ def main():
             torch.bfloat16)
         fl = float(sum(4 * int(n) ** 2 * Dh2 * H2 for n in lens2))
         flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # > L2 (126 MB)
-        reps, ams = 20, 0.0
-        with torch.cuda.stream(st):
-            for _ in range(5):
-                ops.attn(qkv, cu2, H2, Dh2)
-            for _ in range(reps):
-                flush.zero_()
-                a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                a0.record(st)
-                ops.attn(qkv, cu2, H2, Dh2)
-                a1.record(st)
-                a1.synchronize()
-                ams += a0.elapsed_time(a1) / reps
+
+        def time_attn(x, cu_x, reps=20):
+            out = 0.0
+            with torch.cuda.stream(st):
+                for _ in range(5):
+                    ops.attn(x, cu_x, H2, Dh2)
+                for _ in range(reps):
+                    flush.zero_()
+                    a0 = torch.cuda.Event(enable_timing=True)
+                    a1 = torch.cuda.Event(enable_timing=True)
+                    a0.record(st)
+                    ops.attn(x, cu_x, H2, Dh2)
+                    a1.record(st)
+                    a1.synchronize()
+                    out += a0.elapsed_time(a1) / reps
+            return out
+
+        ams = time_attn(qkv, cu2)
+        # fixed-length variant: 64 sequences of exactly 512 tokens
+        cu512 = synth.cu_seqlens(np.full(64, 512))
+        qkv512 = torch.randn(int(cu512[-1]), 3 * H2 * Dh2, device=dev).to(torch.bfloat16)
+        ams512 = time_attn(qkv512, cu512)
+        fl512 = 64 * 4.0 * 512 * 512 * Dh2 * H2
         burst = pk.get("bf16_tflops", FALLBACK["bf16_tflops"])
         line["attention"] = {"config": "c2: 64 seqs x 12 heads x 64, lengths U[32,512], bf16",
                              "ms": ams, "tflops": fl / (ams / 1e3) / 1e12,
                              "frac_of_peak": fl / (ams / 1e3) / 1e12 / burst,
                              "peak": burst, "peak_kind": f"{pk_kind} burst bf16",
+                             "n512": {"ms": ams512, "tflops": fl512 / (ams512 / 1e3) / 1e12,
+                                      "frac_of_peak": fl512 / (ams512 / 1e3) / 1e12 / burst},
                              "l2": "L2 flushed (256 MB write) before every timed launch"}
         if world == 1 and not a.no_cpu_baseline:
             tok, sec, n, kind, cores = reference_sample(spec, weights, a.cpu_seconds, 8, 4096,

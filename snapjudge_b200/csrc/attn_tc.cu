@@ -8,22 +8,25 @@
 //
 // Persistent: 2 CTAs per SM walk a strided list of work items (128 queries of
 // one segment x one head), longest segments first.  192 threads per CTA:
-//   warps 0-3  softmax: thread = query row = TMEM lane; online softmax in
-//              registers; P (bf16) written to 128-byte-swizzled shared memory
-//              once O_{j-1} has been folded (one P buffer); the output
-//              accumulator o[64] lives in registers
-//   warp 4     TMA producer: Q of each item (2 buffers, so the next item's Q
-//              loads during the current one), then its K/V tiles of 64 keys
-//              through a 3-stage ring that runs on across items
-//   warp 5     MMA issuer: S_j = Q K_j^T into TMEM S[g%2] (M=128, N=64, K=64),
-//              O_j = P_j V_j into TMEM O[g%2] (V is the MN-major operand);
-//              g counts key tiles across items, so every buffer's phase runs
-//              on across items as well
-// The softmax warps fold O_{j-1} into o[] while the tensor core computes
-// S_{j+1} and O_j.  Keys past kv_len and outside the window
-// are masked with -inf (tiles wholly inside skip the mask); key tiles wholly
-// outside the window are skipped.  All mbarrier waits are bounded (error code,
-// no trap).
+//   warps 0-3  softmax: thread = query row = TMEM lane.  Reads S_j from TMEM,
+//              writes P_j (bf16) back to TMEM and moves on: the output is
+//              accumulated in TMEM by the tensor core, so the softmax never
+//              waits for a P.V product except to rescale it (below) and at the
+//              end of an item
+//   warp 4     TMA producer: Q of each item (2 buffers), then its K/V tiles of
+//              64 keys through a 4-stage ring that runs on across items
+//   warp 5     MMA issuer: S_j = Q K_j^T into TMEM S[g%2] (M=128, N=64, K=64,
+//              both operands in shared memory); O += P_j V_j with P_j read from
+//              TMEM (the A operand) and V from shared memory (MN-major); g
+//              counts key tiles across items, so every phase runs on across items
+// Rescaling: each row keeps a reference max m_ref for its exponentials and
+// moves it only when a tile's max exceeds it by more than 2^8 (exponent 8 in
+// log2 units); then the row's O (in TMEM) and running sum are multiplied by
+// 2^(m_ref_old - m_ref_new) before the next P.V accumulates.  The result is the
+// same softmax (every term uses the same reference), with P <= 2^8.
+// Keys past kv_len and outside the window are masked with -inf (interior tiles
+// skip the mask); key tiles wholly outside the window are skipped.  All mbarrier
+// waits are bounded (error code, no trap).
 #include <algorithm>
 
 #include "common.cuh"
@@ -41,13 +44,15 @@ using namespace tc;
 constexpr int QT = 128;        // queries per work item
 constexpr int KT = 64;         // keys per tile
 constexpr int DH = 64;
-constexpr int STAGES = 3;
+constexpr int STAGES = 4;
 constexpr int kThreads = 192;
 constexpr int Q_BYTES = QT * DH * 2;       // 16 KB
 constexpr int KV_BYTES = KT * DH * 2;      // 8 KB each for K and V
-constexpr int P_BYTES = QT * KT * 2;       // 16 KB
-constexpr int SMEM_BYTES = 2 * Q_BYTES + STAGES * 2 * KV_BYTES + P_BYTES + 1024;
-constexpr uint32_t TMEM_COLS = 256;        // S[2] x 64 + O[2] x 64
+constexpr int SMEM_BYTES = 2 * Q_BYTES + STAGES * 2 * KV_BYTES + 1024;
+// TMEM columns: S[2] (fp32 64 each) | O (fp32 64) | P[2] (bf16 pairs, 32 each)
+constexpr uint32_t TMEM_COLS = 256;
+constexpr uint32_t COL_S = 0, COL_O = 2 * KT, COL_P = 2 * KT + DH;
+constexpr float kRescaleLog2 = 8.f;  // move the reference max when exceeded by 2^8
 constexpr uint32_t IDESC_S = idesc_bf16(QT, KT, false, false);
 constexpr uint32_t IDESC_O = idesc_bf16(QT, DH, false, true);
 
@@ -102,31 +107,27 @@ __global__ void __launch_bounds__(kThreads, 2)
                    int n_items, int nqt, int* err) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t q_full[2], q_empty[2], kv_full[STAGES], kv_empty[STAGES], s_full[2],
-      s_empty[2], p_full[2], o_full[2], o_empty[2], drain;
+      s_empty[2], p_full[2], pv_done[2], drain;
   __shared__ uint32_t tmem_sh;
   __shared__ volatile int abort_sh;
 
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-  uint8_t* sQ = smem;                                        // Q[2]
-  uint8_t* sKV = smem + 2 * Q_BYTES;                         // stage s: K at s*2*KV, V at +KV
-  uint8_t* sP = smem + 2 * Q_BYTES + STAGES * 2 * KV_BYTES;  // P
+  uint8_t* sQ = smem;                 // Q[2]
+  uint8_t* sKV = smem + 2 * Q_BYTES;  // stage s: K at s*2*KV, V at +KV
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(&q_full[i], 1);
       mbar_init(&q_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 4);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&pv_done[i], 1);
     }
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
-    }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 4);
-      mbar_init(&p_full[i], 4);
-      mbar_init(&o_full[i], 1);
-      mbar_init(&o_empty[i], 4);
     }
     mbar_init(&drain, 1);
     abort_sh = 0;
@@ -137,7 +138,6 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   fence_after_sync();
   const uint32_t tmem = tmem_sh;
-  const uint32_t tS = tmem, tO = tmem + 2 * KT;  // S[i] at tS + i*64, O[i] at tO + i*64
 
   if (warp == 4) {
     if (lane == 0) {
@@ -212,28 +212,27 @@ __global__ void __launch_bounds__(kThreads, 2)
             const uint32_t k_addr = smem_u32(sKV + stage * 2 * KV_BYTES);
 #pragma unroll
             for (int kk = 0; kk < DH / 16; ++kk)
-              mma_bf16(tS + (gj & 1) * KT, desc_kmajor_sw128(q_addr + kk * 32),
+              mma_bf16(tmem + COL_S + (gj & 1) * KT, desc_kmajor_sw128(q_addr + kk * 32),
                        desc_kmajor_sw128(k_addr + kk * 32), IDESC_S, kk != 0);
             mma_commit(&s_full[gj & 1]);
             if (j == it.n_kv - 1) mma_commit(&q_empty[qb]);  // Q free once its last S is done
           }
           if (j >= 1) {
             const uint32_t i = g + j - 1;
-            if (!mbar_wait(&p_full[i & 1], (i >> 1) & 1) ||
-                !mbar_wait(&o_empty[i & 1], ((i >> 1) & 1) ^ 1)) {
+            if (!mbar_wait(&p_full[i & 1], (i >> 1) & 1)) {
               record_err(err, 16);
               abort_sh = 1;
               ok = false;
               break;
             }
             fence_after_sync();
-            const uint32_t p_addr = smem_u32(sP);
             const uint32_t v_addr = smem_u32(sKV + prev_stage * 2 * KV_BYTES + KV_BYTES);
 #pragma unroll
             for (int kk = 0; kk < KT / 16; ++kk)
-              mma_bf16(tO + (i & 1) * DH, desc_kmajor_sw128(p_addr + kk * 32),
-                       desc_mnmajor_sw128(v_addr + kk * 16 * 128), IDESC_O, kk != 0);
-            mma_commit(&o_full[i & 1]);
+              mma_bf16_ts(tmem + COL_O, tmem + COL_P + (i & 1) * (KT / 2) + kk * 8,
+                          desc_mnmajor_sw128(v_addr + kk * 16 * 128), IDESC_O,
+                          (j > 1 || kk > 0) ? 1u : 0u);
+            mma_commit(&pv_done[i & 1]);
             mma_commit(&kv_empty[prev_stage]);
           }
           prev_stage = stage;
@@ -250,8 +249,16 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int r = warp * 32 + lane;  // query row in the tile = TMEM lane
     const float scale = 0.125f * 1.4426950408889634f;  // log2(e) / sqrt(64)
     const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const uint32_t tS = tmem + COL_S + lane_off, tO = tmem + COL_O + lane_off,
+                   tP = tmem + COL_P + lane_off;
     uint32_t g = 0;
     bool failed = false;
+    // bounded wait by lane 0, result broadcast to the warp
+    auto warp_wait = [&](uint64_t* bar, uint32_t parity) -> bool {
+      int okw = 1;
+      if (lane == 0) okw = mbar_wait(bar, parity) ? 1 : 0;
+      return __shfl_sync(0xffffffffu, okw, 0) != 0;
+    };
     for (int w = blockIdx.x; w < n_items && !failed && !abort_sh; w += gridDim.x) {
       Item it;
       if (!decode(w, tiles, H, nqt, cu, kv_lens, window, it)) continue;
@@ -268,57 +275,24 @@ __global__ void __launch_bounds__(kThreads, 2)
         lo = max(0, i_q - window);
         hi = min(it.nk, i_q + window + 1);
       }
-      float o[DH];
-#pragma unroll
-      for (int d = 0; d < DH; ++d) o[d] = 0.f;
-      float m = -INFINITY, l = 0.f;
-      float m_prev_tile = -INFINITY;  // running max used for P_{j-1}
-      float m_acc = -INFINITY;        // scale o[] currently refers to
-
-      auto fold = [&](uint32_t i, float m_i) -> bool {
-        // o = o * 2^(m_acc - m_i) + O_i  (O_i was computed against m_i)
-        int okw = 1;
-        if (lane == 0) okw = mbar_wait(&o_full[i & 1], (i >> 1) & 1) ? 1 : 0;
-        okw = __shfl_sync(0xffffffffu, okw, 0);
-        if (!okw) return false;
-        fence_after_sync();
-        uint32_t ra[32], rb[32];
-        tmem_ld32(tO + (i & 1) * DH + lane_off, ra);
-        tmem_ld32(tO + (i & 1) * DH + 32 + lane_off, rb);
-        tmem_ld_wait();
-        const float c = (m_acc == -INFINITY) ? 0.f : ex2(m_acc - m_i);
-#pragma unroll
-        for (int d = 0; d < 32; ++d) {
-          o[d] = o[d] * c + __uint_as_float(ra[d]);
-          o[32 + d] = o[32 + d] * c + __uint_as_float(rb[d]);
-        }
-        m_acc = m_i;
-        fence_before_sync();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&o_empty[i & 1]);
-        return true;
-      };
-
+      float m_ref = -INFINITY, l = 0.f;
       for (int j = 0; j < it.n_kv; ++j) {
         const uint32_t gj = g + j;
-        int okw = 1;
-        if (lane == 0) okw = mbar_wait(&s_full[gj & 1], (gj >> 1) & 1) ? 1 : 0;
-        okw = __shfl_sync(0xffffffffu, okw, 0);
-        if (!okw || abort_sh) { failed = true; break; }
+        if (!warp_wait(&s_full[gj & 1], (gj >> 1) & 1) || abort_sh) { failed = true; break; }
         fence_after_sync();
         uint32_t ra[32], rb[32];
-        tmem_ld32(tS + (gj & 1) * KT + lane_off, ra);
-        tmem_ld32(tS + (gj & 1) * KT + 32 + lane_off, rb);
+        tmem_ld32(tS + (gj & 1) * KT, ra);
+        tmem_ld32(tS + (gj & 1) * KT + 32, rb);
         tmem_ld_wait();
         fence_before_sync();
         __syncwarp();
         if (lane == 0) mbar_arrive(&s_empty[gj & 1]);
         const int kbase = (it.t_lo + j) * KT;
-        // raw scores stay in ra/rb; masked keys become -inf
-        float tmax = -INFINITY;
+        float t4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
         if (window == 0 && kbase + KT <= it.nk) {  // interior tile: every key visible
 #pragma unroll
-          for (int c = 0; c < KT; ++c) tmax = fmaxf(tmax, __uint_as_float(c < 32 ? ra[c] : rb[c - 32]));
+          for (int c = 0; c < KT; ++c)
+            t4[c & 3] = fmaxf(t4[c & 3], __uint_as_float(c < 32 ? ra[c] : rb[c - 32]));
         } else {
 #pragma unroll
           for (int c = 0; c < KT; ++c) {
@@ -326,52 +300,78 @@ __global__ void __launch_bounds__(kThreads, 2)
             uint32_t& cell = c < 32 ? ra[c] : rb[c - 32];
             const float v = (key >= lo && key < hi) ? __uint_as_float(cell) : -INFINITY;
             cell = __float_as_uint(v);
-            tmax = fmaxf(tmax, v);
+            t4[c & 3] = fmaxf(t4[c & 3], v);
           }
         }
-        // running max in log2 units: m = max(m, tmax / sqrt(Dh) * log2 e)
-        const float m_new = fmaxf(m, tmax * scale);
+        const float m_tile = fmaxf(fmaxf(t4[0], t4[1]), fmaxf(t4[2], t4[3])) * scale;
+        // move the reference max on the first visible tile, or when exceeded by 2^8
+        const bool first = m_ref == -INFINITY;
+        const bool grow = !first && m_tile > m_ref + kRescaleLog2;
+        const float m_new = (first || grow) ? m_tile : m_ref;
         const float m_use = m_new == -INFINITY ? 0.f : m_new;
-        const float corr = m == -INFINITY ? 0.f : ex2(m - m_use);
-        // P_j = 2^(s * scale - m_use) packed to bf16 pairs; fp32 row sum
-        float rs = 0.f;
-        uint32_t pk[KT / 2];
+        if (__any_sync(0xffffffffu, grow) && j >= 1) {
+          // O holds P_0..P_{j-1} V against m_ref: rescale this warp's rows
+          if (!warp_wait(&pv_done[(gj - 1) & 1], ((gj - 1) >> 1) & 1)) { failed = true; break; }
+          fence_after_sync();
+          const float c = grow ? ex2(m_ref - m_new) : 1.f;
+          uint32_t oa[32], ob[32];
+          tmem_ld32(tO, oa);
+          tmem_ld32(tO + 32, ob);
+          tmem_ld_wait();
+#pragma unroll
+          for (int d = 0; d < 32; ++d) {
+            oa[d] = __float_as_uint(__uint_as_float(oa[d]) * c);
+            ob[d] = __float_as_uint(__uint_as_float(ob[d]) * c);
+          }
+          tmem_st32(tO, oa);
+          tmem_st32(tO + 32, ob);
+          tmem_st_wait();
+        }
+        if (grow) l *= ex2(m_ref - m_new);
+        m_ref = m_new;
+        // P_j = 2^(s * scale - m_use) as bf16 pairs; fp32 row sum
+        float r4[4] = {0.f, 0.f, 0.f, 0.f};
+        uint32_t pk[32];
 #pragma unroll
         for (int c = 0; c < KT; c += 2) {
           const float p0 = ex2(fmaf(__uint_as_float(c < 32 ? ra[c] : rb[c - 32]), scale, -m_use));
           const float p1 =
               ex2(fmaf(__uint_as_float(c + 1 < 32 ? ra[c + 1] : rb[c - 31]), scale, -m_use));
-          rs += p0 + p1;
+          r4[(c >> 1) & 3] += p0 + p1;
           __nv_bfloat162 pb = __floats2bfloat162_rn(p0, p1);
-          pk[c / 2] = *reinterpret_cast<uint32_t*>(&pb);
+          pk[c >> 1] = *reinterpret_cast<uint32_t*>(&pb);
         }
-        l = l * corr + rs;
-        m = m_new;
-        // O_{j-1} first: its completion also frees the single P buffer
-        if (j >= 1 && !fold(gj - 1, m_prev_tile)) { failed = true; break; }
-        uint8_t* prow = sP + r * 128;  // 128-byte-swizzled K-major row
-#pragma unroll
-        for (int ch = 0; ch < KT / 8; ++ch)
-          *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) =
-              make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // P visible to the MMA
+        l += (r4[0] + r4[1]) + (r4[2] + r4[3]);
+        // P[gj%2] was last read by the P.V of tile gj-2
+        if (!warp_wait(&pv_done[gj & 1], ((gj >> 1) & 1) ^ 1)) { failed = true; break; }
+        tmem_st32(tP + (gj & 1) * (KT / 2), pk);
+        tmem_st_wait();
+        fence_before_sync();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[gj & 1]);
-        m_prev_tile = m_use;
       }
-      if (failed || !fold(g + it.n_kv - 1, m_prev_tile)) { failed = true; break; }
+      if (failed) break;
+      // the item's output: wait for its last P.V, then O / l
+      const uint32_t last = g + it.n_kv - 1;
+      if (!warp_wait(&pv_done[last & 1], (last >> 1) & 1)) { failed = true; break; }
+      fence_after_sync();
+      uint32_t oa[32], ob[32];
+      tmem_ld32(tO, oa);
+      tmem_ld32(tO + 32, ob);
+      tmem_ld_wait();
+      fence_before_sync();
       g += it.n_kv;
       if (live) {
-        // o is relative to m_acc (= the final running max); l to m
-        const float c = (m_acc == -INFINITY || m == -INFINITY) ? 0.f : ex2(m_acc - m);
-        const float inv = l > 0.f ? c / l : 0.f;
+        const float inv = l > 0.f ? 1.f / l : 0.f;
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
           uint32_t wv[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            __nv_bfloat162 hb =
-                __floats2bfloat162_rn(o[q * 8 + 2 * e] * inv, o[q * 8 + 2 * e + 1] * inv);
+            const int d = q * 8 + 2 * e;
+            const float a = __uint_as_float(d < 32 ? oa[d] : ob[d - 32]) * inv;
+            const float b2 = __uint_as_float(d + 1 < 32 ? oa[d + 1] : ob[d - 31]) * inv;
+            __nv_bfloat162 hb = __floats2bfloat162_rn(a, b2);
             wv[e] = *reinterpret_cast<uint32_t*>(&hb);
           }
           reinterpret_cast<uint4*>(orow)[q] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
