@@ -66,6 +66,19 @@ __device__ __forceinline__ float ex2(float x) {  // 2^x on the MUFU (ex2.approx,
   return y;
 }
 
+// (2^a, 2^b) with one MUFU op: pack to f16 pairs, ex2.approx.f16x2, unpack.
+__device__ __forceinline__ float2 ex2_pair(float a, float b) {
+  uint32_t h;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(b), "f"(a));  // low half = a
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(h) : "r"(h));
+  float2 r;
+  asm("{\n\t.reg .f16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
+      "cvt.f32.f16 %0, lo;\n\tcvt.f32.f16 %1, hi;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "r"(h));
+  return r;
+}
+
 struct Item {
   int b, q0, h, s0, n, nk, t_lo, n_kv;
 };
@@ -184,62 +197,83 @@ __global__ void __launch_bounds__(kThreads, 2)
   } else if (warp == 5) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
-      int stage = 0;
-      uint32_t phase = 0, qi = 0, g = 0;
-      bool ok = true;
-      for (int w = blockIdx.x; w < n_items && ok && !abort_sh; w += gridDim.x) {
+      // Two cursors walk the same sequence of key tiles: the S cursor runs
+      // ahead as far as the two S buffers allow (it never waits behind a P.V),
+      // the P.V cursor follows the softmax.  Each pass issues whatever is ready
+      // (non-blocking tests); no progress for kWaitNs is an error.
+      struct Cursor {
+        int w;
         Item it;
-        if (!decode(w, tiles, H, nqt, cu, kv_lens, window, it) || it.n_kv == 0) continue;
-        const int qb = qi & 1;
-        if (!mbar_wait(&q_full[qb], (qi >> 1) & 1)) {
-          record_err(err, 14);
-          abort_sh = 1;
-          break;
+        int j;
+        uint32_t qi, g;
+        int stage;
+        uint32_t phase;
+        bool done;
+      };
+      auto seek = [&](Cursor& c) {  // first item at or after c.w that has key tiles
+        for (; c.w < n_items; c.w += gridDim.x)
+          if (decode(c.w, tiles, H, nqt, cu, kv_lens, window, c.it) && c.it.n_kv > 0) {
+            c.j = 0;
+            return;
+          }
+        c.done = true;
+      };
+      auto advance = [&](Cursor& c) {
+        ++c.g;
+        if (++c.stage == STAGES) { c.stage = 0; c.phase ^= 1; }
+        if (++c.j == c.it.n_kv) {
+          ++c.qi;
+          c.w += gridDim.x;
+          seek(c);
         }
-        const uint32_t q_addr = smem_u32(sQ + qb * Q_BYTES);
-        int prev_stage = 0;
-        for (int j = 0; j <= it.n_kv; ++j) {
-          if (j < it.n_kv) {
-            const uint32_t gj = g + j;
-            if (!mbar_wait(&kv_full[stage], phase) ||
-                !mbar_wait(&s_empty[gj & 1], ((gj >> 1) & 1) ^ 1)) {
-              record_err(err, 15);
-              abort_sh = 1;
-              ok = false;
-              break;
-            }
+      };
+      Cursor cs{(int)blockIdx.x, {}, 0, 0u, 0u, 0, 0u, false};
+      Cursor cp = cs;
+      seek(cs);
+      seek(cp);
+      uint64_t t_last = globaltimer();
+      while (!cp.done && !abort_sh) {
+        bool progressed = false;
+        if (!cs.done) {
+          const int qb = cs.qi & 1;
+          if ((cs.j > 0 || mbar_test(&q_full[qb], (cs.qi >> 1) & 1)) &&
+              mbar_test(&kv_full[cs.stage], cs.phase) &&
+              mbar_test(&s_empty[cs.g & 1], ((cs.g >> 1) & 1) ^ 1)) {
             fence_after_sync();
-            const uint32_t k_addr = smem_u32(sKV + stage * 2 * KV_BYTES);
+            const uint32_t q_addr = smem_u32(sQ + qb * Q_BYTES);
+            const uint32_t k_addr = smem_u32(sKV + cs.stage * 2 * KV_BYTES);
 #pragma unroll
             for (int kk = 0; kk < DH / 16; ++kk)
-              mma_bf16(tmem + COL_S + (gj & 1) * KT, desc_kmajor_sw128(q_addr + kk * 32),
+              mma_bf16(tmem + COL_S + (cs.g & 1) * KT, desc_kmajor_sw128(q_addr + kk * 32),
                        desc_kmajor_sw128(k_addr + kk * 32), IDESC_S, kk != 0);
-            mma_commit(&s_full[gj & 1]);
-            if (j == it.n_kv - 1) mma_commit(&q_empty[qb]);  // Q free once its last S is done
+            mma_commit(&s_full[cs.g & 1]);
+            if (cs.j == cs.it.n_kv - 1) mma_commit(&q_empty[qb]);  // Q free after its last S
+            advance(cs);
+            progressed = true;
           }
-          if (j >= 1) {
-            const uint32_t i = g + j - 1;
-            if (!mbar_wait(&p_full[i & 1], (i >> 1) & 1)) {
-              record_err(err, 16);
-              abort_sh = 1;
-              ok = false;
-              break;
-            }
-            fence_after_sync();
-            const uint32_t v_addr = smem_u32(sKV + prev_stage * 2 * KV_BYTES + KV_BYTES);
-#pragma unroll
-            for (int kk = 0; kk < KT / 16; ++kk)
-              mma_bf16_ts(tmem + COL_O, tmem + COL_P + (i & 1) * (KT / 2) + kk * 8,
-                          desc_mnmajor_sw128(v_addr + kk * 16 * 128), IDESC_O,
-                          (j > 1 || kk > 0) ? 1u : 0u);
-            mma_commit(&pv_done[i & 1]);
-            mma_commit(&kv_empty[prev_stage]);
-          }
-          prev_stage = stage;
-          if (j < it.n_kv && ++stage == STAGES) { stage = 0; phase ^= 1; }
         }
-        g += it.n_kv;
-        ++qi;
+        if (mbar_test(&p_full[cp.g & 1], (cp.g >> 1) & 1)) {
+          fence_after_sync();
+          const uint32_t v_addr = smem_u32(sKV + cp.stage * 2 * KV_BYTES + KV_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < KT / 16; ++kk)
+            mma_bf16_ts(tmem + COL_O, tmem + COL_P + (cp.g & 1) * (KT / 2) + kk * 8,
+                        desc_mnmajor_sw128(v_addr + kk * 16 * 128), IDESC_O,
+                        (cp.j > 0 || kk > 0) ? 1u : 0u);
+          mma_commit(&pv_done[cp.g & 1]);
+          mma_commit(&kv_empty[cp.stage]);
+          advance(cp);
+          progressed = true;
+        }
+        if (progressed) {
+          t_last = globaltimer();
+        } else if (globaltimer() - t_last > kWaitNs) {
+          record_err(err, 15);
+          abort_sh = 1;
+          break;
+        } else {
+          __nanosleep(20);
+        }
       }
       mma_commit(&drain);
       if (!mbar_wait(&drain, 0)) record_err(err, 17);
@@ -329,16 +363,18 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         if (grow) l *= ex2(m_ref - m_new);
         m_ref = m_new;
-        // P_j = 2^(s * scale - m_use) as bf16 pairs; fp32 row sum
+        // P_j = 2^(s * scale - m_use), two exponentials per MUFU op (ex2 on
+        // f16 pairs: arguments <= 8, results <= 256; P is rounded to bf16
+        // afterwards, below f16's precision); fp32 row sum
         float r4[4] = {0.f, 0.f, 0.f, 0.f};
         uint32_t pk[32];
 #pragma unroll
         for (int c = 0; c < KT; c += 2) {
-          const float p0 = ex2(fmaf(__uint_as_float(c < 32 ? ra[c] : rb[c - 32]), scale, -m_use));
-          const float p1 =
-              ex2(fmaf(__uint_as_float(c + 1 < 32 ? ra[c + 1] : rb[c - 31]), scale, -m_use));
-          r4[(c >> 1) & 3] += p0 + p1;
-          __nv_bfloat162 pb = __floats2bfloat162_rn(p0, p1);
+          const float x0 = fmaf(__uint_as_float(c < 32 ? ra[c] : rb[c - 32]), scale, -m_use);
+          const float x1 = fmaf(__uint_as_float(c + 1 < 32 ? ra[c + 1] : rb[c - 31]), scale, -m_use);
+          const float2 p = ex2_pair(x0, x1);
+          r4[(c >> 1) & 3] += p.x + p.y;
+          __nv_bfloat162 pb = __floats2bfloat162_rn(p.x, p.y);
           pk[c >> 1] = *reinterpret_cast<uint32_t*>(&pb);
         }
         l += (r4[0] + r4[1]) + (r4[2] + r4[3]);
