@@ -53,6 +53,7 @@ constexpr int SMEM_BYTES = 2 * Q_BYTES + STAGES * 2 * KV_BYTES + 1024;
 constexpr uint32_t TMEM_COLS = 256;
 constexpr uint32_t COL_S = 0, COL_O = 2 * KT, COL_P = 2 * KT + DH;
 constexpr float kRescaleLog2 = 8.f;  // move the reference max when exceeded by 2^8
+constexpr int RING = 4;              // decoded work items in flight (producer -> consumers)
 constexpr uint32_t IDESC_S = idesc_bf16(QT, KT, false, false);
 constexpr uint32_t IDESC_O = idesc_bf16(QT, DH, false, true);
 
@@ -80,7 +81,7 @@ __device__ __forceinline__ float2 ex2_pair(float a, float b) {
 }
 
 struct Item {
-  int b, q0, h, s0, n, nk, t_lo, n_kv;
+  int b, q0, h, s0, n, nk, t_lo, n_kv;  // n_kv < 0 marks the end of this CTA's list
 };
 
 // Work item w: list form (tiles != null): tile w / H, head w % H; grid form:
@@ -120,7 +121,8 @@ __global__ void __launch_bounds__(kThreads, 2)
                    int n_items, int nqt, int* err) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t q_full[2], q_empty[2], kv_full[STAGES], kv_empty[STAGES], s_full[2],
-      s_empty[2], p_full[2], pv_done[2], drain;
+      s_empty[2], p_full[2], pv_done[2], drain, it_full[RING], it_empty[RING];
+  __shared__ Item ring[RING];  // this CTA's work items, decoded once by the producer
   __shared__ uint32_t tmem_sh;
   __shared__ volatile int abort_sh;
 
@@ -142,6 +144,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
+    for (int i = 0; i < RING; ++i) {
+      mbar_init(&it_full[i], 1);
+      mbar_init(&it_empty[i], 1 + 4);  // the MMA's P.V cursor + the 4 softmax warps
+    }
     mbar_init(&drain, 1);
     abort_sh = 0;
     fence_barrier_init();
@@ -155,13 +161,34 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (warp == 4) {
     if (lane == 0) {
       // ---------------- TMA producer ----------------
+      // Decodes this CTA's items once (global loads off the consumers' paths),
+      // publishes them in the ring, then loads each item's Q and K/V tiles.
       tma_prefetch(&mapQ);
       tma_prefetch(&mapKV);
       int stage = 0, issued = 0;
-      uint32_t phase = 0, qi = 0;
-      for (int w = blockIdx.x; w < n_items && !abort_sh; w += gridDim.x) {
+      uint32_t phase = 0, qi = 0, ri = 0;
+      auto publish = [&](const Item& it) -> bool {
+        const int slot = ri % RING;
+        if (!mbar_wait(&it_empty[slot], ((ri / RING) & 1) ^ 1)) return false;
+        ring[slot] = it;
+        mbar_arrive(&it_full[slot]);  // release: the item is visible to its consumers
+        ++ri;
+        return true;
+      };
+      for (int w = blockIdx.x;; w += gridDim.x) {
         Item it;
-        if (!decode(w, tiles, H, nqt, cu, kv_lens, window, it) || it.n_kv == 0) continue;
+        if (w >= n_items || abort_sh) {
+          it.n_kv = -1;  // end of this CTA's list
+          if (!publish(it)) record_err(err, 19);
+          break;
+        }
+        if (!decode(w, tiles, H, nqt, cu, kv_lens, window, it)) continue;  // idle grid slot
+        if (!publish(it)) {
+          record_err(err, 19);
+          abort_sh = 1;
+          break;
+        }
+        if (it.n_kv == 0) continue;
         const int qb = qi & 1;
         if (!mbar_wait(&q_empty[qb], ((qi >> 1) & 1) ^ 1)) {
           record_err(err, 10);
@@ -202,39 +229,51 @@ __global__ void __launch_bounds__(kThreads, 2)
       // the P.V cursor follows the softmax.  Each pass issues whatever is ready
       // (non-blocking tests); no progress for kWaitNs is an error.
       struct Cursor {
-        int w;
+        uint32_t ri;  // ring index of the current item
         Item it;
         int j;
         uint32_t qi, g;
         int stage;
         uint32_t phase;
-        bool done;
+        bool have, done;
       };
-      auto seek = [&](Cursor& c) {  // first item at or after c.w that has key tiles
-        for (; c.w < n_items; c.w += gridDim.x)
-          if (decode(c.w, tiles, H, nqt, cu, kv_lens, window, c.it) && c.it.n_kv > 0) {
-            c.j = 0;
+      // Move to the next item with key tiles if the ring has it (non-blocking).
+      // The P.V cursor (release = true) frees ring slots it is done with.
+      auto seek = [&](Cursor& c, bool release) {
+        while (!c.have && !c.done) {
+          const int slot = c.ri % RING;
+          if (!mbar_test(&it_full[slot], (c.ri / RING) & 1)) return;
+          c.it = ring[slot];
+          if (c.it.n_kv < 0) {
+            c.done = true;
             return;
           }
-        c.done = true;
+          if (c.it.n_kv == 0) {
+            if (release) mbar_arrive(&it_empty[slot]);
+            ++c.ri;
+            continue;
+          }
+          c.j = 0;
+          c.have = true;
+        }
       };
-      auto advance = [&](Cursor& c) {
+      auto advance = [&](Cursor& c, bool release) {
         ++c.g;
         if (++c.stage == STAGES) { c.stage = 0; c.phase ^= 1; }
         if (++c.j == c.it.n_kv) {
+          if (release) mbar_arrive(&it_empty[c.ri % RING]);
           ++c.qi;
-          c.w += gridDim.x;
-          seek(c);
+          ++c.ri;
+          c.have = false;
         }
       };
-      Cursor cs{(int)blockIdx.x, {}, 0, 0u, 0u, 0, 0u, false};
+      Cursor cs{0u, {}, 0, 0u, 0u, 0, 0u, false, false};
       Cursor cp = cs;
-      seek(cs);
-      seek(cp);
       uint64_t t_last = globaltimer();
       while (!cp.done && !abort_sh) {
         bool progressed = false;
-        if (!cs.done) {
+        seek(cs, false);
+        if (cs.have) {
           const int qb = cs.qi & 1;
           if ((cs.j > 0 || mbar_test(&q_full[qb], (cs.qi >> 1) & 1)) &&
               mbar_test(&kv_full[cs.stage], cs.phase) &&
@@ -248,11 +287,12 @@ __global__ void __launch_bounds__(kThreads, 2)
                        desc_kmajor_sw128(k_addr + kk * 32), IDESC_S, kk != 0);
             mma_commit(&s_full[cs.g & 1]);
             if (cs.j == cs.it.n_kv - 1) mma_commit(&q_empty[qb]);  // Q free after its last S
-            advance(cs);
+            advance(cs, false);
             progressed = true;
           }
         }
-        if (mbar_test(&p_full[cp.g & 1], (cp.g >> 1) & 1)) {
+        seek(cp, true);
+        if (cp.have && mbar_test(&p_full[cp.g & 1], (cp.g >> 1) & 1)) {
           fence_after_sync();
           const uint32_t v_addr = smem_u32(sKV + cp.stage * 2 * KV_BYTES + KV_BYTES);
 #pragma unroll
@@ -262,7 +302,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                         (cp.j > 0 || kk > 0) ? 1u : 0u);
           mma_commit(&pv_done[cp.g & 1]);
           mma_commit(&kv_empty[cp.stage]);
-          advance(cp);
+          advance(cp, true);
           progressed = true;
         }
         if (progressed) {
@@ -293,9 +333,13 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (lane == 0) okw = mbar_wait(bar, parity) ? 1 : 0;
       return __shfl_sync(0xffffffffu, okw, 0) != 0;
     };
-    for (int w = blockIdx.x; w < n_items && !failed && !abort_sh; w += gridDim.x) {
-      Item it;
-      if (!decode(w, tiles, H, nqt, cu, kv_lens, window, it)) continue;
+    for (uint32_t ri = 0; !failed && !abort_sh; ++ri) {
+      const int slot = ri % RING;
+      if (!warp_wait(&it_full[slot], (ri / RING) & 1)) { failed = true; break; }
+      const Item it = ring[slot];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&it_empty[slot]);
+      if (it.n_kv < 0) break;  // end of this CTA's list
       const int i_q = it.q0 + r;
       const bool live = i_q < it.n;
       bf16* orow = O + (int64_t)(it.s0 + i_q) * H * DH + it.h * DH;

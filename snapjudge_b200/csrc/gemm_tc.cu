@@ -52,8 +52,8 @@ struct EpiArgs {
   int* err;
 };
 
-template <int BN>
-__host__ __device__ constexpr int stages_for() { return BN >= 256 ? 4 : 6; }
+template <int BN, bool PAIR>
+__host__ __device__ constexpr int stages_for() { return PAIR ? 6 : (BN >= 256 ? 4 : 6); }
 
 __device__ __forceinline__ void record_err(int* err, int code) {
   atomicCAS(err ? err : &g_gemm_tc_err, 0, code);
@@ -79,16 +79,20 @@ __device__ __forceinline__ void store_bf16x32(bf16* dst, const float* v) {
   }
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
                    int M, int n_tiles, int K, int up_row0, EpiArgs ep) {
-  constexpr int STAGES = stages_for<BN>();
+  // PAIR: a cluster of 2 CTAs computes 256 x BN tiles with the pair MMA; each CTA
+  // holds 128 rows of A and BN/2 rows of B per stage and 128 rows of the result.
+  constexpr int STAGES = stages_for<BN, PAIR>();
+  constexpr int BROWS = PAIR ? BN / 2 : BN;  // B rows this CTA loads per stage
   constexpr int A_BYTES = BM * BK * 2;
-  constexpr int B_BYTES = BN * BK * 2;
+  constexpr int B_BYTES = BROWS * BK * 2;
   constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   constexpr uint32_t TMEM_COLS = 2 * BN;
-  constexpr uint32_t IDESC = idesc_bf16(BM, BN, false, false);
+  constexpr int TILE_M = PAIR ? 2 * BM : BM;
+  constexpr uint32_t IDESC = idesc_bf16(TILE_M, BN, false, false);
 
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t full_bar[STAGES], empty_bar[STAGES], tfull_bar[2], tempty_bar[2], drain_bar;
@@ -97,7 +101,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m_tiles = (M + BM - 1) / BM;
+  const uint32_t rank = PAIR ? cluster_rank() : 0;
+  const int unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;  // cluster (or CTA) index
+  const int units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  const int m_tiles = (M + TILE_M - 1) / TILE_M;
   const int num_tiles = m_tiles * n_tiles;
   const int k_blocks = K / BK;
 
@@ -108,7 +115,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull_bar[b], 1);
-      mbar_init(&tempty_bar[b], kEpiWarps);
+      mbar_init(&tempty_bar[b], kEpiWarps * (PAIR ? 2 : 1));
     }
     mbar_init(&drain_bar, 1);
     abort_sh = 0;
@@ -116,19 +123,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch(&mapA);
     tma_prefetch(&mapB);
   }
-  if (warp == 1) tmem_alloc(&tmem_base_sh, TMEM_COLS);
+  if (warp == 1) {
+    if (PAIR) tmem_alloc_pair(&tmem_base_sh, TMEM_COLS);
+    else tmem_alloc(&tmem_base_sh, TMEM_COLS);
+  }
   fence_before_sync();
-  __syncthreads();
+  if (PAIR) cluster_sync();  // the peer's barriers exist before anyone signals them
+  else __syncthreads();
   fence_after_sync();
   const uint32_t tmem_base = tmem_base_sh;
 
   if (warp == 0 && lane == 0) {
-    // ---------------- TMA producer ----------------
+    // ---------------- TMA producer (both CTAs of a pair) ----------------
     int stage = 0;
     uint32_t phase = 0;
     int issued = 0;
-    for (int t = blockIdx.x; t < num_tiles && !abort_sh; t += gridDim.x) {
-      const int m0 = (t / n_tiles) * BM, nb = t % n_tiles;
+    for (int t = unit; t < num_tiles && !abort_sh; t += units) {
+      const int m0 = (t / n_tiles) * TILE_M + (int)rank * BM, nb = t % n_tiles;
       for (int kb = 0; kb < k_blocks; ++kb) {
         if (!mbar_wait(&empty_bar[stage], phase ^ 1)) {
           record_err(ep.err, 1);
@@ -137,29 +148,44 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         uint8_t* sa = smem + stage * STAGE_BYTES;
         uint8_t* sb = sa + A_BYTES;
-        mbar_expect_tx(&full_bar[stage], STAGE_BYTES);
-        tma_load_2d(sa, &mapA, &full_bar[stage], kb * BK, m0);
-        if (EPI == TC_GEGLU) {
-          tma_load_2d(sb, &mapB, &full_bar[stage], kb * BK, nb * (BN / 2));
-          tma_load_2d(sb + B_BYTES / 2, &mapB, &full_bar[stage], kb * BK, up_row0 + nb * (BN / 2));
+        if (PAIR) {
+          // both CTAs' bytes are counted on rank 0's barrier
+          const uint32_t bar0 = mapa_shared(smem_u32(&full_bar[stage]), 0);
+          if (rank == 0) mbar_expect_tx(&full_bar[stage], 2 * STAGE_BYTES);
+          tma_load_2d_pair(sa, &mapA, bar0, kb * BK, m0);
+          const int brow = EPI == TC_GEGLU ? (rank == 0 ? nb * BROWS : up_row0 + nb * BROWS)
+                                           : nb * BN + (int)rank * BROWS;
+          tma_load_2d_pair(sb, &mapB, bar0, kb * BK, brow);
         } else {
-          tma_load_2d(sb, &mapB, &full_bar[stage], kb * BK, nb * BN);
+          mbar_expect_tx(&full_bar[stage], STAGE_BYTES);
+          tma_load_2d(sa, &mapA, &full_bar[stage], kb * BK, m0);
+          if (EPI == TC_GEGLU) {
+            tma_load_2d(sb, &mapB, &full_bar[stage], kb * BK, nb * (BN / 2));
+            tma_load_2d(sb + B_BYTES / 2, &mapB, &full_bar[stage], kb * BK,
+                        up_row0 + nb * (BN / 2));
+          } else {
+            tma_load_2d(sb, &mapB, &full_bar[stage], kb * BK, nb * BN);
+          }
         }
         ++issued;
         if (++stage == STAGES) { stage = 0; phase ^= 1; }
       }
     }
-    // drain: every issued copy has landed before the CTA can exit
-    for (int i = 0; i < STAGES && i < issued; ++i) {
-      if (--stage < 0) { stage = STAGES - 1; phase ^= 1; }
-      if (!mbar_wait(&full_bar[stage], phase)) record_err(ep.err, 2);
+    // drain: every issued copy has landed before the CTA can exit (in a pair,
+    // rank 0's barriers count both CTAs' copies; the cluster barrier at the end
+    // keeps rank 1 resident until then)
+    if (!PAIR || rank == 0) {
+      for (int i = 0; i < STAGES && i < issued; ++i) {
+        if (--stage < 0) { stage = STAGES - 1; phase ^= 1; }
+        if (!mbar_wait(&full_bar[stage], phase)) record_err(ep.err, 2);
+      }
     }
-  } else if (warp == 1 && lane == 0) {
-    // ---------------- MMA issuer ----------------
+  } else if (warp == 1 && lane == 0 && rank == 0) {
+    // ---------------- MMA issuer (rank 0 of a pair) ----------------
     int stage = 0;
     uint32_t phase = 0;
     int local = 0;
-    for (int t = blockIdx.x; t < num_tiles && !abort_sh; t += gridDim.x, ++local) {
+    for (int t = unit; t < num_tiles && !abort_sh; t += units, ++local) {
       const int b = local & 1;
       const uint32_t aphase = (local >> 1) & 1;
       if (!mbar_wait(&tempty_bar[b], aphase ^ 1)) {
@@ -179,22 +205,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t a_addr = smem_u32(smem + stage * STAGE_BYTES);
         const uint32_t b_addr = a_addr + A_BYTES;
 #pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk)
-          mma_bf16(d, desc_kmajor_sw128(a_addr + kk * 32), desc_kmajor_sw128(b_addr + kk * 32),
-                   IDESC, (kb | kk) != 0);
-        mma_commit(&empty_bar[stage]);
+        for (int kk = 0; kk < BK / 16; ++kk) {
+          if (PAIR)
+            mma_bf16_pair(d, desc_kmajor_sw128(a_addr + kk * 32),
+                          desc_kmajor_sw128(b_addr + kk * 32), IDESC, (kb | kk) != 0);
+          else
+            mma_bf16(d, desc_kmajor_sw128(a_addr + kk * 32), desc_kmajor_sw128(b_addr + kk * 32),
+                     IDESC, (kb | kk) != 0);
+        }
+        if (PAIR) mma_commit_pair(&empty_bar[stage], 0x3);
+        else mma_commit(&empty_bar[stage]);
         if (++stage == STAGES) { stage = 0; phase ^= 1; }
       }
-      mma_commit(&tfull_bar[b]);
+      if (PAIR) mma_commit_pair(&tfull_bar[b], 0x3);
+      else mma_commit(&tfull_bar[b]);
     }
-    mma_commit(&drain_bar);
+    if (PAIR) mma_commit_pair(&drain_bar, 0x1);
+    else mma_commit(&drain_bar);
     if (!mbar_wait(&drain_bar, 0)) record_err(ep.err, 5);
   } else if (warp >= 2) {
     // ---------------- epilogue ----------------
     const int q = warp & 3;             // TMEM lane quarter this warp may access
     const int hf = (warp - 2) >> 2;     // which half of the tile's columns
     int local = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+    for (int t = unit; t < num_tiles; t += units, ++local) {
       const int b = local & 1;
       const uint32_t aphase = (local >> 1) & 1;
       int ok = 1;
@@ -205,7 +239,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       fence_after_sync();
-      const int m0 = (t / n_tiles) * BM, nb = t % n_tiles;
+      const int m0 = (t / n_tiles) * TILE_M + (int)rank * BM, nb = t % n_tiles;
       const int row = m0 + q * 32 + lane;
       const bool live = row < M;
       const uint32_t tacc = tmem_base + ((uint32_t)(q * 32) << 16) + b * BN;
@@ -314,55 +348,88 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       fence_before_sync();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty_bar[b]);
+      if (lane == 0) {
+        if (PAIR) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty_bar[b]), 0));
+        else mbar_arrive(&tempty_bar[b]);
+      }
     }
   }
 
   fence_before_sync();
-  __syncthreads();
+  if (PAIR) cluster_sync();  // neither CTA leaves while the pair still uses the other
+  else __syncthreads();
   if (warp == 1) {
     __syncwarp();
     fence_after_sync();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    if (PAIR) tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    else tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool PAIR>
 cudaError_t launch(const bf16* A, const bf16* W, int M, int N_out, int K, int w_rows, EpiArgs ep,
                    cudaStream_t st) {
-  constexpr int STAGES = stages_for<BN>();
-  constexpr int SMEM = STAGES * (BM * BK * 2 + BN * BK * 2) + 1024;
+  constexpr int STAGES = stages_for<BN, PAIR>();
+  constexpr int BROWS = PAIR ? BN / 2 : BN;
+  constexpr int SMEM = STAGES * (BM * BK * 2 + BROWS * BK * 2) + 1024;
   static bool attr_set = false;
   if (!attr_set) {
-    cudaError_t rc = cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI>,
+    cudaError_t rc = cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI, PAIR>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
     if (rc != cudaSuccess) return rc;
     attr_set = true;
   }
   CUtensorMap ma, mb;
-  const int b_box = EPI == TC_GEGLU ? BN / 2 : BN;
+  const int b_box = PAIR ? BROWS : (EPI == TC_GEGLU ? BN / 2 : BN);
   if (!make_map_bf16(&ma, A, K, M, (uint64_t)K * 2, BK, BM) ||
       !make_map_bf16(&mb, W, K, w_rows, (uint64_t)K * 2, BK, b_box))
     return cudaErrorInvalidValue;
   const int out_tile = EPI == TC_GEGLU ? BN / 2 : BN;
   const int n_tiles = N_out / out_tile;
-  const int tiles = ((M + BM - 1) / BM) * n_tiles;
-  const int grid = std::min(tiles, sm_count());
+  const int tile_m = PAIR ? 2 * BM : BM;
+  const int tiles = ((M + tile_m - 1) / tile_m) * n_tiles;
   const int up_row0 = EPI == TC_GEGLU ? N_out : 0;
-  gemm_tc_kernel<BN, EPI><<<grid, kThreads, SMEM, st>>>(ma, mb, M, n_tiles, K, up_row0, ep);
-  return cudaGetLastError();
+  if (!PAIR) {
+    const int grid = std::min(tiles, sm_count());
+    gemm_tc_kernel<BN, EPI, false><<<grid, kThreads, SMEM, st>>>(ma, mb, M, n_tiles, K, up_row0, ep);
+    return cudaGetLastError();
+  }
+  const int pairs = std::min(tiles, sm_count() / 2);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, EPI, true>, ma, mb, M, n_tiles, K, up_row0,
+                            ep);
 }
+
+// Pair tiles (256 x 256) for large GEMMs; single-CTA tiles otherwise.
+constexpr int kPairMinRows = 2048;
 
 template <int EPI>
 cudaError_t dispatch_bn(const bf16* A, const bf16* W, int M, int N, int K, int w_rows, EpiArgs ep,
                         cudaStream_t st) {
   if (EPI == TC_GEGLU) {
-    if (N % 128 == 0) return launch<256, EPI>(A, W, M, N, K, w_rows, ep, st);
-    return launch<128, EPI>(A, W, M, N, K, w_rows, ep, st);
+    if (N % 128 == 0) {
+      if (M >= kPairMinRows) return launch<256, EPI, true>(A, W, M, N, K, w_rows, ep, st);
+      return launch<256, EPI, false>(A, W, M, N, K, w_rows, ep, st);
+    }
+    return launch<128, EPI, false>(A, W, M, N, K, w_rows, ep, st);
   }
-  if (N % 256 == 0) return launch<256, EPI>(A, W, M, N, K, w_rows, ep, st);
-  if (N % 128 == 0) return launch<128, EPI>(A, W, M, N, K, w_rows, ep, st);
-  return launch<64, EPI>(A, W, M, N, K, w_rows, ep, st);
+  if (N % 256 == 0) {
+    if (M >= kPairMinRows) return launch<256, EPI, true>(A, W, M, N, K, w_rows, ep, st);
+    return launch<256, EPI, false>(A, W, M, N, K, w_rows, ep, st);
+  }
+  if (N % 128 == 0) return launch<128, EPI, false>(A, W, M, N, K, w_rows, ep, st);
+  return launch<64, EPI, false>(A, W, M, N, K, w_rows, ep, st);
 }
 
 }  // namespace

@@ -36,7 +36,9 @@ def rnd(shape, seed, scale=1.0):
 
 
 @pytest.mark.parametrize("M,N,K", [(1, 64, 64), (37, 96, 48), (300, 256, 128), (129, 768, 768),
-                                   (1000, 2304, 768), (77, 768, 2048)])
+                                   (1000, 2304, 768), (77, 768, 2048),
+                                   # CTA-pair tiles (M >= 2048): full and partial 256-row tiles
+                                   (4096, 768, 768), (2100, 2304, 768), (2311, 768, 2048)])
 @pytest.mark.parametrize("act,bias", [(0, False), (1, True), (2, True)])
 def test_gemm(M, N, K, act, bias):
     A = bf(rnd((M, K), 1))
@@ -47,7 +49,8 @@ def test_gemm(M, N, K, act, bias):
     assert_bf16_close(got, want)
 
 
-@pytest.mark.parametrize("M,F,K", [(5, 8, 16), (200, 256, 64), (513, 2048, 768), (64, 2816, 1024)])
+@pytest.mark.parametrize("M,F,K", [(5, 8, 16), (200, 256, 64), (513, 2048, 768), (64, 2816, 1024),
+                                   (3000, 2048, 768), (2048, 2816, 1024)])
 def test_gemm_geglu(M, F, K):
     A = bf(rnd((M, K), 4))
     Wi = bf(rnd((2 * F, K), 5, 0.05))
