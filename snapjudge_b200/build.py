@@ -67,6 +67,12 @@ def build(verbose: bool = False) -> str:
     os.makedirs(LIB_DIR, exist_ok=True)
     with ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
         objs = list(ex.map(lambda s: _compile(s, verbose), _sources()))
+    # drop cached objects of sources that no longer exist in this form
+    keep = {os.path.basename(o) for o in objs}
+    obj_dir = os.path.join(LIB_DIR, "obj")
+    for f in os.listdir(obj_dir):
+        if f.endswith(".o") and f not in keep:
+            os.remove(os.path.join(obj_dir, f))
     tmp = LIB + ".tmp"
     cmd = [NVCC, *ARCH, "-shared", "-cudart", "static", "-o", tmp, *objs]
     r = subprocess.run(cmd, capture_output=True, text=True)

@@ -52,8 +52,19 @@ struct EpiArgs {
   int* err;
 };
 
-template <int BN, bool PAIR>
-__host__ __device__ constexpr int stages_for() { return PAIR ? 6 : (BN >= 256 ? 4 : 6); }
+// bf16-output epilogues stage each warp's 32 x 64 chunk in shared memory and
+// store it with TMA (double-buffered per warp: 8 KB x 8 warps); the fp32
+// residual epilogue reads and writes X directly.
+template <int BN, int EPI>
+__host__ __device__ constexpr bool staged() { return EPI != TC_RESID && BN >= 128; }
+constexpr int kStageBytesPerWarp = 2 * 32 * 128;
+template <int BN, int EPI>
+__host__ __device__ constexpr int out_bytes() { return staged<BN, EPI>() ? kEpiWarps * kStageBytesPerWarp : 0; }
+template <int BN, int EPI, bool PAIR>
+__host__ __device__ constexpr int stages_for() {
+  return PAIR ? (staged<BN, EPI>() ? 5 : 6)
+              : (BN >= 256 ? (staged<BN, EPI>() ? 3 : 4) : (staged<BN, EPI>() ? 5 : 6));
+}
 
 __device__ __forceinline__ void record_err(int* err, int code) {
   atomicCAS(err ? err : &g_gemm_tc_err, 0, code);
@@ -82,10 +93,12 @@ __device__ __forceinline__ void store_bf16x32(bf16* dst, const float* v) {
 template <int BN, int EPI, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
-                   int M, int n_tiles, int K, int up_row0, EpiArgs ep) {
+                   const __grid_constant__ CUtensorMap mapC, int M, int n_tiles, int K, int up_row0,
+                   EpiArgs ep) {
   // PAIR: a cluster of 2 CTAs computes 256 x BN tiles with the pair MMA; each CTA
   // holds 128 rows of A and BN/2 rows of B per stage and 128 rows of the result.
-  constexpr int STAGES = stages_for<BN, PAIR>();
+  constexpr int STAGES = stages_for<BN, EPI, PAIR>();
+  constexpr bool STAGED = staged<BN, EPI>();
   constexpr int BROWS = PAIR ? BN / 2 : BN;  // B rows this CTA loads per stage
   constexpr int A_BYTES = BM * BK * 2;
   constexpr int B_BYTES = BROWS * BK * 2;
@@ -122,6 +135,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_barrier_init();
     tma_prefetch(&mapA);
     tma_prefetch(&mapB);
+    if (STAGED) tma_prefetch(&mapC);
   }
   if (warp == 1) {
     if (PAIR) tmem_alloc_pair(&tmem_base_sh, TMEM_COLS);
@@ -227,6 +241,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- epilogue ----------------
     const int q = warp & 3;             // TMEM lane quarter this warp may access
     const int hf = (warp - 2) >> 2;     // which half of the tile's columns
+    // staged store of a 32-row x 64-column bf16 chunk (row = lane): write it
+    // 128-byte-swizzled into this warp's staging buffer, then one TMA store
+    uint8_t* stg = smem + STAGES * STAGE_BYTES + (warp - 2) * kStageBytesPerWarp;
+    int sbuf = 0;
+    auto store_chunk = [&](const float* v, int col, int row0) {
+      if (lane == 0) bulk_wait_read<1>();  // this buffer's previous store has read it
+      __syncwarp();
+      uint8_t* rowp = stg + sbuf * (32 * 128) + lane * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          __nv_bfloat162 h = __floats2bfloat162_rn(v[c * 8 + 2 * e], v[c * 8 + 2 * e + 1]);
+          w[e] = *reinterpret_cast<uint32_t*>(&h);
+        }
+        *reinterpret_cast<uint4*>(rowp + ((c ^ (lane & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(&mapC, stg + sbuf * (32 * 128), col, row0);
+        bulk_commit();
+      }
+      sbuf ^= 1;
+    };
     int local = 0;
     for (int t = unit; t < num_tiles; t += units, ++local) {
       const int b = local & 1;
@@ -244,7 +284,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool live = row < M;
       const uint32_t tacc = tmem_base + ((uint32_t)(q * 32) << 16) + b * BN;
       uint32_t r0[32], r1[32];
-      if (EPI == TC_GEGLU) {
+      if (EPI == TC_GEGLU && STAGED) {
+        constexpr int HALF = BN / 2;    // output columns of the tile
+        const int col_base = nb * HALF;
+#pragma unroll 1
+        for (int c = hf * HALF / 2; c < (hf + 1) * HALF / 2; c += 64) {
+          float v[64];
+#pragma unroll
+          for (int k2 = 0; k2 < 2; ++k2) {
+            tmem_ld32(tacc + c + 32 * k2, r0);
+            tmem_ld32(tacc + HALF + c + 32 * k2, r1);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              v[32 * k2 + j] = gelu_erf(__uint_as_float(r0[j])) * __uint_as_float(r1[j]);
+          }
+          store_chunk(v, col_base + c, m0 + q * 32);
+        }
+      } else if (EPI == TC_GEGLU) {
         constexpr int HALF = BN / 2;    // output columns of the tile
         const int col_base = nb * HALF;
 #pragma unroll 1
@@ -292,7 +349,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             v[j] = rot ? x0 * cs[j] - x1 * sn[j] : x0;
             v[32 + j] = rot ? x1 * cs[j] + x0 * sn[j] : x1;
           }
-          if (live) {
+          if (STAGED) {
+            store_chunk(v, col_base + c, m0 + q * 32);
+          } else if (live) {
             store_bf16x32(ep.C + (int64_t)row * ep.ldc + col_base + c, v);
             store_bf16x32(ep.C + (int64_t)row * ep.ldc + col_base + c + 32, v + 32);
           }
@@ -329,6 +388,24 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
+      } else if (STAGED) {
+        const int col_base = nb * BN;
+#pragma unroll 1
+        for (int c = hf * BN / 2; c < (hf + 1) * BN / 2; c += 64) {
+          float v[64];
+#pragma unroll
+          for (int k2 = 0; k2 < 2; ++k2) {
+            tmem_ld32(tacc + c + 32 * k2, r0);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              float a = __uint_as_float(r0[j]);
+              if (ep.bias) a += ep.bias[col_base + c + 32 * k2 + j];
+              v[32 * k2 + j] = act_fn(a, ep.act);
+            }
+          }
+          store_chunk(v, col_base + c, m0 + q * 32);
+        }
       } else {
         const int col_base = nb * BN;
 #pragma unroll 1
@@ -353,6 +430,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         else mbar_arrive(&tempty_bar[b]);
       }
     }
+    if (STAGED && lane == 0) bulk_wait_all();  // staged stores done before the CTA exits
   }
 
   fence_before_sync();
@@ -369,9 +447,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int BN, int EPI, bool PAIR>
 cudaError_t launch(const bf16* A, const bf16* W, int M, int N_out, int K, int w_rows, EpiArgs ep,
                    cudaStream_t st) {
-  constexpr int STAGES = stages_for<BN, PAIR>();
+  constexpr int STAGES = stages_for<BN, EPI, PAIR>();
   constexpr int BROWS = PAIR ? BN / 2 : BN;
-  constexpr int SMEM = STAGES * (BM * BK * 2 + BROWS * BK * 2) + 1024;
+  constexpr int SMEM = STAGES * (BM * BK * 2 + BROWS * BK * 2) + out_bytes<BN, EPI>() + 1024;
   static bool attr_set = false;
   if (!attr_set) {
     cudaError_t rc = cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI, PAIR>,
@@ -379,11 +457,16 @@ cudaError_t launch(const bf16* A, const bf16* W, int M, int N_out, int K, int w_
     if (rc != cudaSuccess) return rc;
     attr_set = true;
   }
-  CUtensorMap ma, mb;
+  CUtensorMap ma, mb, mc;
   const int b_box = PAIR ? BROWS : (EPI == TC_GEGLU ? BN / 2 : BN);
   if (!make_map_bf16(&ma, A, K, M, (uint64_t)K * 2, BK, BM) ||
       !make_map_bf16(&mb, W, K, w_rows, (uint64_t)K * 2, BK, b_box))
     return cudaErrorInvalidValue;
+  if (staged<BN, EPI>()) {
+    if (!make_map_bf16(&mc, ep.C, N_out, M, (uint64_t)N_out * 2, 64, 32)) return cudaErrorInvalidValue;
+  } else {
+    mc = ma;  // unused
+  }
   const int out_tile = EPI == TC_GEGLU ? BN / 2 : BN;
   const int n_tiles = N_out / out_tile;
   const int tile_m = PAIR ? 2 * BM : BM;
@@ -391,7 +474,8 @@ cudaError_t launch(const bf16* A, const bf16* W, int M, int N_out, int K, int w_
   const int up_row0 = EPI == TC_GEGLU ? N_out : 0;
   if (!PAIR) {
     const int grid = std::min(tiles, sm_count());
-    gemm_tc_kernel<BN, EPI, false><<<grid, kThreads, SMEM, st>>>(ma, mb, M, n_tiles, K, up_row0, ep);
+    gemm_tc_kernel<BN, EPI, false><<<grid, kThreads, SMEM, st>>>(ma, mb, mc, M, n_tiles, K, up_row0,
+                                                                  ep);
     return cudaGetLastError();
   }
   const int pairs = std::min(tiles, sm_count() / 2);
@@ -407,8 +491,8 @@ cudaError_t launch(const bf16* A, const bf16* W, int M, int N_out, int K, int w_
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, EPI, true>, ma, mb, M, n_tiles, K, up_row0,
-                            ep);
+  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, EPI, true>, ma, mb, mc, M, n_tiles, K,
+                            up_row0, ep);
 }
 
 // Pair tiles (256 x 256) for large GEMMs; single-CTA tiles otherwise.
