@@ -52,11 +52,12 @@ struct EpiArgs {
   int* err;
 };
 
-// bf16-output epilogues stage each warp's 32 x 64 chunk in shared memory and
-// store it with TMA (double-buffered per warp: 8 KB x 8 warps); the fp32
-// residual epilogue reads and writes X directly.
+// Epilogues move data through a per-warp pair of 4 KB swizzled shared-memory
+// buffers (8 KB x 8 warps): bf16 outputs are staged as 32 x 64 chunks and
+// written with TMA stores; the fp32 residual X is read as 32 x 32 chunks with
+// TMA loads (the next chunk in flight), updated, and written back with TMA.
 template <int BN, int EPI>
-__host__ __device__ constexpr bool staged() { return EPI != TC_RESID && BN >= 128; }
+__host__ __device__ constexpr bool staged() { return BN >= 128; }
 constexpr int kStageBytesPerWarp = 2 * 32 * 128;
 template <int BN, int EPI>
 __host__ __device__ constexpr int out_bytes() { return staged<BN, EPI>() ? kEpiWarps * kStageBytesPerWarp : 0; }
@@ -109,6 +110,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t full_bar[STAGES], empty_bar[STAGES], tfull_bar[2], tempty_bar[2], drain_bar;
+  __shared__ uint64_t xload_bar[kEpiWarps][2];  // residual chunk loads (RESID epilogue)
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_sh;
 
@@ -131,6 +133,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tempty_bar[b], kEpiWarps * (PAIR ? 2 : 1));
     }
     mbar_init(&drain_bar, 1);
+    for (int w = 0; w < kEpiWarps; ++w) {
+      mbar_init(&xload_bar[w][0], 1);
+      mbar_init(&xload_bar[w][1], 1);
+    }
     abort_sh = 0;
     fence_barrier_init();
     tma_prefetch(&mapA);
@@ -245,6 +251,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // 128-byte-swizzled into this warp's staging buffer, then one TMA store
     uint8_t* stg = smem + STAGES * STAGE_BYTES + (warp - 2) * kStageBytesPerWarp;
     int sbuf = 0;
+    uint32_t xphase = 0u;  // bit b: parity of this warp's residual-load barrier b
     auto store_chunk = [&](const float* v, int col, int row0) {
       if (lane == 0) bulk_wait_read<1>();  // this buffer's previous store has read it
       __syncwarp();
@@ -356,38 +363,52 @@ __global__ void __launch_bounds__(kThreads, 1)
             store_bf16x32(ep.C + (int64_t)row * ep.ldc + col_base + c + 32, v + 32);
           }
         }
-      } else if (EPI == TC_RESID) {
-        // X += acc, software-pipelined: the next chunk's residual loads are in
-        // flight while the current chunk is added and stored
+      } else if (EPI == TC_RESID && STAGED) {
+        // X += acc through TMA: 32 x 32 fp32 chunks, the next one loading while
+        // this one is updated; rows past M are neither read nor written
         constexpr int NCH = BN / 64;  // 32-column chunks in this warp's half
         const int c0 = hf * BN / 2;
-        float* xrow = ep.resid + (int64_t)row * ep.ldr + nb * BN + c0;
-        float4 xv[2][8];
-        if (live) {
-#pragma unroll
-          for (int j = 0; j < 8; ++j) xv[0][j] = reinterpret_cast<const float4*>(xrow)[j];
-        }
-#pragma unroll
+        const int xcol = nb * BN + c0, xrow = m0 + q * 32;
+        uint64_t* xb = xload_bar[warp - 2];
+        auto load = [&](int k) {  // chunk k into buffer k & 1 (lane 0)
+          const int bb = k & 1;
+          bulk_wait_read<1>();  // that buffer's previous store has read it
+          mbar_expect_tx(&xb[bb], 32 * 128);
+          tma_load_2d(stg + bb * 4096, &mapC, &xb[bb], xcol + 32 * k, xrow);
+        };
+        if (lane == 0) load(0);
+#pragma unroll 1
         for (int k = 0; k < NCH; ++k) {
-          if (k + 1 < NCH && live) {
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-              xv[(k + 1) & 1][j] = reinterpret_cast<const float4*>(xrow + 32 * (k + 1))[j];
-          }
+          if (lane == 0 && k + 1 < NCH) load(k + 1);
           tmem_ld32(tacc + c0 + 32 * k, r0);
+          int okx = 1;
+          if (lane == 0) okx = mbar_wait(&xb[k & 1], (xphase >> (k & 1)) & 1u) ? 1 : 0;
+          okx = __shfl_sync(0xffffffffu, okx, 0);
+          xphase ^= 1u << (k & 1);
           tmem_ld_wait();
-          if (live) {
+          if (!okx) {
+            if (lane == 0) { record_err(ep.err, 7); abort_sh = 1; }
+            break;
+          }
+          uint8_t* rowp = stg + (k & 1) * 4096 + lane * 128;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              float4 o = xv[k & 1][j];
-              o.x += __uint_as_float(r0[4 * j]);
-              o.y += __uint_as_float(r0[4 * j + 1]);
-              o.z += __uint_as_float(r0[4 * j + 2]);
-              o.w += __uint_as_float(r0[4 * j + 3]);
-              reinterpret_cast<float4*>(xrow + 32 * k)[j] = o;
-            }
+          for (int c = 0; c < 8; ++c) {
+            float4* cell = reinterpret_cast<float4*>(rowp + ((c ^ (lane & 7)) << 4));
+            float4 o = *cell;
+            o.x += __uint_as_float(r0[4 * c]);
+            o.y += __uint_as_float(r0[4 * c + 1]);
+            o.z += __uint_as_float(r0[4 * c + 2]);
+            o.w += __uint_as_float(r0[4 * c + 3]);
+            *cell = o;
+          }
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&mapC, stg + (k & 1) * 4096, xcol + 32 * k, xrow);
+            bulk_commit();
           }
         }
+      } else if (EPI == TC_RESID) {
       } else if (STAGED) {
         const int col_base = nb * BN;
 #pragma unroll 1
@@ -462,7 +483,10 @@ cudaError_t launch(const bf16* A, const bf16* W, int M, int N_out, int K, int w_
   if (!make_map_bf16(&ma, A, K, M, (uint64_t)K * 2, BK, BM) ||
       !make_map_bf16(&mb, W, K, w_rows, (uint64_t)K * 2, BK, b_box))
     return cudaErrorInvalidValue;
-  if (staged<BN, EPI>()) {
+  if (staged<BN, EPI>() && EPI == TC_RESID) {
+    if (!make_map_f32(&mc, ep.resid, N_out, M, (uint64_t)N_out * 4, 32, 32))
+      return cudaErrorInvalidValue;
+  } else if (staged<BN, EPI>()) {
     if (!make_map_bf16(&mc, ep.C, N_out, M, (uint64_t)N_out * 2, 64, 32)) return cudaErrorInvalidValue;
   } else {
     mc = ma;  // unused
