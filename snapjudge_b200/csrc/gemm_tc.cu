@@ -409,6 +409,37 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       } else if (EPI == TC_RESID) {
+        // narrow tiles: X += acc with direct loads and stores, the next
+        // chunk's residual loads in flight while the current one is added
+        constexpr int NCH = BN / 64;  // 32-column chunks in this warp's half
+        const int c0 = hf * BN / 2;
+        float* xrow = ep.resid + (int64_t)row * ep.ldr + nb * BN + c0;
+        float4 xv[2][8];
+        if (live) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) xv[0][j] = reinterpret_cast<const float4*>(xrow)[j];
+        }
+#pragma unroll
+        for (int k = 0; k < NCH; ++k) {
+          if (k + 1 < NCH && live) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              xv[(k + 1) & 1][j] = reinterpret_cast<const float4*>(xrow + 32 * (k + 1))[j];
+          }
+          tmem_ld32(tacc + c0 + 32 * k, r0);
+          tmem_ld_wait();
+          if (live) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              float4 o = xv[k & 1][j];
+              o.x += __uint_as_float(r0[4 * j]);
+              o.y += __uint_as_float(r0[4 * j + 1]);
+              o.z += __uint_as_float(r0[4 * j + 2]);
+              o.w += __uint_as_float(r0[4 * j + 3]);
+              reinterpret_cast<float4*>(xrow + 32 * k)[j] = o;
+            }
+          }
+        }
       } else if (STAGED) {
         const int col_base = nb * BN;
 #pragma unroll 1
