@@ -55,9 +55,10 @@ struct EpiArgs {
 // Epilogues move data through a per-warp pair of 4 KB swizzled shared-memory
 // buffers (8 KB x 8 warps): bf16 outputs are staged as 32 x 64 chunks and
 // written with TMA stores; the fp32 residual X is read as 32 x 32 chunks with
-// TMA loads (the next chunk in flight), updated, and written back with TMA.
+// TMA loads (two in flight), updated, and written back with TMA.  GEGLU on
+// 128-column tiles (32 outputs per warp) and 64-column tiles store directly.
 template <int BN, int EPI>
-__host__ __device__ constexpr bool staged() { return BN >= 128; }
+__host__ __device__ constexpr bool staged() { return BN == 256 || (BN == 128 && EPI != TC_GEGLU); }
 constexpr int kStageBytesPerWarp = 2 * 32 * 128;
 template <int BN, int EPI>
 __host__ __device__ constexpr int out_bytes() { return staged<BN, EPI>() ? kEpiWarps * kStageBytesPerWarp : 0; }
@@ -100,6 +101,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   // holds 128 rows of A and BN/2 rows of B per stage and 128 rows of the result.
   constexpr int STAGES = stages_for<BN, EPI, PAIR>();
   constexpr bool STAGED = staged<BN, EPI>();
+  // the residual epilogue releases the accumulator as soon as it is in registers
+  constexpr bool EARLY = EPI == TC_RESID && STAGED;
   constexpr int BROWS = PAIR ? BN / 2 : BN;  // B rows this CTA loads per stage
   constexpr int A_BYTES = BM * BK * 2;
   constexpr int B_BYTES = BROWS * BK * 2;
@@ -252,6 +255,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* stg = smem + STAGES * STAGE_BYTES + (warp - 2) * kStageBytesPerWarp;
     int sbuf = 0;
     uint32_t xphase = 0u;  // bit b: parity of this warp's residual-load barrier b
+    uint64_t* xb = xload_bar[warp - 2];
+    // hand accumulator buffer b back to the MMA warp (rank 0's barrier in a pair)
+    auto release = [&](int b) {
+      fence_before_sync();
+      __syncwarp();
+      if (lane == 0) {
+        if (PAIR) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty_bar[b]), 0));
+        else mbar_arrive(&tempty_bar[b]);
+      }
+    };
     auto store_chunk = [&](const float* v, int col, int row0) {
       if (lane == 0) bulk_wait_read<1>();  // this buffer's previous store has read it
       __syncwarp();
@@ -278,6 +291,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = unit; t < num_tiles; t += units, ++local) {
       const int b = local & 1;
       const uint32_t aphase = (local >> 1) & 1;
+      const int m0 = (t / n_tiles) * TILE_M + (int)rank * BM, nb = t % n_tiles;
+      if (EARLY && lane == 0) {
+        // request this tile's first two X chunks while its MMAs still run
+        bulk_wait_read<0>();  // the previous tile's stores have read both buffers
+#pragma unroll
+        for (int k = 0; k < 2 && k < BN / 64; ++k) {
+          mbar_expect_tx(&xb[k], 32 * 128);
+          tma_load_2d(stg + k * 4096, &mapC, &xb[k], nb * BN + hf * BN / 2 + 32 * k, m0 + q * 32);
+        }
+      }
       int ok = 1;
       if (lane == 0) ok = mbar_wait(&tfull_bar[b], aphase) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -286,7 +309,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       fence_after_sync();
-      const int m0 = (t / n_tiles) * TILE_M + (int)rank * BM, nb = t % n_tiles;
       const int row = m0 + q * 32 + lane;
       const bool live = row < M;
       const uint32_t tacc = tmem_base + ((uint32_t)(q * 32) << 16) + b * BN;
@@ -364,28 +386,25 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       } else if (EPI == TC_RESID && STAGED) {
-        // X += acc through TMA: 32 x 32 fp32 chunks, the next one loading while
-        // this one is updated; rows past M are neither read nor written
+        // X += acc through TMA: the warp's half of the accumulator is read into
+        // registers and released at once; X arrives as 32 x 32 fp32 chunks in
+        // two buffers (the first two requested before the accumulator was
+        // ready), is updated and written back; rows past M are neither read
+        // nor written
         constexpr int NCH = BN / 64;  // 32-column chunks in this warp's half
         const int c0 = hf * BN / 2;
         const int xcol = nb * BN + c0, xrow = m0 + q * 32;
-        uint64_t* xb = xload_bar[warp - 2];
-        auto load = [&](int k) {  // chunk k into buffer k & 1 (lane 0)
-          const int bb = k & 1;
-          bulk_wait_read<1>();  // that buffer's previous store has read it
-          mbar_expect_tx(&xb[bb], 32 * 128);
-          tma_load_2d(stg + bb * 4096, &mapC, &xb[bb], xcol + 32 * k, xrow);
-        };
-        if (lane == 0) load(0);
-#pragma unroll 1
+        uint32_t acc[NCH][32];
+#pragma unroll
+        for (int k = 0; k < NCH; ++k) tmem_ld32(tacc + c0 + 32 * k, acc[k]);
+        tmem_ld_wait();
+        release(b);
+#pragma unroll
         for (int k = 0; k < NCH; ++k) {
-          if (lane == 0 && k + 1 < NCH) load(k + 1);
-          tmem_ld32(tacc + c0 + 32 * k, r0);
           int okx = 1;
           if (lane == 0) okx = mbar_wait(&xb[k & 1], (xphase >> (k & 1)) & 1u) ? 1 : 0;
           okx = __shfl_sync(0xffffffffu, okx, 0);
           xphase ^= 1u << (k & 1);
-          tmem_ld_wait();
           if (!okx) {
             if (lane == 0) { record_err(ep.err, 7); abort_sh = 1; }
             break;
@@ -395,10 +414,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int c = 0; c < 8; ++c) {
             float4* cell = reinterpret_cast<float4*>(rowp + ((c ^ (lane & 7)) << 4));
             float4 o = *cell;
-            o.x += __uint_as_float(r0[4 * c]);
-            o.y += __uint_as_float(r0[4 * c + 1]);
-            o.z += __uint_as_float(r0[4 * c + 2]);
-            o.w += __uint_as_float(r0[4 * c + 3]);
+            o.x += __uint_as_float(acc[k][4 * c]);
+            o.y += __uint_as_float(acc[k][4 * c + 1]);
+            o.z += __uint_as_float(acc[k][4 * c + 2]);
+            o.w += __uint_as_float(acc[k][4 * c + 3]);
             *cell = o;
           }
           fence_async_smem();
@@ -406,6 +425,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane == 0) {
             tma_store_2d(&mapC, stg + (k & 1) * 4096, xcol + 32 * k, xrow);
             bulk_commit();
+            if (k + 2 < NCH) {  // chunk k + 2 into this buffer once the store has read it
+              bulk_wait_read<0>();
+              mbar_expect_tx(&xb[k & 1], 32 * 128);
+              tma_load_2d(stg + (k & 1) * 4096, &mapC, &xb[k & 1], xcol + 32 * (k + 2), xrow);
+            }
           }
         }
       } else if (EPI == TC_RESID) {
@@ -475,12 +499,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           store_bf16x32(ep.C + (int64_t)row * ep.ldc + col_base + c, v);
         }
       }
-      fence_before_sync();
-      __syncwarp();
-      if (lane == 0) {
-        if (PAIR) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty_bar[b]), 0));
-        else mbar_arrive(&tempty_bar[b]);
-      }
+      if constexpr (!EARLY) release(b);
     }
     if (STAGED && lane == 0) bulk_wait_all();  // staged stores done before the CTA exits
   }

@@ -50,7 +50,9 @@ def test_gemm(M, N, K, act, bias):
 
 
 @pytest.mark.parametrize("M,F,K", [(5, 8, 16), (200, 256, 64), (513, 2048, 768), (64, 2816, 1024),
-                                   (3000, 2048, 768), (2048, 2816, 1024)])
+                                   (3000, 2048, 768), (2048, 2816, 1024),
+                                   # F an odd multiple of 64: 128-column tiles, direct stores
+                                   (300, 192, 128), (2200, 320, 256)])
 def test_gemm_geglu(M, F, K):
     A = bf(rnd((M, K), 4))
     Wi = bf(rnd((2 * F, K), 5, 0.05))
