@@ -6,27 +6,29 @@
 // q/k/v/o, fp32 scores and accumulation; P is rounded to bf16 for the P.V MMA
 // (the row normaliser sums the fp32 probabilities).
 //
-// Persistent: 2 CTAs per SM walk a strided list of work items (128 queries of
-// one segment x one head), longest segments first.  192 threads per CTA:
-//   warps 0-3  softmax: thread = query row = TMEM lane.  Reads S_j from TMEM,
-//              writes P_j (bf16) back to TMEM and moves on: the output is
-//              accumulated in TMEM by the tensor core, so the softmax never
-//              waits for a P.V product except to rescale it (below) and at the
-//              end of an item
-//   warp 4     TMA producer: Q of each item (2 buffers), then its K/V tiles of
-//              64 keys through a 4-stage ring that runs on across items
-//   warp 5     MMA issuer: S_j = Q K_j^T into TMEM S[g%2] (M=128, N=64, K=64,
-//              both operands in shared memory); O += P_j V_j with P_j read from
-//              TMEM (the A operand) and V from shared memory (MN-major); g
-//              counts key tiles across items, so every phase runs on across items
+// Built for many short items: 4 small CTAs per SM, each a complete pipeline of
+// its own, so an SM always has several independent (S -> softmax -> P.V)
+// chains in flight.  A work item is 128 queries of one segment x one head; a
+// CTA walks a strided list of items, longest segments first.
+//   128 threads: thread = query row = TMEM lane (softmax, output).  Thread 0
+//   also issues the TMA loads and the MMAs:
+//     Q of the item (one 16 KB buffer, loaded for the next item as soon as the
+//     current item's last S is computed), K/V tiles of 64 keys through a
+//     2-stage ring that runs on across items;
+//     S = Q K^T (M=128, N=64, K=64) into TMEM, then O += P V with P read from
+//     TMEM (the A operand) and V from shared memory (MN-major).
+//   TMEM (128 columns): S (fp32, 64) — P (bf16 pairs) overwrites its first 32
+//   columns once S is in registers — and O (fp32, 64).
 // Rescaling: each row keeps a reference max m_ref for its exponentials and
 // moves it only when a tile's max exceeds it by more than 2^8 (exponent 8 in
 // log2 units); then the row's O (in TMEM) and running sum are multiplied by
 // 2^(m_ref_old - m_ref_new) before the next P.V accumulates.  The result is the
 // same softmax (every term uses the same reference), with P <= 2^8.
 // Keys past kv_len and outside the window are masked with -inf (interior tiles
-// skip the mask); key tiles wholly outside the window are skipped.  All mbarrier
-// waits are bounded (error code, no trap).
+// skip the mask); key tiles wholly outside the window are skipped.
+// Work items are decoded into shared memory 64 at a time by all threads.  Every
+// mbarrier wait is bounded; a failed wait is carried to the next block-wide
+// barrier (__syncthreads_or), where all threads leave together (no trap).
 #include <algorithm>
 
 #include "common.cuh"
@@ -44,16 +46,16 @@ using namespace tc;
 constexpr int QT = 128;        // queries per work item
 constexpr int KT = 64;         // keys per tile
 constexpr int DH = 64;
-constexpr int STAGES = 4;
-constexpr int kThreads = 192;
+constexpr int KV_STAGES = 2;
+constexpr int kThreads = 128;
+constexpr int kCtasPerSm = 4;
+constexpr int CHUNK = 64;      // work items decoded at a time
 constexpr int Q_BYTES = QT * DH * 2;       // 16 KB
 constexpr int KV_BYTES = KT * DH * 2;      // 8 KB each for K and V
-constexpr int SMEM_BYTES = 2 * Q_BYTES + STAGES * 2 * KV_BYTES + 1024;
-// TMEM columns: S[2] (fp32 64 each) | O (fp32 64) | P[2] (bf16 pairs, 32 each)
-constexpr uint32_t TMEM_COLS = 256;
-constexpr uint32_t COL_S = 0, COL_O = 2 * KT, COL_P = 2 * KT + DH;
+constexpr int SMEM_BYTES = Q_BYTES + KV_STAGES * 2 * KV_BYTES + 1024;
+constexpr uint32_t TMEM_COLS = 128;
+constexpr uint32_t COL_S = 0, COL_O = KT;  // P (bf16 pairs) in columns [0, 32) over S
 constexpr float kRescaleLog2 = 8.f;  // move the reference max when exceeded by 2^8
-constexpr int RING = 4;              // decoded work items in flight (producer -> consumers)
 constexpr uint32_t IDESC_S = idesc_bf16(QT, KT, false, false);
 constexpr uint32_t IDESC_O = idesc_bf16(QT, DH, false, true);
 
@@ -80,29 +82,35 @@ __device__ __forceinline__ float2 ex2_pair(float a, float b) {
   return r;
 }
 
-struct Item {
-  int b, q0, h, s0, n, nk, t_lo, n_kv;  // n_kv < 0 marks the end of this CTA's list
+struct __align__(16) Item {
+  int q0, h, s0, n, nk, t_lo, n_kv, pad;  // n_kv: -1 idle grid slot, 0 no visible key
 };
 
 // Work item w: list form (tiles != null): tile w / H, head w % H; grid form:
-// w = ((b * nqt) + qtile) * H + h.  False for idle grid-form items.
-__device__ __forceinline__ bool decode(int w, const int2* tiles, int H, int nqt,
-                                       const int32_t* cu, const int32_t* kv_lens, int window,
-                                       Item& it) {
+// w = ((b * nqt) + qtile) * H + h.  Idle grid-form items get n_kv = -1.
+__device__ __forceinline__ Item decode(int w, const int2* tiles, int H, int nqt,
+                                       const int32_t* cu, const int32_t* kv_lens, int window) {
+  Item it;
   it.h = w % H;
   const int rest = w / H;
+  int b;
   if (tiles) {
     const int2 t = tiles[rest];
-    it.b = t.x;
+    b = t.x;
     it.q0 = t.y;
   } else {
-    it.b = rest / nqt;
+    b = rest / nqt;
     it.q0 = (rest % nqt) * QT;
   }
-  it.s0 = cu[it.b];
-  it.n = cu[it.b + 1] - it.s0;
-  if (it.q0 >= it.n) return false;
-  int nk = kv_lens ? kv_lens[it.b] : it.n;
+  it.s0 = cu[b];
+  it.n = cu[b + 1] - it.s0;
+  it.pad = 0;
+  if (it.q0 >= it.n) {
+    it.nk = it.t_lo = 0;
+    it.n_kv = -1;
+    return it;
+  }
+  const int nk = kv_lens ? kv_lens[b] : it.n;
   it.nk = min(nk, it.n);
   int k_lo = 0, k_hi = it.nk;
   if (window > 0) {
@@ -111,260 +119,184 @@ __device__ __forceinline__ bool decode(int w, const int2* tiles, int H, int nqt,
   }
   it.t_lo = k_lo / KT;
   it.n_kv = k_hi > k_lo ? (k_hi - 1) / KT - it.t_lo + 1 : 0;
-  return true;
+  return it;
 }
 
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, kCtasPerSm)
     attn_tc_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapKV,
                    const int32_t* __restrict__ cu, const int32_t* __restrict__ kv_lens,
                    bf16* __restrict__ O, int H, int window, const int2* __restrict__ tiles,
                    int n_items, int nqt, int* err) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t q_full[2], q_empty[2], kv_full[STAGES], kv_empty[STAGES], s_full[2],
-      s_empty[2], p_full[2], pv_done[2], drain, it_full[RING], it_empty[RING];
-  __shared__ Item ring[RING];  // this CTA's work items, decoded once by the producer
+  __shared__ uint64_t q_full, kv_full[KV_STAGES], s_full, pv_done, drain;
+  __shared__ Item items[2][CHUNK];  // this CTA's work items, chunk c in items[c & 1]
   __shared__ uint32_t tmem_sh;
-  __shared__ volatile int abort_sh;
 
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-  uint8_t* sQ = smem;                 // Q[2]
-  uint8_t* sKV = smem + 2 * Q_BYTES;  // stage s: K at s*2*KV, V at +KV
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint8_t* sQ = smem;
+  uint8_t* sKV = smem + Q_BYTES;  // stage s: K at s * 2 * KV, V at + KV
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const bool leader = tid == 0;
 
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&q_full[i], 1);
-      mbar_init(&q_empty[i], 1);
-      mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 4);
-      mbar_init(&p_full[i], 4);
-      mbar_init(&pv_done[i], 1);
-    }
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
-    }
-    for (int i = 0; i < RING; ++i) {
-      mbar_init(&it_full[i], 1);
-      mbar_init(&it_empty[i], 1 + 4);  // the MMA's P.V cursor + the 4 softmax warps
-    }
+  // this CTA's items: w = blockIdx.x + k * gridDim.x, k < cnt
+  const int cnt =
+      n_items > (int)blockIdx.x ? (n_items - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  auto decode_chunk = [&](int c) {
+    const int k = c * CHUNK + tid;
+    if (tid < CHUNK && k < cnt)
+      items[c & 1][tid] = decode((int)blockIdx.x + k * (int)gridDim.x, tiles, H, nqt, cu, kv_lens,
+                                 window);
+  };
+
+  if (leader) {
+    mbar_init(&q_full, 1);
+    for (int s = 0; s < KV_STAGES; ++s) mbar_init(&kv_full[s], 1);
+    mbar_init(&s_full, 1);
+    mbar_init(&pv_done, 1);
     mbar_init(&drain, 1);
-    abort_sh = 0;
     fence_barrier_init();
+    tma_prefetch(&mapQ);
+    tma_prefetch(&mapKV);
   }
-  if (warp == 5) tmem_alloc(&tmem_sh, TMEM_COLS);
+  if (warp == 0) tmem_alloc(&tmem_sh, TMEM_COLS);
+  decode_chunk(0);
+  decode_chunk(1);
   fence_before_sync();
   __syncthreads();
   fence_after_sync();
   const uint32_t tmem = tmem_sh;
 
-  if (warp == 4) {
-    if (lane == 0) {
-      // ---------------- TMA producer ----------------
-      // Decodes this CTA's items once (global loads off the consumers' paths),
-      // publishes them in the ring, then loads each item's Q and K/V tiles.
-      tma_prefetch(&mapQ);
-      tma_prefetch(&mapKV);
-      int stage = 0, issued = 0;
-      uint32_t phase = 0, qi = 0, ri = 0;
-      auto publish = [&](const Item& it) -> bool {
-        const int slot = ri % RING;
-        if (!mbar_wait(&it_empty[slot], ((ri / RING) & 1) ^ 1)) return false;
-        ring[slot] = it;
-        mbar_arrive(&it_full[slot]);  // release: the item is visible to its consumers
-        ++ri;
-        return true;
-      };
-      for (int w = blockIdx.x;; w += gridDim.x) {
-        Item it;
-        if (w >= n_items || abort_sh) {
-          it.n_kv = -1;  // end of this CTA's list
-          if (!publish(it)) record_err(err, 19);
-          break;
-        }
-        if (!decode(w, tiles, H, nqt, cu, kv_lens, window, it)) continue;  // idle grid slot
-        if (!publish(it)) {
-          record_err(err, 19);
-          abort_sh = 1;
-          break;
-        }
-        if (it.n_kv == 0) continue;
-        const int qb = qi & 1;
-        if (!mbar_wait(&q_empty[qb], ((qi >> 1) & 1) ^ 1)) {
-          record_err(err, 10);
-          abort_sh = 1;
-          break;
-        }
-        mbar_expect_tx(&q_full[qb], Q_BYTES);
-        tma_load_2d(sQ + qb * Q_BYTES, &mapQ, &q_full[qb], it.h * DH, it.s0 + it.q0);
-        ++qi;
-        for (int j = 0; j < it.n_kv; ++j) {
-          if (!mbar_wait(&kv_empty[stage], phase ^ 1)) {
-            record_err(err, 11);
-            abort_sh = 1;
-            break;
-          }
-          const int row = it.s0 + (it.t_lo + j) * KT;
-          uint8_t* dst = sKV + stage * 2 * KV_BYTES;
-          mbar_expect_tx(&kv_full[stage], 2 * KV_BYTES);
-          tma_load_2d(dst, &mapKV, &kv_full[stage], (H + it.h) * DH, row);
-          tma_load_2d(dst + KV_BYTES, &mapKV, &kv_full[stage], (2 * H + it.h) * DH, row);
-          ++issued;
-          if (++stage == STAGES) { stage = 0; phase ^= 1; }
-        }
-      }
-      // drain: every issued copy has landed before the CTA can exit
-      for (uint32_t k = qi > 2 ? qi - 2 : 0; k < qi; ++k)
-        if (!mbar_wait(&q_full[k & 1], (k >> 1) & 1)) record_err(err, 12);
-      for (int i = 0; i < STAGES && i < issued; ++i) {
-        if (--stage < 0) { stage = STAGES - 1; phase ^= 1; }
-        if (!mbar_wait(&kv_full[stage], phase)) record_err(err, 13);
-      }
-    }
-  } else if (warp == 5) {
-    if (lane == 0) {
-      // ---------------- MMA issuer ----------------
-      // Two cursors walk the same sequence of key tiles: the S cursor runs
-      // ahead as far as the two S buffers allow (it never waits behind a P.V),
-      // the P.V cursor follows the softmax.  Each pass issues whatever is ready
-      // (non-blocking tests); no progress for kWaitNs is an error.
-      struct Cursor {
-        uint32_t ri;  // ring index of the current item
-        Item it;
-        int j;
-        uint32_t qi, g;
-        int stage;
-        uint32_t phase;
-        bool have, done;
-      };
-      // Move to the next item with key tiles if the ring has it (non-blocking).
-      // The P.V cursor (release = true) frees ring slots it is done with.
-      auto seek = [&](Cursor& c, bool release) {
-        while (!c.have && !c.done) {
-          const int slot = c.ri % RING;
-          if (!mbar_test(&it_full[slot], (c.ri / RING) & 1)) return;
-          c.it = ring[slot];
-          if (c.it.n_kv < 0) {
-            c.done = true;
-            return;
-          }
-          if (c.it.n_kv == 0) {
-            if (release) mbar_arrive(&it_empty[slot]);
-            ++c.ri;
-            continue;
-          }
-          c.j = 0;
-          c.have = true;
-        }
-      };
-      auto advance = [&](Cursor& c, bool release) {
-        ++c.g;
-        if (++c.stage == STAGES) { c.stage = 0; c.phase ^= 1; }
-        if (++c.j == c.it.n_kv) {
-          if (release) mbar_arrive(&it_empty[c.ri % RING]);
-          ++c.qi;
-          ++c.ri;
-          c.have = false;
-        }
-      };
-      Cursor cs{0u, {}, 0, 0u, 0u, 0, 0u, false, false};
-      Cursor cp = cs;
-      uint64_t t_last = globaltimer();
-      while (!cp.done && !abort_sh) {
-        bool progressed = false;
-        seek(cs, false);
-        if (cs.have) {
-          const int qb = cs.qi & 1;
-          if ((cs.j > 0 || mbar_test(&q_full[qb], (cs.qi >> 1) & 1)) &&
-              mbar_test(&kv_full[cs.stage], cs.phase) &&
-              mbar_test(&s_empty[cs.g & 1], ((cs.g >> 1) & 1) ^ 1)) {
-            fence_after_sync();
-            const uint32_t q_addr = smem_u32(sQ + qb * Q_BYTES);
-            const uint32_t k_addr = smem_u32(sKV + cs.stage * 2 * KV_BYTES);
-#pragma unroll
-            for (int kk = 0; kk < DH / 16; ++kk)
-              mma_bf16(tmem + COL_S + (cs.g & 1) * KT, desc_kmajor_sw128(q_addr + kk * 32),
-                       desc_kmajor_sw128(k_addr + kk * 32), IDESC_S, kk != 0);
-            mma_commit(&s_full[cs.g & 1]);
-            if (cs.j == cs.it.n_kv - 1) mma_commit(&q_empty[qb]);  // Q free after its last S
-            advance(cs, false);
-            progressed = true;
-          }
-        }
-        seek(cp, true);
-        if (cp.have && mbar_test(&p_full[cp.g & 1], (cp.g >> 1) & 1)) {
-          fence_after_sync();
-          const uint32_t v_addr = smem_u32(sKV + cp.stage * 2 * KV_BYTES + KV_BYTES);
-#pragma unroll
-          for (int kk = 0; kk < KT / 16; ++kk)
-            mma_bf16_ts(tmem + COL_O, tmem + COL_P + (cp.g & 1) * (KT / 2) + kk * 8,
-                        desc_mnmajor_sw128(v_addr + kk * 16 * 128), IDESC_O,
-                        (cp.j > 0 || kk > 0) ? 1u : 0u);
-          mma_commit(&pv_done[cp.g & 1]);
-          mma_commit(&kv_empty[cp.stage]);
-          advance(cp, true);
-          progressed = true;
-        }
-        if (progressed) {
-          t_last = globaltimer();
-        } else if (globaltimer() - t_last > kWaitNs) {
-          record_err(err, 15);
-          abort_sh = 1;
-          break;
-        } else {
-          __nanosleep(20);
-        }
-      }
-      mma_commit(&drain);
-      if (!mbar_wait(&drain, 0)) record_err(err, 17);
-    }
-  } else {
-    // ---------------- softmax warps 0-3 ----------------
-    const int r = warp * 32 + lane;  // query row in the tile = TMEM lane
-    const float scale = 0.125f * 1.4426950408889634f;  // log2(e) / sqrt(64)
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-    const uint32_t tS = tmem + COL_S + lane_off, tO = tmem + COL_O + lane_off,
-                   tP = tmem + COL_P + lane_off;
-    uint32_t g = 0;
-    bool failed = false;
-    // bounded wait by lane 0, result broadcast to the warp
-    auto warp_wait = [&](uint64_t* bar, uint32_t parity) -> bool {
-      int okw = 1;
-      if (lane == 0) okw = mbar_wait(bar, parity) ? 1 : 0;
-      return __shfl_sync(0xffffffffu, okw, 0) != 0;
-    };
-    for (uint32_t ri = 0; !failed && !abort_sh; ++ri) {
-      const int slot = ri % RING;
-      if (!warp_wait(&it_full[slot], (ri / RING) & 1)) { failed = true; break; }
-      const Item it = ring[slot];
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&it_empty[slot]);
-      if (it.n_kv < 0) break;  // end of this CTA's list
-      const int i_q = it.q0 + r;
-      const bool live = i_q < it.n;
-      bf16* orow = O + (int64_t)(it.s0 + i_q) * H * DH + it.h * DH;
-      if (it.n_kv == 0) {  // no visible key at all: the reference's empty sum gives 0
-        if (live)
-          for (int q = 0; q < 8; ++q) reinterpret_cast<uint4*>(orow)[q] = make_uint4(0, 0, 0, 0);
+  // ---- loads (thread 0): K/V tiles in item order through the ring, Q per item ----
+  int lk = 0, lj = 0;          // next K/V tile to load: item lk, tile lj
+  uint32_t kv_issued = 0;      // K/V tiles loaded (tile t goes to stage t % KV_STAGES)
+  uint32_t kv_done = 0;        // K/V tiles whose arrival the MMA issuer has seen
+  uint32_t q_issued = 0, q_done = 0;
+  int q_item = -1;             // item whose Q is in the buffer or on its way
+  auto item_at = [&](int k) -> const Item& { return items[(k / CHUNK) & 1][k % CHUNK]; };
+  // K/V loads while a stage is free (`released` tiles have finished their P.V)
+  // and the item is decoded (chunks up to `chunk_hi`)
+  auto issue_kv = [&](uint32_t released, int chunk_hi) {
+    const int k_end = min(cnt, (chunk_hi + 1) * CHUNK);
+    while (kv_issued < released + KV_STAGES && lk < k_end) {
+      const Item& it = item_at(lk);
+      if (it.n_kv <= 0) {
+        ++lk;
+        lj = 0;
         continue;
       }
-      int lo = 0, hi = it.nk;
-      if (window > 0) {
-        lo = max(0, i_q - window);
-        hi = min(it.nk, i_q + window + 1);
+      const int stage = kv_issued % KV_STAGES;
+      const int row = it.s0 + (it.t_lo + lj) * KT;
+      uint8_t* dst = sKV + stage * 2 * KV_BYTES;
+      mbar_expect_tx(&kv_full[stage], 2 * KV_BYTES);
+      tma_load_2d(dst, &mapKV, &kv_full[stage], (H + it.h) * DH, row);
+      tma_load_2d(dst + KV_BYTES, &mapKV, &kv_full[stage], (2 * H + it.h) * DH, row);
+      ++kv_issued;
+      if (++lj == it.n_kv) {
+        ++lk;
+        lj = 0;
       }
-      float m_ref = -INFINITY, l = 0.f;
-      for (int j = 0; j < it.n_kv; ++j) {
-        const uint32_t gj = g + j;
-        if (!warp_wait(&s_full[gj & 1], (gj >> 1) & 1) || abort_sh) { failed = true; break; }
+    }
+  };
+  auto issue_q = [&](int k) {
+    const Item& it = item_at(k);
+    mbar_expect_tx(&q_full, Q_BYTES);
+    tma_load_2d(sQ, &mapQ, &q_full, it.h * DH, it.s0 + it.q0);
+    ++q_issued;
+    q_item = k;
+  };
+
+  // ---- per-thread state ----
+  const float scale = 0.125f * 1.4426950408889634f;  // log2(e) / sqrt(64)
+  const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+  const uint32_t tS = tmem + COL_S + lane_off, tO = tmem + COL_O + lane_off;
+  uint32_t g = 0;  // K/V tiles consumed (global over items)
+  int fail = 0;    // a wait ran out (uniform within each warp)
+  // bounded wait by lane 0, result broadcast to the warp (all 32 lanes call it)
+  auto warp_wait = [&](uint64_t* bar, uint32_t parity) -> bool {
+    int okw = 1;
+    if (lane == 0) okw = mbar_wait(bar, parity) ? 1 : 0;
+    return __shfl_sync(0xffffffffu, okw, 0) != 0;
+  };
+  // after a thread-0-only section: warp 0 reconverges and adopts thread 0's failure
+  auto leader_join = [&]() {
+    if (warp == 0) {
+      __syncwarp();
+      fail |= __shfl_sync(0xffffffffu, fail, 0);
+    }
+  };
+
+  for (int k = 0; k < cnt; ++k) {
+    if (k > 0 && k % CHUNK == 0) {
+      // entering chunk c: decode chunk c + 1 into the buffer chunk c - 1 used
+      if (__syncthreads_or(fail)) break;
+      decode_chunk(k / CHUNK + 1);
+      if (__syncthreads_or(fail)) break;
+    }
+    const int chunk_hi = k / CHUNK + 1;
+    const Item it = item_at(k);
+    if (it.n_kv < 0) continue;  // idle grid slot
+    const int i_q = it.q0 + tid;
+    const bool live = i_q < it.n;
+    bf16* orow = O + (int64_t)(it.s0 + i_q) * H * DH + it.h * DH;
+    if (it.n_kv == 0) {  // no visible key at all: the reference's empty sum gives 0
+      if (live)
+        for (int q = 0; q < 8; ++q) reinterpret_cast<uint4*>(orow)[q] = make_uint4(0, 0, 0, 0);
+      continue;
+    }
+    if (leader && !fail) {
+      if (q_item != k) issue_q(k);
+      if (lk < k) {  // items lk..k-1 had no tiles (their buffer may be reused)
+        lk = k;
+        lj = 0;
+      }
+      issue_kv(g, chunk_hi);  // at least this item's first tiles
+    }
+    leader_join();
+    int lo = 0, hi = it.nk;
+    if (window > 0) {
+      lo = max(0, i_q - window);
+      hi = min(it.nk, i_q + window + 1);
+    }
+    float m_ref = -INFINITY, l = 0.f;
+    bool broke = false;
+    for (int j = 0; j < it.n_kv; ++j, ++g) {
+      // S = Q K_j^T (thread 0)
+      if (leader && !fail) {
+        bool ok = true;
+        if (j == 0) {
+          ok = mbar_wait(&q_full, q_done & 1);
+          if (ok) ++q_done;
+        }
+        if (ok) {
+          ok = mbar_wait(&kv_full[g % KV_STAGES], (g / KV_STAGES) & 1);
+          if (ok) ++kv_done;
+        }
+        if (!ok) {
+          record_err(err, 10);
+          fail = 1;
+        } else {
+          fence_after_sync();
+          const uint32_t q_addr = smem_u32(sQ);
+          const uint32_t k_addr = smem_u32(sKV + (g % KV_STAGES) * 2 * KV_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < DH / 16; ++kk)
+            mma_bf16(tmem + COL_S, desc_kmajor_sw128(q_addr + kk * 32),
+                     desc_kmajor_sw128(k_addr + kk * 32), IDESC_S, kk != 0);
+          mma_commit(&s_full);
+        }
+      }
+      leader_join();
+      // softmax: S_j -> P_j (every thread, its row)
+      if (!fail && !warp_wait(&s_full, g & 1)) {
+        if (lane == 0) record_err(err, 11);
+        fail = 1;
+      }
+      if (!fail) {
         fence_after_sync();
         uint32_t ra[32], rb[32];
-        tmem_ld32(tS + (gj & 1) * KT, ra);
-        tmem_ld32(tS + (gj & 1) * KT + 32, rb);
+        tmem_ld32(tS, ra);
+        tmem_ld32(tS + 32, rb);
         tmem_ld_wait();
-        fence_before_sync();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&s_empty[gj & 1]);
         const int kbase = (it.t_lo + j) * KT;
         float t4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
         if (window == 0 && kbase + KT <= it.nk) {  // interior tile: every key visible
@@ -387,25 +319,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         const bool grow = !first && m_tile > m_ref + kRescaleLog2;
         const float m_new = (first || grow) ? m_tile : m_ref;
         const float m_use = m_new == -INFINITY ? 0.f : m_new;
-        if (__any_sync(0xffffffffu, grow) && j >= 1) {
-          // O holds P_0..P_{j-1} V against m_ref: rescale this warp's rows
-          if (!warp_wait(&pv_done[(gj - 1) & 1], ((gj - 1) >> 1) & 1)) { failed = true; break; }
-          fence_after_sync();
-          const float c = grow ? ex2(m_ref - m_new) : 1.f;
-          uint32_t oa[32], ob[32];
-          tmem_ld32(tO, oa);
-          tmem_ld32(tO + 32, ob);
-          tmem_ld_wait();
-#pragma unroll
-          for (int d = 0; d < 32; ++d) {
-            oa[d] = __float_as_uint(__uint_as_float(oa[d]) * c);
-            ob[d] = __float_as_uint(__uint_as_float(ob[d]) * c);
-          }
-          tmem_st32(tO, oa);
-          tmem_st32(tO + 32, ob);
-          tmem_st_wait();
-        }
-        if (grow) l *= ex2(m_ref - m_new);
+        const float resc = grow ? ex2(m_ref - m_new) : 1.f;
+        if (grow) l *= resc;
         m_ref = m_new;
         // P_j = 2^(s * scale - m_use), two exponentials per MUFU op (ex2 on
         // f16 pairs: arguments <= 8, results <= 256; P is rounded to bf16
@@ -422,52 +337,99 @@ __global__ void __launch_bounds__(kThreads, 2)
           pk[c >> 1] = *reinterpret_cast<uint32_t*>(&pb);
         }
         l += (r4[0] + r4[1]) + (r4[2] + r4[3]);
-        // P[gj%2] was last read by the P.V of tile gj-2
-        if (!warp_wait(&pv_done[gj & 1], ((gj >> 1) & 1) ^ 1)) { failed = true; break; }
-        tmem_st32(tP + (gj & 1) * (KT / 2), pk);
-        tmem_st_wait();
-        fence_before_sync();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&p_full[gj & 1]);
-      }
-      if (failed) break;
-      // the item's output: wait for its last P.V, then O / l
-      const uint32_t last = g + it.n_kv - 1;
-      if (!warp_wait(&pv_done[last & 1], (last >> 1) & 1)) { failed = true; break; }
-      fence_after_sync();
-      uint32_t oa[32], ob[32];
-      tmem_ld32(tO, oa);
-      tmem_ld32(tO + 32, ob);
-      tmem_ld_wait();
-      fence_before_sync();
-      g += it.n_kv;
-      if (live) {
-        const float inv = l > 0.f ? 1.f / l : 0.f;
+        tmem_st32(tS, pk);  // P over the first 32 columns of S (S is in registers)
+        if (__any_sync(0xffffffffu, grow) && j >= 1) {
+          // O holds P_0..P_{j-1} V against the old reference (the P.V of tile
+          // j - 1 is done: S_j was issued after it): rescale this warp's rows
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          uint32_t wv[4];
+          for (int half = 0; half < 2; ++half) {
+            uint32_t ov[32];
+            tmem_ld32(tO + 32 * half, ov);
+            tmem_ld_wait();
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int d = q * 8 + 2 * e;
-            const float a = __uint_as_float(d < 32 ? oa[d] : ob[d - 32]) * inv;
-            const float b2 = __uint_as_float(d + 1 < 32 ? oa[d + 1] : ob[d - 31]) * inv;
-            __nv_bfloat162 hb = __floats2bfloat162_rn(a, b2);
-            wv[e] = *reinterpret_cast<uint32_t*>(&hb);
+            for (int d = 0; d < 32; ++d) ov[d] = __float_as_uint(__uint_as_float(ov[d]) * resc);
+            tmem_st32(tO + 32 * half, ov);
           }
-          reinterpret_cast<uint4*>(orow)[q] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+        }
+        tmem_st_wait();
+      }
+      fence_before_sync();
+      if (__syncthreads_or(fail)) {
+        broke = true;
+        break;
+      }
+      // O += P_j V_j (thread 0), then the loads this frees
+      if (leader) {
+        fence_after_sync();
+        const uint32_t v_addr = smem_u32(sKV + (g % KV_STAGES) * 2 * KV_BYTES + KV_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < KT / 16; ++kk)
+          mma_bf16_ts(tmem + COL_O, tmem + COL_S + kk * 8,
+                      desc_mnmajor_sw128(v_addr + kk * 16 * 128), IDESC_O,
+                      (j > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(&pv_done);
+        if (j == it.n_kv - 1) {
+          // Q is free (this item's last S is done): load the next item's
+          const int k_end = min(cnt, (chunk_hi + 1) * CHUNK);
+          for (int k2 = k + 1; k2 < k_end; ++k2)
+            if (item_at(k2).n_kv > 0) {
+              issue_q(k2);
+              break;
+            }
+        }
+        if (!mbar_wait(&pv_done, g & 1)) {
+          record_err(err, 12);
+          fail = 1;
+        } else {
+          issue_kv(g + 1, chunk_hi);
         }
       }
+      leader_join();
     }
-    if (failed && lane == 0) {
-      record_err(err, 18);
-      abort_sh = 1;
+    if (broke) break;
+    // the item's output: wait for its last P.V (thread 0 already has: the
+    // phase is complete for it), then O / l
+    if (!fail && !warp_wait(&pv_done, (g - 1) & 1)) {
+      if (lane == 0) record_err(err, 13);
+      fail = 1;
+    }
+    if (fail) continue;  // carried to the next block-wide barrier
+    fence_after_sync();
+    uint32_t oa[32], ob[32];
+    tmem_ld32(tO, oa);
+    tmem_ld32(tO + 32, ob);
+    tmem_ld_wait();
+    fence_before_sync();
+    if (live) {
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        uint32_t wv[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int d = q * 8 + 2 * e;
+          const float a = __uint_as_float(d < 32 ? oa[d] : ob[d - 32]) * inv;
+          const float b2 = __uint_as_float(d + 1 < 32 ? oa[d + 1] : ob[d - 31]) * inv;
+          __nv_bfloat162 hb = __floats2bfloat162_rn(a, b2);
+          wv[e] = *reinterpret_cast<uint32_t*>(&hb);
+        }
+        reinterpret_cast<uint4*>(orow)[q] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+      }
     }
   }
 
+  // drain: every issued copy has landed and every MMA is done before TMEM and
+  // shared memory are released (at most one Q and KV_STAGES K/V loads are open)
+  if (leader) {
+    if (q_issued > q_done && !mbar_wait(&q_full, q_done & 1)) record_err(err, 14);
+    for (uint32_t t = kv_done; t < kv_issued; ++t)
+      if (!mbar_wait(&kv_full[t % KV_STAGES], (t / KV_STAGES) & 1)) record_err(err, 15);
+    mma_commit(&drain);
+    if (!mbar_wait(&drain, 0)) record_err(err, 16);
+  }
   fence_before_sync();
   __syncthreads();
-  if (warp == 5) {
-    __syncwarp();
+  if (warp == 0) {
     fence_after_sync();
     tmem_dealloc(tmem, TMEM_COLS);
   }
@@ -497,7 +459,7 @@ cudaError_t attn_tc(const bf16* qkv, const int32_t* cu, const int32_t* kv_lens, 
   const long long items = tiles ? (long long)n_tiles * H : (long long)B * nqt * H;
   if (items <= 0) return cudaSuccess;
   if (items > 0x7fffffff) return cudaErrorInvalidValue;
-  const int grid = (int)std::min<long long>(items, 2LL * sm_count());
+  const int grid = (int)std::min<long long>(items, (long long)kCtasPerSm * sm_count());
   attn_tc_kernel<<<grid, kThreads, SMEM_BYTES, st>>>(mq, mkv, cu, kv_lens, O, H, window, tiles,
                                                       (int)items, nqt, err);
   return cudaGetLastError();

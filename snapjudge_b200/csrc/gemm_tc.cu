@@ -15,7 +15,8 @@
 //                 STORE  C = bf16(acc + bias, act)           (act: GELU-erf / ReLU)
 //                 RESID  X += acc                            (fp32 residual stream)
 //                 GEGLU  G = bf16(gelu(acc_g) * acc_u)        (W tile = 128 gate rows
-//                                                             + 128 up rows of [Wg; Wu])
+//                                                             + 128 up rows of [Wg; Wu];
+//                                                             erf per A&S 7.1.26, packed fp32)
 //                 ROPE   QKV = bf16(rotate-half(acc)) on q/k heads of 64, v as is
 // The epilogue of tile i overlaps the MMAs of tile i+1 (double-buffered TMEM).
 // Every mbarrier wait is bounded; a wait that runs out records an error code
@@ -76,6 +77,71 @@ __device__ __forceinline__ float act_fn(float v, int act) {
   if (act == ACT_GELU) return gelu_erf(v);
   if (act == ACT_RELU) return fmaxf(v, 0.f);
   return v;
+}
+
+// ---- GEGLU gate on column pairs, packed fp32 (fma/mul .f32x2) ----
+// erf by Abramowitz & Stegun, Handbook of Mathematical Functions, eq. 7.1.26:
+//   erfc(z) = (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-z^2),
+//   t = 1 / (1 + p z), z >= 0, |error| <= 1.5e-7,
+// with z = |x| / sqrt(2), so 1 - Phi(|x|) = erfc(z) / 2 and
+//   gelu(x) = x Phi(x) = relu(x) - |x| (1 - Phi(|x|)).
+// The reciprocal and exponential are the approximate hardware ones (relative
+// error ~2^-22); the gate is then rounded to bf16, so the result matches the
+// erf GELU to within one bf16 rounding step.
+typedef unsigned long long f32x2;
+__device__ __forceinline__ f32x2 pk2(float a, float b) {
+  f32x2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float2 unpk2(f32x2 v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ f32x2 fma2(f32x2 a, f32x2 b, f32x2 c) {
+  f32x2 d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ f32x2 mul2(f32x2 a, f32x2 b) {
+  f32x2 d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ f32x2 splat2(float a) { return pk2(a, a); }
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// (gelu(ga) * ua, gelu(gb) * ub)
+__device__ __forceinline__ float2 geglu_pair(float ga, float gb, float ua, float ub) {
+  constexpr float kP = 0.3275911f * 0.70710678118654752f;  // p / sqrt(2)
+  // -a_i / 2: the polynomial comes out as -erfc(z) / 2 before the exponential
+  constexpr float kA1 = -0.5f * 0.254829592f, kA2 = 0.5f * 0.284496736f,
+                  kA3 = -0.5f * 1.421413741f, kA4 = 0.5f * 1.453152027f,
+                  kA5 = -0.5f * 1.061405429f;
+  constexpr float kE = -0.5f * 1.4426950408889634f;  // -z^2 log2(e) = x^2 * kE
+  const f32x2 ax = pk2(fabsf(ga), fabsf(gb));
+  const float2 d = unpk2(fma2(ax, splat2(kP), splat2(1.f)));
+  const f32x2 t = pk2(rcp_approx(d.x), rcp_approx(d.y));
+  f32x2 p = fma2(t, splat2(kA5), splat2(kA4));
+  p = fma2(t, p, splat2(kA3));
+  p = fma2(t, p, splat2(kA2));
+  p = fma2(t, p, splat2(kA1));
+  p = mul2(p, t);
+  const f32x2 g = pk2(ga, gb);
+  const float2 e = unpk2(mul2(mul2(g, g), splat2(kE)));
+  const f32x2 h = mul2(p, pk2(ex2_approx(e.x), ex2_approx(e.y)));  // -(1 - Phi(|x|))
+  const f32x2 gelu = fma2(ax, h, pk2(fmaxf(ga, 0.f), fmaxf(gb, 0.f)));
+  return unpk2(mul2(gelu, pk2(ua, ub)));
 }
 
 __device__ __forceinline__ void store_bf16x32(bf16* dst, const float* v) {
@@ -325,8 +391,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_ld32(tacc + HALF + c + 32 * k2, r1);
             tmem_ld_wait();
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              v[32 * k2 + j] = gelu_erf(__uint_as_float(r0[j])) * __uint_as_float(r1[j]);
+            for (int j = 0; j < 32; j += 2) {
+              const float2 o = geglu_pair(__uint_as_float(r0[j]), __uint_as_float(r0[j + 1]),
+                                          __uint_as_float(r1[j]), __uint_as_float(r1[j + 1]));
+              v[32 * k2 + j] = o.x;
+              v[32 * k2 + j + 1] = o.y;
+            }
           }
           store_chunk(v, col_base + c, m0 + q * 32);
         }
@@ -340,8 +410,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld_wait();
           float v[32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
-            v[j] = gelu_erf(__uint_as_float(r0[j])) * __uint_as_float(r1[j]);
+          for (int j = 0; j < 32; j += 2) {
+            const float2 o = geglu_pair(__uint_as_float(r0[j]), __uint_as_float(r0[j + 1]),
+                                        __uint_as_float(r1[j]), __uint_as_float(r1[j + 1]));
+            v[j] = o.x;
+            v[j + 1] = o.y;
+          }
           if (live) store_bf16x32(ep.C + (int64_t)row * ep.ldc + col_base + c, v);
         }
       } else if (EPI == TC_ROPE) {
