@@ -16,9 +16,14 @@
 //     current item's last S is computed), K/V tiles of 64 keys through a
 //     2-stage ring that runs on across items;
 //     S = Q K^T (M=128, N=64, K=64) into TMEM, then O += P V with P read from
-//     TMEM (the A operand) and V from shared memory (MN-major).
+//     TMEM (the A operand) and V from shared memory (MN-major); the next S
+//     (of this item, or of the next one once its Q is in) is issued as soon
+//     as the P.V completes, before the loads that P.V frees.
 //   TMEM (128 columns): S (fp32, 64) — P (bf16 pairs) overwrites its first 32
 //   columns once S is in registers — and O (fp32, 64).
+// Without a window every row of a tile sees the same keys [kbase, kbase +
+// lim): a tile with lim <= 32 (short segments, last tiles) exponentiates 32
+// columns and its P.V runs over 32 keys.
 // Rescaling: each row keeps a reference max m_ref for its exponentials and
 // moves it only when a tile's max exceeds it by more than 2^8 (exponent 8 in
 // log2 units); then the row's O (in TMEM) and running sum are multiplied by
@@ -69,17 +74,85 @@ __device__ __forceinline__ float ex2(float x) {  // 2^x on the MUFU (ex2.approx,
   return y;
 }
 
-// (2^a, 2^b) with one MUFU op: pack to f16 pairs, ex2.approx.f16x2, unpack.
-__device__ __forceinline__ float2 ex2_pair(float a, float b) {
-  uint32_t h;
-  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(b), "f"(a));  // low half = a
-  asm("ex2.approx.f16x2 %0, %1;" : "=r"(h) : "r"(h));
+// ---- packed fp32 pairs (fma/add .f32x2) ----
+typedef unsigned long long f32x2;
+__device__ __forceinline__ f32x2 pk2(float a, float b) {
+  f32x2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float2 unpk2(f32x2 v) {
   float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ f32x2 fma2(f32x2 a, f32x2 b, f32x2 c) {
+  f32x2 d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ f32x2 add2(f32x2 a, f32x2 b) {
+  f32x2 d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x on both halves with one MUFU op: pack to f16 pairs, ex2.approx.f16x2, unpack.
+__device__ __forceinline__ f32x2 ex2_pair(f32x2 x) {
+  const float2 v = unpk2(x);
+  uint32_t h;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(v.y), "f"(v.x));  // low half = v.x
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(h) : "r"(h));
+  float a, b;
   asm("{\n\t.reg .f16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
       "cvt.f32.f16 %0, lo;\n\tcvt.f32.f16 %1, hi;\n\t}"
-      : "=f"(r.x), "=f"(r.y)
+      : "=f"(a), "=f"(b)
       : "r"(h));
-  return r;
+  return pk2(a, b);
+}
+
+// Row halves of 32 S columns (thread = row).  Columns at or past `lim`
+// (relative to the half) become -inf; with a window, those outside
+// [lo, hi) (relative) do.
+__device__ __forceinline__ void mask_hi(uint32_t (&r)[32], int lim) {
+#pragma unroll
+  for (int c = 0; c < 32; ++c)
+    if (c >= lim) r[c] = __float_as_uint(-INFINITY);
+}
+__device__ __forceinline__ void mask_lohi(uint32_t (&r)[32], int lo, int hi) {
+#pragma unroll
+  for (int c = 0; c < 32; ++c)
+    if (c < lo || c >= hi) r[c] = __float_as_uint(-INFINITY);
+}
+__device__ __forceinline__ float max32(const uint32_t (&r)[32]) {
+  float a = -INFINITY, b = -INFINITY, c = -INFINITY, d = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < 32; i += 8) {
+    a = max3(a, __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
+    b = max3(b, __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
+    c = max3(c, __uint_as_float(r[i + 4]), __uint_as_float(r[i + 5]));
+    d = max3(d, __uint_as_float(r[i + 6]), __uint_as_float(r[i + 7]));
+  }
+  return max3(a, b, fmaxf(c, d));
+}
+// P = 2^(s * scale - m) for 32 columns -> 16 bf16 pairs; fp32 row sums in acc0/acc1
+__device__ __forceinline__ void exp32(const uint32_t (&r)[32], f32x2 scale2, f32x2 negm2,
+                                      uint32_t* pk, f32x2& acc0, f32x2& acc1) {
+#pragma unroll
+  for (int c = 0; c < 32; c += 2) {
+    const f32x2 x = fma2(pk2(__uint_as_float(r[c]), __uint_as_float(r[c + 1])), scale2, negm2);
+    const f32x2 p = ex2_pair(x);
+    if ((c >> 1) & 1) acc1 = add2(acc1, p);
+    else acc0 = add2(acc0, p);
+    const float2 pf = unpk2(p);
+    __nv_bfloat162 pb = __floats2bfloat162_rn(pf.x, pf.y);
+    pk[c >> 1] = *reinterpret_cast<uint32_t*>(&pb);
+  }
 }
 
 struct __align__(16) Item {
@@ -167,11 +240,23 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   const uint32_t tmem = tmem_sh;
 
   // ---- loads (thread 0): K/V tiles in item order through the ring, Q per item ----
-  int lk = 0, lj = 0;          // next K/V tile to load: item lk, tile lj
-  uint32_t kv_issued = 0;      // K/V tiles loaded (tile t goes to stage t % KV_STAGES)
-  uint32_t kv_done = 0;        // K/V tiles whose arrival the MMA issuer has seen
-  uint32_t q_issued = 0, q_done = 0;
-  int q_item = -1;             // item whose Q is in the buffer or on its way
+  // thread 0's bookkeeping lives in shared memory (no registers in the other threads)
+  __shared__ struct {
+    int lk, lj;            // next K/V tile to load: item lk, tile lj
+    uint32_t kv_issued;    // K/V tiles loaded (tile t goes to stage t % KV_STAGES)
+    uint32_t kv_done;      // K/V tiles whose arrival the MMA issuer has seen
+    uint32_t q_issued, q_done;
+    int q_item;            // item whose Q is in the buffer or on its way
+    uint32_t s_issued;     // S computed or on its way for tiles < s_issued
+  } ls;
+  if (leader) {
+    ls.lk = ls.lj = 0;
+    ls.kv_issued = ls.kv_done = ls.q_issued = ls.q_done = ls.s_issued = 0;
+    ls.q_item = -1;
+  }
+  int &lk = ls.lk, &lj = ls.lj, &q_item = ls.q_item;
+  uint32_t &kv_issued = ls.kv_issued, &kv_done = ls.kv_done, &q_issued = ls.q_issued,
+           &q_done = ls.q_done, &s_issued = ls.s_issued;
   auto item_at = [&](int k) -> const Item& { return items[(k / CHUNK) & 1][k % CHUNK]; };
   // K/V loads while a stage is free (`released` tiles have finished their P.V)
   // and the item is decoded (chunks up to `chunk_hi`)
@@ -203,6 +288,25 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     tma_load_2d(sQ, &mapQ, &q_full, it.h * DH, it.s0 + it.q0);
     ++q_issued;
     q_item = k;
+  };
+  // S of K/V tile t (the first of its item: wait for Q too); false if a wait ran out
+  auto issue_s = [&](bool first, uint32_t t) -> bool {
+    if (first) {
+      if (!mbar_wait(&q_full, q_done & 1)) return false;
+      ++q_done;
+    }
+    if (!mbar_wait(&kv_full[t % KV_STAGES], (t / KV_STAGES) & 1)) return false;
+    ++kv_done;
+    fence_after_sync();
+    const uint32_t q_addr = smem_u32(sQ);
+    const uint32_t k_addr = smem_u32(sKV + (t % KV_STAGES) * 2 * KV_BYTES);
+#pragma unroll
+    for (int kk = 0; kk < DH / 16; ++kk)
+      mma_bf16(tmem + COL_S, desc_kmajor_sw128(q_addr + kk * 32),
+               desc_kmajor_sw128(k_addr + kk * 32), IDESC_S, kk != 0);
+    mma_commit(&s_full);
+    s_issued = t + 1;
+    return true;
   };
 
   // ---- per-thread state ----
@@ -260,29 +364,16 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     float m_ref = -INFINITY, l = 0.f;
     bool broke = false;
     for (int j = 0; j < it.n_kv; ++j, ++g) {
-      // S = Q K_j^T (thread 0)
-      if (leader && !fail) {
-        bool ok = true;
-        if (j == 0) {
-          ok = mbar_wait(&q_full, q_done & 1);
-          if (ok) ++q_done;
-        }
-        if (ok) {
-          ok = mbar_wait(&kv_full[g % KV_STAGES], (g / KV_STAGES) & 1);
-          if (ok) ++kv_done;
-        }
-        if (!ok) {
+      // this tile's visible keys: without a window, [kbase, kbase + lim) for
+      // every row (uniform); a tile with lim <= 32 uses its first 32 columns
+      const int kbase = (it.t_lo + j) * KT;
+      const int lim = window == 0 ? min(KT, it.nk - kbase) : KT;
+      const bool two = lim > 32;
+      // S = Q K_j^T (thread 0), unless issued right after the previous P.V
+      if (leader && !fail && s_issued <= g) {
+        if (!issue_s(j == 0, g)) {
           record_err(err, 10);
           fail = 1;
-        } else {
-          fence_after_sync();
-          const uint32_t q_addr = smem_u32(sQ);
-          const uint32_t k_addr = smem_u32(sKV + (g % KV_STAGES) * 2 * KV_BYTES);
-#pragma unroll
-          for (int kk = 0; kk < DH / 16; ++kk)
-            mma_bf16(tmem + COL_S, desc_kmajor_sw128(q_addr + kk * 32),
-                     desc_kmajor_sw128(k_addr + kk * 32), IDESC_S, kk != 0);
-          mma_commit(&s_full);
         }
       }
       leader_join();
@@ -291,29 +382,31 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         if (lane == 0) record_err(err, 11);
         fail = 1;
       }
+      if (leader && !fail && j == it.n_kv - 1) {
+        // Q is free (this item's last S is done): load the next item's
+        const int k_end = min(cnt, (chunk_hi + 1) * CHUNK);
+        for (int k2 = k + 1; k2 < k_end; ++k2)
+          if (item_at(k2).n_kv > 0) {
+            issue_q(k2);
+            break;
+          }
+      }
       if (!fail) {
         fence_after_sync();
         uint32_t ra[32], rb[32];
         tmem_ld32(tS, ra);
-        tmem_ld32(tS + 32, rb);
+        if (two) tmem_ld32(tS + 32, rb);
         tmem_ld_wait();
-        const int kbase = (it.t_lo + j) * KT;
-        float t4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-        if (window == 0 && kbase + KT <= it.nk) {  // interior tile: every key visible
-#pragma unroll
-          for (int c = 0; c < KT; ++c)
-            t4[c & 3] = fmaxf(t4[c & 3], __uint_as_float(c < 32 ? ra[c] : rb[c - 32]));
+        if (window == 0) {
+          if (lim < 32) mask_hi(ra, lim);
+          if (two && lim < KT) mask_hi(rb, lim - 32);
         } else {
-#pragma unroll
-          for (int c = 0; c < KT; ++c) {
-            const int key = kbase + c;
-            uint32_t& cell = c < 32 ? ra[c] : rb[c - 32];
-            const float v = (key >= lo && key < hi) ? __uint_as_float(cell) : -INFINITY;
-            cell = __float_as_uint(v);
-            t4[c & 3] = fmaxf(t4[c & 3], v);
-          }
+          mask_lohi(ra, lo - kbase, hi - kbase);
+          mask_lohi(rb, lo - kbase - 32, hi - kbase - 32);
         }
-        const float m_tile = fmaxf(fmaxf(t4[0], t4[1]), fmaxf(t4[2], t4[3])) * scale;
+        float mt = max32(ra);
+        if (two) mt = fmaxf(mt, max32(rb));
+        const float m_tile = mt * scale;
         // move the reference max on the first visible tile, or when exceeded by 2^8
         const bool first = m_ref == -INFINITY;
         const bool grow = !first && m_tile > m_ref + kRescaleLog2;
@@ -325,19 +418,18 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         // P_j = 2^(s * scale - m_use), two exponentials per MUFU op (ex2 on
         // f16 pairs: arguments <= 8, results <= 256; P is rounded to bf16
         // afterwards, below f16's precision); fp32 row sum
-        float r4[4] = {0.f, 0.f, 0.f, 0.f};
-        uint32_t pk[32];
-#pragma unroll
-        for (int c = 0; c < KT; c += 2) {
-          const float x0 = fmaf(__uint_as_float(c < 32 ? ra[c] : rb[c - 32]), scale, -m_use);
-          const float x1 = fmaf(__uint_as_float(c + 1 < 32 ? ra[c + 1] : rb[c - 31]), scale, -m_use);
-          const float2 p = ex2_pair(x0, x1);
-          r4[(c >> 1) & 3] += p.x + p.y;
-          __nv_bfloat162 pb = __floats2bfloat162_rn(p.x, p.y);
-          pk[c >> 1] = *reinterpret_cast<uint32_t*>(&pb);
+        const f32x2 scale2 = pk2(scale, scale), negm2 = pk2(-m_use, -m_use);
+        f32x2 acc0 = pk2(0.f, 0.f), acc1 = pk2(0.f, 0.f);
+        // P over the first 16 (32) columns of S, which is in registers
+        uint32_t pk[16];
+        exp32(ra, scale2, negm2, pk, acc0, acc1);
+        tmem_st16(tS, pk);
+        if (two) {
+          exp32(rb, scale2, negm2, pk, acc0, acc1);
+          tmem_st16(tS + 16, pk);
         }
-        l += (r4[0] + r4[1]) + (r4[2] + r4[3]);
-        tmem_st32(tS, pk);  // P over the first 32 columns of S (S is in registers)
+        const float2 s0 = unpk2(acc0), s1 = unpk2(acc1);
+        l += (s0.x + s0.y) + (s1.x + s1.y);
         if (__any_sync(0xffffffffu, grow) && j >= 1) {
           // O holds P_0..P_{j-1} V against the old reference (the P.V of tile
           // j - 1 is done: S_j was issued after it): rescale this warp's rows
@@ -358,30 +450,33 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         broke = true;
         break;
       }
-      // O += P_j V_j (thread 0), then the loads this frees
+      // O += P_j V_j (thread 0; 32 keys when the tile's second half is
+      // empty), then the next S at once, then the loads the P.V frees
       if (leader) {
         fence_after_sync();
         const uint32_t v_addr = smem_u32(sKV + (g % KV_STAGES) * 2 * KV_BYTES + KV_BYTES);
+        const int ksteps = two ? KT / 16 : 2;
 #pragma unroll
         for (int kk = 0; kk < KT / 16; ++kk)
-          mma_bf16_ts(tmem + COL_O, tmem + COL_S + kk * 8,
-                      desc_mnmajor_sw128(v_addr + kk * 16 * 128), IDESC_O,
-                      (j > 0 || kk > 0) ? 1u : 0u);
+          if (kk < ksteps)
+            mma_bf16_ts(tmem + COL_O, tmem + COL_S + kk * 8,
+                        desc_mnmajor_sw128(v_addr + kk * 16 * 128), IDESC_O,
+                        (j > 0 || kk > 0) ? 1u : 0u);
         mma_commit(&pv_done);
-        if (j == it.n_kv - 1) {
-          // Q is free (this item's last S is done): load the next item's
-          const int k_end = min(cnt, (chunk_hi + 1) * CHUNK);
-          for (int k2 = k + 1; k2 < k_end; ++k2)
-            if (item_at(k2).n_kv > 0) {
-              issue_q(k2);
-              break;
-            }
-        }
         if (!mbar_wait(&pv_done, g & 1)) {
           record_err(err, 12);
           fail = 1;
         } else {
-          issue_kv(g + 1, chunk_hi);
+          // tile g + 1 belongs to this item or to the item whose Q is loading;
+          // issue its S now if its K/V load is out (and, for a new item, its Q is in)
+          const bool same = j + 1 < it.n_kv;
+          bool go = kv_issued > g + 1 && (same || q_item > k);
+          if (go && !same) go = mbar_test(&q_full, q_done & 1);
+          if (go && !issue_s(!same, g + 1)) {
+            record_err(err, 10);
+            fail = 1;
+          }
+          if (!fail) issue_kv(g + 1, chunk_hi);
         }
       }
       leader_join();
