@@ -239,24 +239,31 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   fence_after_sync();
   const uint32_t tmem = tmem_sh;
 
-  // ---- loads (thread 0): K/V tiles in item order through the ring, Q per item ----
-  // thread 0's bookkeeping lives in shared memory (no registers in the other threads)
+  // ---- loads (thread 96, the loader): K/V tiles in item order through the
+  // ring, Q per item; MMAs (thread 0).  Both keep their bookkeeping in shared
+  // memory (no registers in the other threads); thread 0 reads the loader's
+  // counters (volatile, monotonic) only to decide whether a load is out.
   __shared__ struct {
-    int lk, lj;            // next K/V tile to load: item lk, tile lj
-    uint32_t kv_issued;    // K/V tiles loaded (tile t goes to stage t % KV_STAGES)
-    uint32_t kv_done;      // K/V tiles whose arrival the MMA issuer has seen
-    uint32_t q_issued, q_done;
-    int q_item;            // item whose Q is in the buffer or on its way
-    uint32_t s_issued;     // S computed or on its way for tiles < s_issued
+    int lk, lj;            // loader: next K/V tile to load: item lk, tile lj
+    uint32_t kv_issued;    // loader: K/V tiles loaded (tile t goes to stage t % KV_STAGES)
+    uint32_t q_issued;     // loader: Q loads
+    int q_item;            // loader: item whose Q is in the buffer or on its way
+    uint32_t kv_done;      // thread 0: K/V tiles whose arrival it has seen
+    uint32_t q_done;       // thread 0: Q loads whose arrival it has seen
+    uint32_t s_issued;     // thread 0: S computed or on its way for tiles < s_issued
   } ls;
+  const bool loader = tid == 96;  // lane 0 of warp 3
   if (leader) {
     ls.lk = ls.lj = 0;
     ls.kv_issued = ls.kv_done = ls.q_issued = ls.q_done = ls.s_issued = 0;
     ls.q_item = -1;
   }
+  __syncthreads();
   int &lk = ls.lk, &lj = ls.lj, &q_item = ls.q_item;
   uint32_t &kv_issued = ls.kv_issued, &kv_done = ls.kv_done, &q_issued = ls.q_issued,
            &q_done = ls.q_done, &s_issued = ls.s_issued;
+  auto kv_out = [&]() { return *reinterpret_cast<volatile uint32_t*>(&ls.kv_issued); };
+  auto q_out_item = [&]() { return *reinterpret_cast<volatile int*>(&ls.q_item); };
   auto item_at = [&](int k) -> const Item& { return items[(k / CHUNK) & 1][k % CHUNK]; };
   // K/V loads while a stage is free (`released` tiles have finished their P.V)
   // and the item is decoded (chunks up to `chunk_hi`)
@@ -308,6 +315,15 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     s_issued = t + 1;
     return true;
   };
+  // Q for the first active item after k within the decoded chunks (loader)
+  auto prefetch_q = [&](int k, int chunk_hi) {
+    const int k_end = min(cnt, (chunk_hi + 1) * CHUNK);
+    for (int k2 = k + 1; k2 < k_end; ++k2)
+      if (item_at(k2).n_kv > 0) {
+        issue_q(k2);
+        break;
+      }
+  };
 
   // ---- per-thread state ----
   const float scale = 0.125f * 1.4426950408889634f;  // log2(e) / sqrt(64)
@@ -321,9 +337,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     if (lane == 0) okw = mbar_wait(bar, parity) ? 1 : 0;
     return __shfl_sync(0xffffffffu, okw, 0) != 0;
   };
-  // after a thread-0-only section: warp 0 reconverges and adopts thread 0's failure
-  auto leader_join = [&]() {
-    if (warp == 0) {
+  // after a section run by lane 0 of warp w alone (thread 0: w = 0, the
+  // loader: w = 3): the warp reconverges and adopts lane 0's failure
+  auto join = [&](int w) {
+    if (warp == w) {
       __syncwarp();
       fail |= __shfl_sync(0xffffffffu, fail, 0);
     }
@@ -347,7 +364,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         for (int q = 0; q < 8; ++q) reinterpret_cast<uint4*>(orow)[q] = make_uint4(0, 0, 0, 0);
       continue;
     }
-    if (leader && !fail) {
+    if (loader && !fail) {
       if (q_item != k) issue_q(k);
       if (lk < k) {  // items lk..k-1 had no tiles (their buffer may be reused)
         lk = k;
@@ -355,7 +372,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       }
       issue_kv(g, chunk_hi);  // at least this item's first tiles
     }
-    leader_join();
+    join(3);
     int lo = 0, hi = it.nk;
     if (window > 0) {
       lo = max(0, i_q - window);
@@ -376,21 +393,15 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
           fail = 1;
         }
       }
-      leader_join();
+      join(0);
       // softmax: S_j -> P_j (every thread, its row)
       if (!fail && !warp_wait(&s_full, g & 1)) {
         if (lane == 0) record_err(err, 11);
         fail = 1;
       }
-      if (leader && !fail && j == it.n_kv - 1) {
-        // Q is free (this item's last S is done): load the next item's
-        const int k_end = min(cnt, (chunk_hi + 1) * CHUNK);
-        for (int k2 = k + 1; k2 < k_end; ++k2)
-          if (item_at(k2).n_kv > 0) {
-            issue_q(k2);
-            break;
-          }
-      }
+      // Q is free once this item's last S is done: the loader fetches the next item's
+      if (loader && !fail && j == it.n_kv - 1) prefetch_q(k, chunk_hi);
+      join(3);
       if (!fail) {
         fence_after_sync();
         uint32_t ra[32], rb[32];
@@ -451,7 +462,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         break;
       }
       // O += P_j V_j (thread 0; 32 keys when the tile's second half is
-      // empty), then the next S at once, then the loads the P.V frees
+      // empty), then the next S at once; the loader issues the loads the
+      // P.V frees
       if (leader) {
         fence_after_sync();
         const uint32_t v_addr = smem_u32(sKV + (g % KV_STAGES) * 2 * KV_BYTES + KV_BYTES);
@@ -468,18 +480,27 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
           fail = 1;
         } else {
           // tile g + 1 belongs to this item or to the item whose Q is loading;
-          // issue its S now if its K/V load is out (and, for a new item, its Q is in)
+          // issue its S now if the loader has its K/V load out (and, for a
+          // new item, its Q is in)
           const bool same = j + 1 < it.n_kv;
-          bool go = kv_issued > g + 1 && (same || q_item > k);
+          bool go = kv_out() > g + 1 && (same || q_out_item() > k);
           if (go && !same) go = mbar_test(&q_full, q_done & 1);
           if (go && !issue_s(!same, g + 1)) {
             record_err(err, 10);
             fail = 1;
           }
-          if (!fail) issue_kv(g + 1, chunk_hi);
         }
       }
-      leader_join();
+      join(0);
+      if (loader) {
+        if (!mbar_wait(&pv_done, g & 1)) {
+          record_err(err, 12);
+          fail = 1;
+        } else {
+          issue_kv(g + 1, chunk_hi);
+        }
+      }
+      join(3);
     }
     if (broke) break;
     // the item's output: wait for its last P.V (thread 0 already has: the
@@ -514,7 +535,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   }
 
   // drain: every issued copy has landed and every MMA is done before TMEM and
-  // shared memory are released (at most one Q and KV_STAGES K/V loads are open)
+  // shared memory are released (at most one Q and KV_STAGES K/V loads are open;
+  // the barrier makes the loader's counters visible to thread 0)
+  __syncthreads();
   if (leader) {
     if (q_issued > q_done && !mbar_wait(&q_full, q_done & 1)) record_err(err, 14);
     for (uint32_t t = kv_done; t < kv_issued; ++t)
