@@ -155,6 +155,26 @@ int sj_fast_encode(sj_fast* e, const int64_t* ids, const int32_t* cu_seqlens,
 int sj_fast_decide(sj_fast* e, const int64_t* ids, const int32_t* cu_seqlens, int B,
                    float* probs);
 
+/* The whole DecisionModel::forward (src/model.cpp:309-536) on the GPU, host
+ * buffers (synchronous): the encoder, then the decision-model tail — type
+ * embedding, the head TransformerEncoderLayers, the scorer on the marker rows
+ * and the act head (:402-535).  Replaces the reference fast path's forward
+ * (include/snapjudge/fast.hpp:24-30, cuda/fast.cpp:170-267) behind
+ * FastSnapjudge::forward.  Needs the checkpoint's type_emb.weight,
+ * head.layers.*, scorer.* and act_head.* tensors (set before commit).
+ * Inputs as sj_fast_encode (a padded [B, L] batch is B segments of length L
+ * with kv_lens = the attention-mask lengths); marker_pos int64 [B, K]
+ * (clamped to the segment), marker_mask uint8 [B, K], qtype int64 [B] in
+ * [0, 3).  Outputs: logits fp32 [B, K] (masked markers -1e4), act fp32
+ * [B, n_act] (sj_fast_n_act). */
+int sj_fast_forward(sj_fast* e, const int64_t* ids, const int32_t* cu_seqlens,
+                    const int32_t* kv_lens, int B, const int64_t* marker_pos,
+                    const uint8_t* marker_mask, int K, const int64_t* qtype, float* logits,
+                    float* act);
+
+/* Outputs of the act head (0 when the engine has no decision-model head). */
+int sj_fast_n_act(const sj_fast* e);
+
 /* Device-buffer variants, asynchronous on `stream` (NULL = the engine's
  * stream).  T = cu_seqlens_host[B] must not exceed the engine's max_tokens.
  * cu_seqlens_host mirrors the device array (it sizes the launches).

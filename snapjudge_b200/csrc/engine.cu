@@ -60,6 +60,24 @@ struct LayerDev {
   bool sliding = false;
 };
 
+// One pre-norm TransformerEncoderLayer of the decision head (model.cpp:134-152):
+// LN weights/biases and GEMM biases fp32, GEMM weights in the activation precision.
+struct HeadLayerDev {
+  float *n1w = nullptr, *n1b = nullptr, *n2w = nullptr, *n2b = nullptr;
+  void *in_w = nullptr, *out_w = nullptr, *l1w = nullptr, *l2w = nullptr;  // [3D,D] [D,D] [4D,D] [D,4D]
+  float *in_b = nullptr, *out_b = nullptr, *l1b = nullptr, *l2b = nullptr;
+};
+
+// Per-pass device inputs and outputs of the decision-model tail.
+struct DmPass {
+  const int64_t* qtype;   // [B]
+  const int64_t* pos;     // [B, K]
+  const uint8_t* mask;    // [B, K]
+  int K;
+  float* logits;          // [B, K]
+  float* act;             // [B, n_act]
+};
+
 }  // namespace
 
 struct sj_fast {
@@ -87,6 +105,21 @@ struct sj_fast {
   sjb::HeadSpec spec{};
   bool has_heads = false;
   float *head_w = nullptr, *head_b = nullptr;
+  // decision-model tail of DecisionModel::forward (model.cpp:402-535)
+  bool has_dm = false;
+  int n_act = 0;
+  std::vector<HeadLayerDev> hlayers;
+  float* type_emb = nullptr;  // [3, D]
+  float *sc_lnw = nullptr, *sc_lnb = nullptr, *sc_w1 = nullptr, *sc_b1 = nullptr,
+        *sc_w2 = nullptr, *sc_b2 = nullptr;
+  float *act_w1 = nullptr, *act_b1 = nullptr, *act_w2 = nullptr, *act_b2 = nullptr;
+  // its per-call buffers, grown on demand: marker rows [BK, D] x 3, scores [BK],
+  // logits [BK], act [B, n_act], and the inputs
+  size_t dm_cap_bk = 0, dm_cap_b = 0;
+  float *dm_m = nullptr, *dm_s = nullptr, *dm_s1 = nullptr, *dm_s2 = nullptr,
+        *dm_logits = nullptr, *dm_act = nullptr;
+  int64_t *dm_pos = nullptr, *dm_qt = nullptr;
+  uint8_t* dm_mask = nullptr;
 
   // workspace
   float* X = nullptr;
@@ -221,12 +254,32 @@ struct sj_fast {
   template <typename T>
   int forward(const int64_t* d_ids, const int32_t* d_cu, const int32_t* hcu,
               const int32_t* d_kvl, int B, int ntok, float* d_hidden, float* d_probs,
-              cudaStream_t st);
+              const DmPass* dm, cudaStream_t st);
+  template <typename T>
+  int head_forward(const int32_t* d_cu, const int32_t* d_kvl, int B, int ntok, int nt,
+                   float* h, const DmPass& dm, cudaStream_t st);
+  template <typename T>
+  int gemm_any(int cls, const T* A, const void* W, const float* bias, int act, T* C,
+               float* resid, int M, int N, int K, int epi, const float* ct, const float* stb,
+               cudaStream_t st);
   int run(const int64_t* d_ids, const int32_t* d_cu, const int32_t* hcu, const int32_t* d_kvl,
-          int B, float* d_hidden, float* d_probs, cudaStream_t st);
+          int B, float* d_hidden, float* d_probs, const DmPass* dm, cudaStream_t st);
   int check_flags(cudaStream_t st);
   int host_call(const int64_t* ids_h, const int32_t* cu_h, const int32_t* kvl_h, int B,
                 float* hidden_h, float* probs_h);
+  int dm_call(const int64_t* ids_h, const int32_t* cu_h, const int32_t* kvl_h, int B,
+              const int64_t* pos_h, const uint8_t* mask_h, int K, const int64_t* qtype_h,
+              float* logits_h, float* act_h);
+  template <typename P>
+  cudaError_t grow(P** p, size_t n) {  // replace *p by a buffer of n elements
+    if (*p) {
+      auto it = std::find(allocs.begin(), allocs.end(), static_cast<void*>(*p));
+      if (it != allocs.end()) allocs.erase(it);
+      cudaFree(*p);
+      *p = nullptr;
+    }
+    return dalloc(p, n);
+  }
 };
 
 // ------------------------------------------------------------------ commit
@@ -307,12 +360,71 @@ int sj_fast::commit() {
     if ((s = upload_f32(&w, &head_w))) return s;
     if ((s = upload_f32(&b, &head_b))) return s;
   }
+  // decision-model tail (model.cpp:130-176), when the checkpoint has one: the
+  // type embedding, head TransformerEncoderLayers, scorer and act head
+  if (get("type_emb.weight")) {
+    if ((s = require("type_emb.weight", {3, D}, &t))) return s;
+    if ((s = upload_f32(t, &type_emb))) return s;
+    for (int i = 0; get("head.layers." + std::to_string(i) + ".norm1.weight"); ++i) {
+      HeadLayerDev hl;
+      const std::string p = "head.layers." + std::to_string(i) + ".";
+      const int64_t d = D;
+      struct {
+        const char* name;
+        std::vector<int64_t> shape;
+        float** f32;
+        void** w;
+      } items[] = {{"norm1.weight", {d}, &hl.n1w, nullptr},
+                   {"norm1.bias", {d}, &hl.n1b, nullptr},
+                   {"norm2.weight", {d}, &hl.n2w, nullptr},
+                   {"norm2.bias", {d}, &hl.n2b, nullptr},
+                   {"self_attn.in_proj_weight", {3 * d, d}, nullptr, &hl.in_w},
+                   {"self_attn.in_proj_bias", {3 * d}, &hl.in_b, nullptr},
+                   {"self_attn.out_proj.weight", {d, d}, nullptr, &hl.out_w},
+                   {"self_attn.out_proj.bias", {d}, &hl.out_b, nullptr},
+                   {"linear1.weight", {4 * d, d}, nullptr, &hl.l1w},
+                   {"linear1.bias", {4 * d}, &hl.l1b, nullptr},
+                   {"linear2.weight", {d, 4 * d}, nullptr, &hl.l2w},
+                   {"linear2.bias", {d}, &hl.l2b, nullptr}};
+      for (auto& it : items) {
+        if ((s = require(p + it.name, it.shape, &t))) return s;
+        if ((s = it.f32 ? upload_f32(t, it.f32) : upload_w(t, it.w))) return s;
+      }
+      hlayers.push_back(hl);
+    }
+    // scorer: LayerNorm + Linear(D, D) + GELU + Linear(D, 1); its biases are optional
+    if ((s = require("scorer.0.weight", {D}, &t)) || (s = upload_f32(t, &sc_lnw))) return s;
+    if ((s = require("scorer.1.weight", {D, D}, &t)) || (s = upload_f32(t, &sc_w1))) return s;
+    if ((s = require("scorer.3.weight", {1, D}, &t)) || (s = upload_f32(t, &sc_w2))) return s;
+    if (get("scorer.0.bias") &&
+        ((s = require("scorer.0.bias", {D}, &t)) || (s = upload_f32(t, &sc_lnb))))
+      return s;
+    if (get("scorer.1.bias") &&
+        ((s = require("scorer.1.bias", {D}, &t)) || (s = upload_f32(t, &sc_b1))))
+      return s;
+    if (get("scorer.3.bias") &&
+        ((s = require("scorer.3.bias", {1}, &t)) || (s = upload_f32(t, &sc_b2))))
+      return s;
+    // act head: Linear(D + 4, 256) + GELU + Linear(256, n_act)
+    const HostTensor* a2 = get("act_head.2.weight");
+    if (!a2 || a2->shape.size() != 2 || a2->shape[1] != 256 || a2->shape[0] < 1)
+      return fail(SJ_ERR_INVALID, "Model 'act_head.2.weight' must be [n_act, 256]");
+    n_act = (int)a2->shape[0];
+    if ((s = require("act_head.0.weight", {256, (int64_t)D + 4}, &t)) ||
+        (s = upload_f32(t, &act_w1)) || (s = require("act_head.0.bias", {256}, &t)) ||
+        (s = upload_f32(t, &act_b1)) || (s = require("act_head.2.weight", {n_act, 256}, &t)) ||
+        (s = upload_f32(t, &act_w2)) || (s = require("act_head.2.bias", {n_act}, &t)) ||
+        (s = upload_f32(t, &act_b2)))
+      return s;
+    has_dm = true;
+  }
   // workspace
   const size_t T = (size_t)max_tokens, es = bf16_mode ? 2 : 4;
   max_tiles = max_tokens / 64 + max_tokens + 1;
   if ((rc = dalloc(&X, T * D)) || (rc = dalloc((char**)&Y, T * D * es)) ||
       (rc = dalloc((char**)&QKV, T * 3 * D * es)) || (rc = dalloc((char**)&O, T * D * es)) ||
-      (rc = dalloc((char**)&G, T * F * es)) || (rc = dalloc(&pos, T)) || (rc = dalloc(&ids, T)) ||
+      (rc = dalloc((char**)&G, T * (hlayers.empty() ? F : std::max(F, 4 * D)) * es)) ||
+      (rc = dalloc(&pos, T)) || (rc = dalloc(&ids, T)) ||
       (rc = dalloc(&cu, T + 1)) || (rc = dalloc(&kvl, T)) || (rc = dalloc(&tiles, max_tiles)) ||
       (rc = dalloc(&Hc, T * D)) || (rc = dalloc(&probs, T * (size_t)std::max(1, spec.n_total))) ||
       (rc = dalloc(&hid, T * D)) || (rc = dalloc(&z, T * (size_t)std::max(1, lora_r))) ||
@@ -341,10 +453,32 @@ int sj_fast::commit() {
     if (rc_ != cudaSuccess) return cuda_fail(rc_, #expr);  \
   } while (0)
 
+// C = act(A W^T + bias) (epi STORE), resid += A W^T (+ bias) (RESID), GEGLU or
+// QKV + RoPE: the tcgen05 GEMM in bf16 mode when it takes the shape, the
+// CUDA-core GEMM otherwise (fp32 mode, odd shapes).
+template <typename T>
+int sj_fast::gemm_any(int cls, const T* A, const void* W, const float* bias, int act, T* C,
+                      float* resid, int M, int N, int K, int epi, const float* ct,
+                      const float* stb, cudaStream_t st) {
+  if constexpr (std::is_same<T, bf16>::value) {
+    const bool geglu = epi == sjb::TC_GEGLU;
+    if (sjb::gemm_tc_supported(M, N, K, geglu) && (epi != sjb::TC_ROPE || Dh == 64)) {
+      sjb::TcRope rp{ct, stb, pos, H};
+      SJ_LAUNCH(cls, sjb::gemm_tc(A, static_cast<const bf16*>(W), bias, C, resid, M, N, K, epi, act,
+                                  rp, dflags + 1, st));
+      return SJ_OK;
+    }
+  }
+  SJ_LAUNCH(cls, (sjb::gemm_simt<T, T>(A, static_cast<const T*>(W), bias, C, resid, M, N, K, act,
+                                       epi == sjb::TC_GEGLU, st)));
+  if (epi == sjb::TC_ROPE) SJ_LAUNCH(cls, sjb::rope<T>(C, ct, stb, pos, M, H, Dh, st));
+  return SJ_OK;
+}
+
 template <typename T>
 int sj_fast::forward(const int64_t* d_ids, const int32_t* d_cu, const int32_t* hcu,
                      const int32_t* d_kvl, int B, int ntok, float* d_hidden, float* d_probs,
-                     cudaStream_t st) {
+                     const DmPass* dm, cudaStream_t st) {
   constexpr bool kBf16 = std::is_same<T, bf16>::value;
   const bool tc_attn = kBf16 && sjb::attn_tc_supported(Dh);
   const int qt = tc_attn ? 128 : 64;
@@ -381,20 +515,7 @@ int sj_fast::forward(const int64_t* d_ids, const int32_t* d_cu, const int32_t* h
 
   auto gemm = [&](int cls, const T* A, const void* W, T* C, float* resid, int N, int K, int epi,
                   const float* ct, const float* stb) -> int {
-    if constexpr (kBf16) {
-      const bool geglu = epi == sjb::TC_GEGLU;
-      if (sjb::gemm_tc_supported(ntok, N, K, geglu) &&
-          (epi != sjb::TC_ROPE || Dh == 64)) {
-        sjb::TcRope rp{ct, stb, pos, H};
-        SJ_LAUNCH(cls, sjb::gemm_tc(A, static_cast<const bf16*>(W), nullptr, C, resid, ntok, N, K, epi,
-                               0, rp, dflags + 1, st));
-        return SJ_OK;
-      }
-    }
-    SJ_LAUNCH(cls, (sjb::gemm_simt<T, T>(A, static_cast<const T*>(W), nullptr, C, resid, ntok, N, K, 0,
-                                    epi == sjb::TC_GEGLU, st)));
-    if (epi == sjb::TC_ROPE) SJ_LAUNCH(cls, sjb::rope<T>(C, ct, stb, pos, ntok, H, Dh, st));
-    return SJ_OK;
+    return gemm_any<T>(cls, A, W, nullptr, 0, C, resid, ntok, N, K, epi, ct, stb, st);
   };
 
   int s;
@@ -432,6 +553,7 @@ int sj_fast::forward(const int64_t* d_ids, const int32_t* d_cu, const int32_t* h
       SJ_LAUNCH(SJ_K_FINAL, (sjb::gemm_simt<float, float>(z, lora_b, nullptr, nullptr, d_hidden, ntok, D,
                                               lora_r, 0, false, st)));
     }
+    if (dm && (s = head_forward<T>(d_cu, d_kvl, B, ntok, nt, d_hidden, *dm, st))) return s;
   }
   if (d_probs && has_heads) {
     SJ_LAUNCH(SJ_K_FINAL, (sjb::add_ln<float, float>(X, nullptr, final_norm, nullptr, Hc, B, D, eps, d_cu, st)));
@@ -446,8 +568,66 @@ int sj_fast::forward(const int64_t* d_ids, const int32_t* d_cu, const int32_t* h
   return SJ_OK;
 }
 
+// The decision-model tail on the final-norm hidden states h [ntok, D] (fp32,
+// the head's residual stream), DecisionModel::forward model.cpp:402-535:
+//   h += type_emb[qtype]
+//   per head layer: h += out_proj(attn(LN1(h) in_proj^T + b)) + b   (no RoPE, keys < kv_len)
+//                   h += linear2(relu(linear1(LN2(h)))) (+ biases)  (LN eps 1e-5)
+//   scorer on the marker rows: LN -> Linear + GELU -> Linear(1); masked logits
+//   act head per segment (head.cu)
+// The head layers run in the activation precision on the encoder's kernels;
+// the scorer and act head in fp32.
+template <typename T>
+int sj_fast::head_forward(const int32_t* d_cu, const int32_t* d_kvl, int B, int ntok, int nt,
+                          float* h, const DmPass& dm, cudaStream_t st) {
+  constexpr bool kBf16 = std::is_same<T, bf16>::value;
+  const bool tc_attn = kBf16 && sjb::attn_tc_supported(Dh);
+  T* Yt = static_cast<T*>(Y);
+  T* Qt = static_cast<T*>(QKV);
+  T* Ot = static_cast<T*>(O);
+  T* Ft = static_cast<T*>(G);
+  int s;
+  SJ_LAUNCH(SJ_K_FINAL, sjb::type_emb_add(h, d_cu, B, dm.qtype, type_emb, D, ntok, st));
+  for (const HeadLayerDev& hl : hlayers) {
+    SJ_LAUNCH(SJ_K_LN, (sjb::add_ln<T, T>(h, nullptr, hl.n1w, hl.n1b, Yt, ntok, D, 1e-5f, nullptr, st)));
+    if ((s = gemm_any<T>(SJ_K_QKV, Yt, hl.in_w, hl.in_b, 0, Qt, nullptr, ntok, 3 * D, D,
+                         sjb::TC_STORE, nullptr, nullptr, st)))
+      return s;
+    if (tc_attn) {
+      if constexpr (kBf16)
+        SJ_LAUNCH(SJ_K_ATTN, sjb::attn_tc(Qt, d_cu, d_kvl, Ot, ntok, H, 0, tiles, nt, B, 0,
+                                         dflags + 2, st));
+    } else {
+      SJ_LAUNCH(SJ_K_ATTN, sjb::attn_simt<T>(Qt, d_cu, d_kvl, Ot, H, Dh, 0, tiles, nt, B, 0, st));
+    }
+    if ((s = gemm_any<T>(SJ_K_WO, Ot, hl.out_w, hl.out_b, 0, nullptr, h, ntok, D, D, sjb::TC_RESID,
+                         nullptr, nullptr, st)))
+      return s;
+    SJ_LAUNCH(SJ_K_LN, (sjb::add_ln<T, T>(h, nullptr, hl.n2w, hl.n2b, Yt, ntok, D, 1e-5f, nullptr, st)));
+    if ((s = gemm_any<T>(SJ_K_GEGLU, Yt, hl.l1w, hl.l1b, sjb::ACT_RELU, Ft, nullptr, ntok, 4 * D, D,
+                         sjb::TC_STORE, nullptr, nullptr, st)))
+      return s;
+    if ((s = gemm_any<T>(SJ_K_WO2, Ft, hl.l2w, hl.l2b, 0, nullptr, h, ntok, D, 4 * D, sjb::TC_RESID,
+                         nullptr, nullptr, st)))
+      return s;
+  }
+  // scorer (model.cpp:462-487) and act head (:489-533), fp32
+  const int BK = B * dm.K;
+  SJ_LAUNCH(SJ_K_FINAL, sjb::gather_markers(h, d_cu, dm.pos, B, dm.K, D, dm_m, st));
+  SJ_LAUNCH(SJ_K_FINAL, (sjb::add_ln<float, float>(dm_m, nullptr, sc_lnw, sc_lnb, dm_s, BK, D,
+                                                   cfg.norm_eps, nullptr, st)));
+  SJ_LAUNCH(SJ_K_FINAL, (sjb::gemm_simt<float, float>(dm_s, sc_w1, sc_b1, dm_s1, nullptr, BK, D, D,
+                                                      sjb::ACT_GELU, false, st)));
+  SJ_LAUNCH(SJ_K_FINAL, (sjb::gemm_simt<float, float>(dm_s1, sc_w2, sc_b2, dm_s2, nullptr, BK, 1, D,
+                                                      0, false, st)));
+  SJ_LAUNCH(SJ_K_FINAL, sjb::act_head(h, d_cu, B, dm_s2, dm.mask, dm.K, act_w1, act_b1, act_w2,
+                                      act_b2, n_act, D, dm.logits, dm.act, st));
+  return SJ_OK;
+}
+
 int sj_fast::run(const int64_t* d_ids, const int32_t* d_cu, const int32_t* hcu,
-                 const int32_t* d_kvl, int B, float* d_hidden, float* d_probs, cudaStream_t st) {
+                 const int32_t* d_kvl, int B, float* d_hidden, float* d_probs, const DmPass* dm,
+                 cudaStream_t st) {
   if (!committed) return fail(SJ_ERR_STATE, "forward before sj_fast_commit");
   if (B < 0) return fail(SJ_ERR_INVALID, "negative batch");
   if (B == 0) return SJ_OK;
@@ -470,8 +650,8 @@ int sj_fast::run(const int64_t* d_ids, const int32_t* d_cu, const int32_t* hcu,
   launches = 0;
   cudaError_t rc = cudaSetDevice(cfg.device);
   if (rc != cudaSuccess) return cuda_fail(rc, "cudaSetDevice");
-  return bf16_mode ? forward<bf16>(d_ids, d_cu, hcu, d_kvl, B, T, d_hidden, d_probs, st)
-                   : forward<float>(d_ids, d_cu, hcu, d_kvl, B, T, d_hidden, d_probs, st);
+  return bf16_mode ? forward<bf16>(d_ids, d_cu, hcu, d_kvl, B, T, d_hidden, d_probs, dm, st)
+                   : forward<float>(d_ids, d_cu, hcu, d_kvl, B, T, d_hidden, d_probs, dm, st);
 }
 
 int sj_fast::check_flags(cudaStream_t st) {
@@ -531,7 +711,7 @@ int sj_fast::host_call(const int64_t* ids_h, const int32_t* cu_h, const int32_t*
     // h_cu is read by run() for the schedule; it is pinned host memory that
     // stays untouched until the next pass's event wait above.
     int s = run(ids, cu, h_cu, kvl_h ? kvl : nullptr, nb, hidden_h ? hid : nullptr,
-                probs_h ? probs : nullptr, stream);
+                probs_h ? probs : nullptr, nullptr, stream);
     if (s) return s;
     if (hidden_h && (rc = cudaMemcpyAsync(hidden_h + (int64_t)base * D, hid,
                                           (size_t)T * D * sizeof(float), cudaMemcpyDeviceToHost,
@@ -543,6 +723,92 @@ int sj_fast::host_call(const int64_t* ids_h, const int32_t* cu_h, const int32_t*
       return cuda_fail(rc, "cudaMemcpyAsync (probs)");
     if ((rc = cudaEventRecord(staged_ev, stream))) return cuda_fail(rc, "cudaEventRecord");
     b0 = b1;
+  }
+  return check_flags(stream);
+}
+
+int sj_fast::dm_call(const int64_t* ids_h, const int32_t* cu_h, const int32_t* kvl_h, int B,
+                     const int64_t* pos_h, const uint8_t* mask_h, int K, const int64_t* qtype_h,
+                     float* logits_h, float* act_h) {
+  if (!committed) return fail(SJ_ERR_STATE, "forward before sj_fast_commit");
+  if (!has_dm)
+    return fail(SJ_ERR_STATE, "the checkpoint has no decision-model head (type_emb, head, scorer, "
+                              "act_head)");
+  if (B <= 0) return B == 0 ? SJ_OK : fail(SJ_ERR_INVALID, "negative batch");
+  if (K < 1 || K > 4096) return fail(SJ_ERR_INVALID, "K (markers per sequence) must be in [1, 4096]");
+  if (!cu_h || !ids_h || !pos_h || !mask_h || !qtype_h || !logits_h || !act_h)
+    return fail(SJ_ERR_INVALID, "null input or output");
+  if (cu_h[0] != 0) return fail(SJ_ERR_INVALID, "cu_seqlens[0] must be 0");
+  for (int b = 0; b < B; ++b) {
+    const int n = cu_h[b + 1] - cu_h[b];
+    if (n < 1) return fail(SJ_ERR_INVALID, "every sequence needs at least one row ([CLS])");
+    if (n > max_tokens) return fail(SJ_ERR_INVALID, "sequence longer than max_tokens");
+    if (kvl_h && (kvl_h[b] < 0 || kvl_h[b] > n))
+      return fail(SJ_ERR_INVALID, "kv_lens[b] must lie in [0, length of segment b]");
+    if (qtype_h[b] < 0 || qtype_h[b] >= 3)
+      return fail(SJ_ERR_INVALID, "qtype " + std::to_string(qtype_h[b]) + " outside [0, 3)");
+  }
+  for (int64_t r = 0; r < cu_h[B]; ++r)
+    if (ids_h[r] < 0 || ids_h[r] >= V)
+      return fail(SJ_ERR_INVALID, "input id " + std::to_string(ids_h[r]) + " at row " +
+                                      std::to_string(r) + " outside the vocabulary [0, vocab_size)");
+  cudaError_t rc = cudaSetDevice(cfg.device);
+  if (rc != cudaSuccess) return cuda_fail(rc, "cudaSetDevice");
+  // passes of whole sequences; per-call buffers sized for the largest pass
+  std::vector<std::pair<int, int>> passes;
+  size_t max_nb = 0;
+  for (int b0 = 0; b0 < B;) {
+    int b1 = b0;
+    while (b1 < B && cu_h[b1 + 1] - cu_h[b0] <= max_tokens) ++b1;
+    passes.emplace_back(b0, b1);
+    max_nb = std::max(max_nb, (size_t)(b1 - b0));
+    b0 = b1;
+  }
+  if ((rc = cudaStreamSynchronize(stream))) return cuda_fail(rc, "cudaStreamSynchronize");
+  const size_t bk = max_nb * (size_t)K;
+  if (bk > dm_cap_bk) {
+    if ((rc = grow(&dm_m, bk * D)) || (rc = grow(&dm_s, bk * D)) || (rc = grow(&dm_s1, bk * D)) ||
+        (rc = grow(&dm_s2, bk)) || (rc = grow(&dm_logits, bk)) || (rc = grow(&dm_pos, bk)) ||
+        (rc = grow(&dm_mask, bk)))
+      return cuda_fail(rc, "cudaMalloc (marker rows)");
+    dm_cap_bk = bk;
+  }
+  if (max_nb > dm_cap_b) {
+    if ((rc = grow(&dm_qt, max_nb)) || (rc = grow(&dm_act, max_nb * (size_t)n_act)))
+      return cuda_fail(rc, "cudaMalloc (act)");
+    dm_cap_b = max_nb;
+  }
+  for (const auto& p : passes) {
+    const int b0 = p.first, b1 = p.second, nb = b1 - b0, base = cu_h[b0], T = cu_h[b1] - base;
+    rc = cudaEventSynchronize(staged_ev);
+    if (rc != cudaSuccess) return cuda_fail(rc, "cudaEventSynchronize");
+    for (int b = 0; b <= nb; ++b) h_cu[b] = cu_h[b0 + b] - base;
+    if (kvl_h) for (int b = 0; b < nb; ++b) h_kvl[b] = kvl_h[b0 + b];
+    const size_t nbk = (size_t)nb * K;
+    if ((rc = cudaMemcpyAsync(ids, ids_h + base, T * sizeof(int64_t), cudaMemcpyHostToDevice,
+                              stream)) ||
+        (rc = cudaMemcpyAsync(cu, h_cu, (nb + 1) * sizeof(int32_t), cudaMemcpyHostToDevice,
+                              stream)) ||
+        (kvl_h && (rc = cudaMemcpyAsync(kvl, h_kvl, nb * sizeof(int32_t), cudaMemcpyHostToDevice,
+                                        stream))) ||
+        (rc = cudaMemcpyAsync(dm_qt, qtype_h + b0, nb * sizeof(int64_t), cudaMemcpyHostToDevice,
+                              stream)) ||
+        (rc = cudaMemcpyAsync(dm_pos, pos_h + (size_t)b0 * K, nbk * sizeof(int64_t),
+                              cudaMemcpyHostToDevice, stream)) ||
+        (rc = cudaMemcpyAsync(dm_mask, mask_h + (size_t)b0 * K, nbk, cudaMemcpyHostToDevice,
+                              stream)))
+      return cuda_fail(rc, "cudaMemcpyAsync (inputs)");
+    DmPass dm{dm_qt, dm_pos, dm_mask, K, dm_logits, dm_act};
+    int s = run(ids, cu, h_cu, kvl_h ? kvl : nullptr, nb, hid, nullptr, &dm, stream);
+    if (s) return s;
+    if ((rc = cudaMemcpyAsync(logits_h + (size_t)b0 * K, dm_logits, nbk * sizeof(float),
+                              cudaMemcpyDeviceToHost, stream)) ||
+        (rc = cudaMemcpyAsync(act_h + (size_t)b0 * n_act, dm_act,
+                              (size_t)nb * n_act * sizeof(float), cudaMemcpyDeviceToHost, stream)))
+      return cuda_fail(rc, "cudaMemcpyAsync (outputs)");
+    if ((rc = cudaEventRecord(staged_ev, stream))) return cuda_fail(rc, "cudaEventRecord");
+    // the next pass overwrites dm_* and the inputs: let this one finish reading them
+    if ((rc = cudaStreamSynchronize(stream))) return cuda_fail(rc, "cudaStreamSynchronize");
   }
   return check_flags(stream);
 }
@@ -639,6 +905,16 @@ int sj_fast_decide(sj_fast* e, const int64_t* ids, const int32_t* cu_seqlens, in
   return e->host_call(ids, cu_seqlens, nullptr, B, nullptr, probs);
 }
 
+int sj_fast_forward(sj_fast* e, const int64_t* ids, const int32_t* cu_seqlens,
+                    const int32_t* kv_lens, int B, const int64_t* marker_pos,
+                    const uint8_t* marker_mask, int K, const int64_t* qtype, float* logits,
+                    float* act) {
+  if (!e) return SJ_ERR_INVALID;
+  return e->dm_call(ids, cu_seqlens, kv_lens, B, marker_pos, marker_mask, K, qtype, logits, act);
+}
+
+int sj_fast_n_act(const sj_fast* e) { return e && e->has_dm ? e->n_act : 0; }
+
 int sj_fast_encode_device(sj_fast* e, const int64_t* ids, const int32_t* cu_seqlens,
                           const int32_t* cu_seqlens_host, const int32_t* kv_lens, int B,
                           float* hidden, float* probs, void* stream) {
@@ -647,7 +923,7 @@ int sj_fast_encode_device(sj_fast* e, const int64_t* ids, const int32_t* cu_seql
     return e->fail(SJ_ERR_INVALID, "null input");
   if (probs && !e->has_heads) return e->fail(SJ_ERR_STATE, "no decision heads set");
   cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : e->stream;
-  return e->run(ids, cu_seqlens, cu_seqlens_host, kv_lens, B, hidden, probs, st);
+  return e->run(ids, cu_seqlens, cu_seqlens_host, kv_lens, B, hidden, probs, nullptr, st);
 }
 
 int sj_fast_sync(sj_fast* e, void* stream) {

@@ -13,7 +13,7 @@
 //               lanes 32*(w%4)..+31 = tile rows; warps 2-5 take the first half
 //               of the tile's columns, warps 6-9 the second), then one of
 //                 STORE  C = bf16(acc + bias, act)           (act: GELU-erf / ReLU)
-//                 RESID  X += acc                            (fp32 residual stream)
+//                 RESID  X += acc (+bias)                    (fp32 residual stream)
 //                 GEGLU  G = bf16(gelu(acc_g) * acc_u)        (W tile = 128 gate rows
 //                                                             + 128 up rows of [Wg; Wu];
 //                                                             erf per A&S 7.1.26, packed fp32)
@@ -484,14 +484,26 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           uint8_t* rowp = stg + (k & 1) * 4096 + lane * 128;
+          const float4* bias4 =
+              ep.bias ? reinterpret_cast<const float4*>(ep.bias + xcol + 32 * k) : nullptr;
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             float4* cell = reinterpret_cast<float4*>(rowp + ((c ^ (lane & 7)) << 4));
             float4 o = *cell;
-            o.x += __uint_as_float(acc[k][4 * c]);
-            o.y += __uint_as_float(acc[k][4 * c + 1]);
-            o.z += __uint_as_float(acc[k][4 * c + 2]);
-            o.w += __uint_as_float(acc[k][4 * c + 3]);
+            float4 a = make_float4(__uint_as_float(acc[k][4 * c]), __uint_as_float(acc[k][4 * c + 1]),
+                                   __uint_as_float(acc[k][4 * c + 2]),
+                                   __uint_as_float(acc[k][4 * c + 3]));
+            if (bias4) {
+              const float4 bv = bias4[c];
+              a.x += bv.x;
+              a.y += bv.y;
+              a.z += bv.z;
+              a.w += bv.w;
+            }
+            o.x += a.x;
+            o.y += a.y;
+            o.z += a.z;
+            o.w += a.w;
             *cell = o;
           }
           fence_async_smem();
@@ -527,13 +539,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld32(tacc + c0 + 32 * k, r0);
           tmem_ld_wait();
           if (live) {
+            const float* bk = ep.bias ? ep.bias + nb * BN + c0 + 32 * k : nullptr;
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
+              float4 a = make_float4(__uint_as_float(r0[4 * j]), __uint_as_float(r0[4 * j + 1]),
+                                     __uint_as_float(r0[4 * j + 2]), __uint_as_float(r0[4 * j + 3]));
+              if (bk) {
+                const float4 bv = reinterpret_cast<const float4*>(bk)[j];
+                a.x += bv.x;
+                a.y += bv.y;
+                a.z += bv.z;
+                a.w += bv.w;
+              }
               float4 o = xv[k & 1][j];
-              o.x += __uint_as_float(r0[4 * j]);
-              o.y += __uint_as_float(r0[4 * j + 1]);
-              o.z += __uint_as_float(r0[4 * j + 2]);
-              o.w += __uint_as_float(r0[4 * j + 3]);
+              o.x += a.x;
+              o.y += a.y;
+              o.z += a.z;
+              o.w += a.w;
               reinterpret_cast<float4*>(xrow + 32 * k)[j] = o;
             }
           }

@@ -80,6 +80,19 @@ cudaError_t dec_heads(const float* Hc, int B, int D, const float* W, const float
 // Y[i] = bf16(X[i]) (identity attn_norm in bf16 mode).
 cudaError_t cast_bf16(const float* X, bf16* Y, int64_t n, cudaStream_t st);
 
+// decision-model tail (head.cu): h[r] += type_emb[qtype[segment of r]];
+// marker rows m[b*K + k] = h[cu[b] + clamp(pos, 0, n_b - 1)]; the act head
+// (masked logits, softmax statistics, act MLP and softmax), one block per segment
+cudaError_t type_emb_add(float* h, const int32_t* cu, int B, const int64_t* qtype,
+                         const float* te, int D, int T, cudaStream_t st);
+cudaError_t gather_markers(const float* h, const int32_t* cu, const int64_t* pos, int B, int K,
+                           int D, float* m, cudaStream_t st);
+size_t act_head_smem(int K, int D, int n_act);
+cudaError_t act_head(const float* h, const int32_t* cu, int B, const float* score,
+                     const uint8_t* mask, int K, const float* w1, const float* b1,
+                     const float* w2, const float* b2, int n_act, int D, float* logits,
+                     float* act, cudaStream_t st);
+
 // ---- tcgen05 GEMM (gemm_tc.cu) ------------------------------------------------
 // True when the tensor-core GEMM takes this shape (K % 64 == 0, N tiles of 256
 // or, for geglu, F % 128 == 0, 16-byte aligned rows).
@@ -93,7 +106,7 @@ struct TcRope {
   int H;  // q and k heads of 64 columns rotate; v columns pass through
 };
 // bf16 A[M, K], W[N, K] (for TC_GEGLU W = [Wg; Wu], 2N rows, N = F), fp32 accum.
-// TC_STORE: C = acc (+bias, act); TC_RESID: resid += acc; TC_ROPE: C = rope(acc).
+// TC_STORE: C = acc (+bias, act); TC_RESID: resid += acc (+bias); TC_ROPE: C = rope(acc).
 cudaError_t gemm_tc(const bf16* A, const bf16* W, const float* bias, bf16* C, float* resid,
                     int M, int N, int K, int epi, int act, TcRope rope, int* err,
                     cudaStream_t st);

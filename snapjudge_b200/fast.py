@@ -107,6 +107,32 @@ class FastSnapjudge:
         out = self.encode_packed(ids.reshape(-1), np.full(B, L, np.int64), kv_lens=lens)
         return out.reshape(B, L, self.D)
 
+    @property
+    def n_act(self) -> int:
+        """Outputs of the act head (0 without a decision-model head)."""
+        return int(_lib.lib().sj_fast_n_act(self._h))
+
+    def forward(self, input_ids, attention_mask, marker_pos, marker_mask, qtype):
+        """DecisionModel::forward (src/model.cpp:309-536) on the GPU: padded
+        [B, L] ids + mask, marker_pos / marker_mask [B, K], qtype [B] ->
+        (logits [B, K], act [B, n_act])."""
+        ids = np.ascontiguousarray(input_ids, dtype=np.int64)
+        mask = np.asarray(attention_mask, dtype=np.int64)
+        B, L = ids.shape
+        pos = np.ascontiguousarray(marker_pos, dtype=np.int64)
+        mm = np.ascontiguousarray(marker_mask, dtype=np.uint8)
+        qt = np.ascontiguousarray(qtype, dtype=np.int64)
+        K = pos.shape[1] if pos.ndim == 2 else 0
+        if pos.shape != (B, K) or mm.shape != (B, K) or qt.shape != (B,):
+            raise ValueError("marker_pos / marker_mask must be [B, K] and qtype [B]")
+        kvl = np.ascontiguousarray(mask.sum(axis=1), dtype=np.int32)
+        cu = (np.arange(B + 1, dtype=np.int64) * L).astype(np.int32)
+        logits = np.empty((B, K), np.float32)
+        act = np.empty((B, max(1, self.n_act)), np.float32)
+        check(_lib.lib().sj_fast_forward(self._h, _ptr(ids), _ptr(cu), _ptr(kvl), B, _ptr(pos),
+                                         _ptr(mm), K, _ptr(qt), _ptr(logits), _ptr(act)), self._h)
+        return logits, act[:, :self.n_act]
+
     def decide(self, ids, lengths, out: np.ndarray | None = None, cu=None) -> np.ndarray:
         """Encoder + heads; probs [B, sum n_out].  `out` / `cu` may be preallocated
         (e.g. pinned) host arrays: float32 [B, n_out] and int32 [B + 1]."""
