@@ -123,6 +123,32 @@ def test_c3_subset_vs_oracle():
     _subset_check(synth.SPECS["c3"], 6, 77)
 
 
+def test_sliding_window_layers_at_scale():
+    """ModernBERT's layer pattern on the C3 architecture: every third layer
+    global, the others sliding (local_attention 128 -> |i - j| <= 64, RoPE
+    theta of the sliding layers), on sequences up to 512 tokens (model.cpp:103-111)."""
+    import dataclasses
+    base = synth.SPECS["c3"]
+    cfg = dataclasses.replace(
+        base.cfg, local_attention=128,
+        layer_types=["full_attention" if i % 3 == 0 else "sliding_attention"
+                     for i in range(base.cfg.num_hidden_layers)])
+    spec = dataclasses.replace(base, cfg=cfg)
+    assert cfg.layer_window(1) == 64 and cfg.layer_window(0) == 0
+    t = synth.make_weights(spec)
+    lengths = np.array([512, 300, 129, 64, 1])
+    ids = synth.make_ids(spec, lengths, seed=91)
+    eng = FastSnapjudge(cfg, t, precision="bf16")
+    got = eng.encode_packed(ids, lengths)
+    want = oracle.Oracle(cfg, t).encode_packed(ids, lengths)
+    assert np.isfinite(got).all()
+    assert np.abs(got - want).max() <= 6e-2
+    # the window changes the result (the oracle's windowed and full forwards
+    # differ by 0.47 here): the same weights without sliding layers differ
+    full = FastSnapjudge(base.cfg, t, precision="bf16").encode_packed(ids, lengths)
+    assert np.abs(full - got)[:512].max() > 3 * 6e-2
+
+
 def test_c5_subset_vs_oracle():
     _subset_check(synth.SPECS["c5"], 24, 78)
 

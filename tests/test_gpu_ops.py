@@ -104,6 +104,7 @@ ATTN_CASES = [
     (12, 64, [300, 200], 64, None),
     (4, 64, [100, 100], 0, [100, 37]),  # padded-batch semantics: keys < kv_len
     (16, 64, [2048], 0, None),
+    (16, 64, [2048, 1000], 128, None),  # sliding window at scale: out-of-window tiles skipped
 ]
 
 
