@@ -1,7 +1,8 @@
 // adapter_check.cpp — the reference's DecisionModel::forward (CPU, fp32) against
 // snapjudge::FastSnapjudge::forward (snapjudge_b200/integration/fast.cpp, the
-// encoder on the GPU through the C ABI) on one checkpoint and a ragged padded
-// batch.  TEST INFRASTRUCTURE ONLY (built by oracle/Makefile into oracle/_ref/).
+// whole forward on the GPU through the C ABI) on one checkpoint and a ragged
+// padded batch, once packed to its valid rows and once with a live marker on a
+// padded row (the padding computed).  TEST INFRASTRUCTURE ONLY (built by oracle/Makefile into oracle/_ref/).
 //
 // usage: adapter_check <checkpoint dir>  -> prints one JSON line of max diffs;
 // exit 0 when the bf16 tolerances hold (logits 2e-2, act probabilities 5e-3).
@@ -47,15 +48,23 @@ int main(int argc, char** argv) {
     }
     qt[b] = static_cast<int64_t>(rng() % 3);
   }
-  std::vector<std::vector<float>> lg_ref, act_ref, lg, act;
-  model->forward(ids, mask, mp, mm, qt, lg_ref, act_ref);
   FastSnapjudge fast(model.get(), 512, true);
-  fast.forward(ids, mask, mp, mm, qt, lg, act);
   double dl = 0, da = 0;
-  for (int b = 0; b < B; ++b) {
-    for (int k = 0; k < K; ++k) dl = std::max(dl, (double)std::fabs(lg[b][k] - lg_ref[b][k]));
-    for (size_t j = 0; j < act[b].size(); ++j)
-      da = std::max(da, (double)std::fabs(act[b][j] - act_ref[b][j]));
+  // batch 1: markers on valid rows (the adapter packs the batch to its valid
+  // rows); batch 2: one live marker on a padded row (it computes the padding)
+  for (int pass = 0; pass < 2; ++pass) {
+    if (pass == 1) {
+      mp[3][0] = lens[3] + 5;  // a padded position of row 3
+      mm[3][0] = 1;
+    }
+    std::vector<std::vector<float>> lg_ref, act_ref, lg, act;
+    model->forward(ids, mask, mp, mm, qt, lg_ref, act_ref);
+    fast.forward(ids, mask, mp, mm, qt, lg, act);
+    for (int b = 0; b < B; ++b) {
+      for (int k = 0; k < K; ++k) dl = std::max(dl, (double)std::fabs(lg[b][k] - lg_ref[b][k]));
+      for (size_t j = 0; j < act[b].size(); ++j)
+        da = std::max(da, (double)std::fabs(act[b][j] - act_ref[b][j]));
+    }
   }
   std::printf("{\"logits_max_abs\": %.3g, \"act_max_abs\": %.3g}\n", dl, da);
   return (dl <= 2e-2 && da <= 5e-3) ? 0 : 1;

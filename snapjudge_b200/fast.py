@@ -112,10 +112,16 @@ class FastSnapjudge:
         """Outputs of the act head (0 without a decision-model head)."""
         return int(_lib.lib().sj_fast_n_act(self._h))
 
-    def forward(self, input_ids, attention_mask, marker_pos, marker_mask, qtype):
+    def forward(self, input_ids, attention_mask, marker_pos, marker_mask, qtype, pack=None):
         """DecisionModel::forward (src/model.cpp:309-536) on the GPU: padded
         [B, L] ids + mask, marker_pos / marker_mask [B, K], qtype [B] ->
-        (logits [B, K], act [B, n_act])."""
+        (logits [B, K], act [B, n_act]).
+
+        The outputs depend on the padded rows only through a live marker that
+        points past its row's length (the reference gathers that padded row).
+        Without one, the batch is packed to its valid rows (``pack=None``:
+        decided per batch; True / False force it), which gives the same
+        outputs without computing the padding."""
         ids = np.ascontiguousarray(input_ids, dtype=np.int64)
         mask = np.asarray(attention_mask, dtype=np.int64)
         B, L = ids.shape
@@ -125,11 +131,23 @@ class FastSnapjudge:
         K = pos.shape[1] if pos.ndim == 2 else 0
         if pos.shape != (B, K) or mm.shape != (B, K) or qt.shape != (B,):
             raise ValueError("marker_pos / marker_mask must be [B, K] and qtype [B]")
-        kvl = np.ascontiguousarray(mask.sum(axis=1), dtype=np.int32)
-        cu = (np.arange(B + 1, dtype=np.int64) * L).astype(np.int32)
+        lens = mask.sum(axis=1)
+        if pack is None:
+            gathered = np.clip(pos, 0, L - 1)
+            pack = bool((lens >= 1).all() and not ((mm != 0) & (gathered >= lens[:, None])).any())
+        if pack:
+            rows = np.arange(L)[None, :] < lens[:, None]
+            flat = np.ascontiguousarray(ids[rows])
+            cu = np.zeros(B + 1, np.int32)
+            np.cumsum(lens, out=cu[1:])
+            kvl = None
+        else:
+            flat = ids
+            cu = (np.arange(B + 1, dtype=np.int64) * L).astype(np.int32)
+            kvl = np.ascontiguousarray(lens, dtype=np.int32)
         logits = np.empty((B, K), np.float32)
         act = np.empty((B, max(1, self.n_act)), np.float32)
-        check(_lib.lib().sj_fast_forward(self._h, _ptr(ids), _ptr(cu), _ptr(kvl), B, _ptr(pos),
+        check(_lib.lib().sj_fast_forward(self._h, _ptr(flat), _ptr(cu), _ptr(kvl), B, _ptr(pos),
                                          _ptr(mm), K, _ptr(qt), _ptr(logits), _ptr(act)), self._h)
         return logits, act[:, :self.n_act]
 

@@ -9,9 +9,10 @@
 //
 // The whole forward (model.cpp:309-536) runs on the GPU through the C ABI
 // (sj_fast_forward): the encoder, then the decision-model tail (type embedding,
-// head TransformerEncoderLayers, scorer on the marker rows, act head).  Every
-// padded row is computed, keys masked by the row's attention-mask length, so
-// padded rows match the CPU forward too.
+// head TransformerEncoderLayers, scorer on the marker rows, act head).  A
+// padded batch is packed to its valid rows unless a live marker points into
+// the padding; then every padded row is computed, keys masked by the row's
+// attention-mask length, as the CPU forward does.
 // Failures throw std::runtime_error("snapjudge CUDA: ..."), as cuda/fast.cpp:54-58.
 #include <algorithm>
 #include <cstring>
@@ -143,25 +144,39 @@ void FastSnapjudge::forward(const std::vector<std::vector<int64_t>>& input_ids,
   const int64_t M = B * L;
   const int n_act = sj_fast_n_act(impl_->e);
 
-  // each padded row is a segment of length L whose queries attend the first
-  // lens[b] keys (the padded-batch semantics)
-  std::vector<int64_t> flat(static_cast<size_t>(M)), pos(static_cast<size_t>(B * K));
+  std::vector<int64_t> pos(static_cast<size_t>(B * K));
   std::vector<uint8_t> mm(static_cast<size_t>(B * K));
-  std::vector<int32_t> cu(static_cast<size_t>(B + 1)), kvl(static_cast<size_t>(B));
+  std::vector<int32_t> kvl(static_cast<size_t>(B));
+  // The outputs depend on padded rows only through a live marker that points
+  // past its row's length (model.cpp:463-474 gathers that padded row).  Without
+  // one, only the valid rows are computed (packed segments); otherwise each
+  // padded row is a segment of length L whose queries attend the first lens[b]
+  // keys (the padded-batch semantics).
+  bool pack = true;
   for (int64_t b = 0; b < B; ++b) {
-    std::copy(input_ids[b].begin(), input_ids[b].end(), flat.begin() + b * L);
     std::copy(marker_pos[b].begin(), marker_pos[b].end(), pos.begin() + b * K);
     std::copy(marker_mask[b].begin(), marker_mask[b].end(), mm.begin() + b * K);
     int64_t s = 0;
     for (int64_t v : attention_mask[b]) s += v;
     kvl[b] = static_cast<int32_t>(s);
-    cu[b] = static_cast<int32_t>(b * L);
+    if (s < 1) pack = false;
+    for (int64_t k = 0; k < K; ++k) {
+      const int64_t p = std::min(std::max<int64_t>(marker_pos[b][k], 0), L - 1);
+      if (marker_mask[b][k] && p >= s) pack = false;
+    }
   }
-  cu[B] = static_cast<int32_t>(M);
+  std::vector<int64_t> flat;
+  std::vector<int32_t> cu(static_cast<size_t>(B + 1), 0);
+  flat.reserve(static_cast<size_t>(M));
+  for (int64_t b = 0; b < B; ++b) {
+    const int64_t n = pack ? kvl[b] : L;
+    flat.insert(flat.end(), input_ids[b].begin(), input_ids[b].begin() + n);
+    cu[b + 1] = cu[b] + static_cast<int32_t>(n);
+  }
   std::vector<float> lg(static_cast<size_t>(B * K)), ac(static_cast<size_t>(B * n_act));
-  int rc = sj_fast_forward(impl_->e, flat.data(), cu.data(), kvl.data(), static_cast<int>(B),
-                           pos.data(), mm.data(), static_cast<int>(K), qtype.data(), lg.data(),
-                           ac.data());
+  int rc = sj_fast_forward(impl_->e, flat.data(), cu.data(), pack ? nullptr : kvl.data(),
+                           static_cast<int>(B), pos.data(), mm.data(), static_cast<int>(K),
+                           qtype.data(), lg.data(), ac.data());
   if (rc) fail(impl_->e, rc, "sj_fast_forward");
   logits_out.assign(static_cast<size_t>(B), std::vector<float>(static_cast<size_t>(K)));
   act_out.assign(static_cast<size_t>(B), std::vector<float>(static_cast<size_t>(n_act)));

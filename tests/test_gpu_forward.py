@@ -101,6 +101,37 @@ def test_forward_c3_architecture_vs_oracle():
     assert np.abs(l2 - logits).max() <= 2e-2 and np.abs(a2 - act).max() <= 5e-3
 
 
+@pytest.mark.parametrize("precision", ["fp32", "bf16"])
+def test_forward_packed_equals_padded(precision):
+    """Packing a padded batch to its valid rows (markers on valid rows) gives the
+    outputs of computing the padding; a live marker on a padded row makes the
+    padded computation necessary (and pack=None picks it)."""
+    spec = synth.SPECS["c1"]
+    t = synth.make_weights(spec)
+    eng = FastSnapjudge(spec.cfg, t, precision=precision)
+    lengths = np.array([32, 17, 1, 9])
+    pid, mask = synth.pad_batch(synth.make_ids(spec, lengths, seed=5), lengths)
+    rng = np.random.default_rng(6)
+    pos, mm = markers(rng, lengths, 4)
+    pos[mm == 0] = 0
+    qt = rng.integers(0, 3, size=4).astype(np.int64)
+    lp, ap = eng.forward(pid, mask, pos, mm, qt, pack=True)
+    lf, af = eng.forward(pid, mask, pos, mm, qt, pack=False)
+    assert np.abs(lp - lf).max() <= 1e-5 and np.abs(ap - af).max() <= 1e-5
+    # a live marker on a padded row: only the padded computation matches the reference
+    E = np.load(GOLD)
+    c = next(c for c in cases(E, "c1") if len(c["lengths"]) == 4 and c["lengths"][1] == 17)
+    pid, mask = synth.pad_batch(c["ids"], c["lengths"])
+    pos, mm = c["marker_pos"].copy(), c["marker_mask"].copy()
+    la, aa = eng.forward(pid, mask, pos, mm, c["qtype"])
+    lb, ab = eng.forward(pid, mask, pos, mm, c["qtype"], pack=False)
+    assert np.abs(la - lb).max() <= 1e-5 and np.abs(aa - ab).max() <= 1e-5
+    pos[3, 0], mm[3, 0] = 20, 1  # row 3 has 9 valid rows
+    lc, _ = eng.forward(pid, mask, pos, mm, c["qtype"])
+    ld, _ = eng.forward(pid, mask, pos, mm, c["qtype"], pack=False)
+    assert np.abs(lc - ld).max() <= 1e-5
+
+
 def test_forward_errors():
     spec = synth.SPECS["c1"]
     t = synth.make_weights(spec)
