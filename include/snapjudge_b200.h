@@ -123,7 +123,20 @@ typedef struct sj_fast_config {
   int precision;                /* SJ_PREC_BF16 or SJ_PREC_FP32 */
   int device;                   /* CUDA device ordinal */
   int max_tokens;               /* tokens per device pass (workspace size); 0 = default */
+  int arch;                     /* SJ_ARCH_MODERNBERT (0) or SJ_ARCH_SJMODEL (1) */
 } sj_fast_config;
+
+/* Model families the engine runs:
+ * SJ_ARCH_MODERNBERT  the DecisionModel encoder (src/model.cpp), tensors
+ *                     "encoder.*", "type_emb.weight", "head.layers.*", "scorer.*",
+ *                     "act_head.*";
+ * SJ_ARCH_SJMODEL     SjModel (src/sj_model.cpp:206-255): BERT-style pre-LN
+ *                     encoder with learned positions (max_position_embeddings =
+ *                     max_positions), biased q/k/v/o and GELU FFN, biased LNs;
+ *                     tensors "sj.*" (sj_model.cpp:117-202); no RoPE or window;
+ *                     sj_fast_forward gives act = [top1, 1 - top1]. */
+#define SJ_ARCH_MODERNBERT 0
+#define SJ_ARCH_SJMODEL 1
 
 /* Create an engine on cfg->device.  Weights are then given by name with
  * sj_fast_set_tensor and uploaded by sj_fast_commit. */

@@ -328,6 +328,13 @@ def _ref(noblas=False):
         lib.sjref_attention.argtypes = [_F, _F, _F, C.c_int64, C.c_int64, C.c_int64, C.c_int64,
                                         _I64, C.c_int, _F]
         lib.sjref_rope.argtypes = [_F, C.c_int64, _F, _F, C.c_int64, C.c_int64, C.c_int64]
+        lib.sjref_sj_load.argtypes = [C.c_char_p]
+        lib.sjref_sj_load.restype = C.c_void_p
+        lib.sjref_sj_free.argtypes = [C.c_void_p]
+        lib.sjref_sj_encode.argtypes = [C.c_void_p, _I64, _I64, C.c_int64, C.c_int64,
+                                        C.c_int64, _F]
+        lib.sjref_sj_forward.argtypes = [C.c_void_p, _I64, _I64, C.c_int64, C.c_int64, _I64,
+                                         _U8, C.c_int64, _I64, _F, _F]
         _REF[key] = lib
     return _REF[key]
 
@@ -369,6 +376,131 @@ class RefModel:
         if self.lib.sjref_forward(self.h, _ip(ids), _ip(mask), B, L, _ip(mp),
                                   mm.ctypes.data_as(_U8), K, _ip(qt), _fp(logits),
                                   _fp(act)) != 0:
+            raise RuntimeError(self.lib.sjref_last_error().decode())
+        return logits, act
+
+
+def _erf(x):
+    """erf elementwise (math.erf on float64), as the reference's erff."""
+    import math
+    return np.vectorize(math.erf, otypes=[np.float64])(np.asarray(x, np.float64))
+
+
+class SjOracle:
+    """NumPy restatement of the SjModel forward (reference src/sj_model.cpp), fp32
+    GEMMs with fp64 LN statistics and softmax sums like the reference's tensor ops:
+    * embeddings: word[ids] + position[min(i, max_positions - 1)], LN with bias (:217-233);
+    * per layer (:235-245): X += o(attn(LN_a(X))), X += w2(gelu(w1(LN_f(X))));
+      attention with separate biased q/k/v/o (:40-88), keys j < lens[b];
+    * final LN with bias (:246);
+    * forward (:277-368): + type_emb[qtype], head layers of the same shape,
+      scorer on the marker rows, act = [top1, 1 - top1]."""
+
+    def __init__(self, cfg, tensors):
+        self.cfg = cfg
+        self.t = {k: np.asarray(v, np.float32) for k, v in tensors.items()}
+
+    def _ln(self, x, name, eps=None):
+        eps = self.cfg.norm_eps if eps is None else eps
+        xd = x.astype(np.float64)
+        mu = xd.mean(-1, keepdims=True)
+        var = ((xd - mu) ** 2).mean(-1, keepdims=True)
+        y = (xd - mu) / np.sqrt(var + eps)
+        return (y * self.t[name + ".weight"] + self.t[name + ".bias"]).astype(np.float32)
+
+    def _lin(self, x, name, act=0):
+        y = x @ self.t[name + ".weight"].T + self.t[name + ".bias"]
+        if act == 1:
+            y = (0.5 * y * (1.0 + _erf(y / np.sqrt(2.0)))).astype(np.float32)
+        return y.astype(np.float32)
+
+    def _attn(self, Y, p, lens):
+        B, L, D = Y.shape
+        H = self.cfg.num_heads
+        Dh = D // H
+        q = self._lin(Y, p + "attn.q").reshape(B, L, H, Dh)
+        k = self._lin(Y, p + "attn.k").reshape(B, L, H, Dh)
+        v = self._lin(Y, p + "attn.v").reshape(B, L, H, Dh)
+        s = np.einsum("bihd,bjhd->bhij", q, k) / np.float32(np.sqrt(Dh))
+        keep = np.arange(L)[None, :] < np.asarray(lens)[:, None]       # [B, L] keys
+        s = np.where(keep[:, None, None, :], s, -np.inf)
+        m = s.max(-1, keepdims=True)
+        e = np.exp((s - m).astype(np.float32))
+        o = np.einsum("bhij,bjhd->bihd", e, v) / e.astype(np.float64).sum(-1)[..., None].transpose(0, 2, 1, 3)
+        return self._lin(o.reshape(B, L, D).astype(np.float32), p + "attn.o")
+
+    def _layer(self, X, p, lens, n1, n2):
+        X = X + self._attn(self._ln(X, p + n1), p, lens)
+        return X + self._lin(self._lin(self._ln(X, p + n2), p + "ffn.w1", 1), p + "ffn.w2")
+
+    def encode_padded(self, ids, mask):
+        c = self.cfg
+        ids = np.asarray(ids, np.int64)
+        B, L = ids.shape
+        lens = np.asarray(mask, np.int64).sum(1)
+        pos = np.minimum(np.arange(L), c.max_positions - 1)
+        X = self.t["sj.embeddings.word.weight"][ids] + self.t["sj.embeddings.position.weight"][pos][None]
+        X = self._ln(X, "sj.embeddings.norm")
+        for i in range(c.num_layers):
+            X = self._layer(X, f"sj.encoder.layers.{i}.", lens, "attn_norm", "ffn_norm")
+        return self._ln(X, "sj.encoder.final_norm")
+
+    def forward_padded(self, ids, mask, marker_pos, marker_mask, qtype):
+        c = self.cfg
+        h = self.encode_padded(ids, mask)
+        B, L, D = h.shape
+        lens = np.asarray(mask, np.int64).sum(1)
+        h = h + self.t["sj.type_emb.weight"][np.asarray(qtype, np.int64)][:, None, :]
+        for i in range(c.head_layers):
+            h = self._layer(h, f"sj.head.layers.{i}.", lens, "norm1", "norm2")
+        pos = np.clip(np.asarray(marker_pos, np.int64), 0, L - 1)
+        m = h[np.arange(B)[:, None], pos]                                   # [B, K, D]
+        s = self._lin(self._lin(self._ln(m, "sj.scorer.norm"), "sj.scorer.w1", 1), "sj.scorer.w2")
+        logits = np.where(np.asarray(marker_mask) != 0, s[..., 0], np.float32(-1e4)).astype(np.float32)
+        mx = logits.max(1, keepdims=True)
+        e = np.exp((logits - mx).astype(np.float32)).astype(np.float64)
+        top1 = (e / e.sum(1, keepdims=True)).max(1)
+        return logits, np.stack([top1, 1.0 - top1], 1).astype(np.float32)
+
+
+class RefSjModel:
+    """The reference SjModel (src/sj_model.cpp), loaded from an sj_config.json +
+    model.safetensors directory: encode (:257-275) and forward (:277-368)."""
+
+    def __init__(self, ckpt_dir: str, hidden_size: int, noblas: bool = False):
+        self.lib = _ref(noblas)
+        self.D = hidden_size
+        self.h = self.lib.sjref_sj_load(ckpt_dir.encode())
+        if not self.h:
+            raise RuntimeError(self.lib.sjref_last_error().decode())
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            self.lib.sjref_sj_free(self.h)
+            self.h = None
+
+    def encode(self, ids, mask):
+        ids = np.ascontiguousarray(ids, np.int64)
+        mask = np.ascontiguousarray(mask, np.int64)
+        B, L = ids.shape
+        out = np.empty((B, L, self.D), np.float32)
+        if self.lib.sjref_sj_encode(self.h, _ip(ids), _ip(mask), B, L, self.D, _fp(out)) != 0:
+            raise RuntimeError(self.lib.sjref_last_error().decode())
+        return out
+
+    def forward(self, ids, mask, marker_pos, marker_mask, qtype):
+        ids = np.ascontiguousarray(ids, np.int64)
+        mask = np.ascontiguousarray(mask, np.int64)
+        mp = np.ascontiguousarray(marker_pos, np.int64)
+        mm = np.ascontiguousarray(marker_mask, np.uint8)
+        qt = np.ascontiguousarray(qtype, np.int64)
+        B, L = ids.shape
+        K = mp.shape[1]
+        logits = np.empty((B, K), np.float32)
+        act = np.empty((B, 2), np.float32)
+        if self.lib.sjref_sj_forward(self.h, _ip(ids), _ip(mask), B, L, _ip(mp),
+                                     mm.ctypes.data_as(_U8), K, _ip(qt), _fp(logits),
+                                     _fp(act)) != 0:
             raise RuntimeError(self.lib.sjref_last_error().decode())
         return logits, act
 

@@ -7,6 +7,8 @@
 // reference arm times it.  The product library never links it.
 //
 // Entry points wrap, one to one:
+//   sjref_sj_*     SjModel (src/sj_model.cpp): load from sj_config.json +
+//                  model.safetensors (:88-204), encode (:257-275), forward (:277-368)
 //   sjref_load     Agent::Agent's loading steps (src/agent.cpp:40-85):
 //                  rl_agent_config.json + encoder/config.json + model.safetensors
 //                  -> DecisionModel::load (src/model.cpp:35-205)
@@ -23,6 +25,7 @@
 #include "nlohmann/json.hpp"
 #include "snapjudge/model.hpp"
 #include "snapjudge/safetensors.hpp"
+#include "snapjudge/sj_model.hpp"
 #include "snapjudge/tensor.hpp"
 
 using nlohmann::json;
@@ -113,6 +116,69 @@ int sjref_forward(void* h, const int64_t* ids, const int64_t* mask, int64_t B, i
     for (int64_t b = 0; b < B; ++b) {
       std::memcpy(logits + b * K, lo[b].data(), sizeof(float) * K);
       std::memcpy(act + b * na, ao[b].data(), sizeof(float) * na);
+    }
+    return 0;
+  } catch (const std::exception& e) {
+    g_err = e.what();
+    return -1;
+  }
+}
+
+// ---- SjModel (src/sj_model.cpp) ----
+void* sjref_sj_load(const char* dir) {
+  try {
+    std::string d(dir);
+    json cfg = read_json(d + "/sj_config.json");
+    SafeTensors w = SafeTensors::load(d + "/model.safetensors");
+    return SjModel::load(cfg, w, d).release();
+  } catch (const std::exception& e) {
+    g_err = e.what();
+    return nullptr;
+  }
+}
+
+void sjref_sj_free(void* h) { delete static_cast<SjModel*>(h); }
+
+int sjref_sj_encode(void* h, const int64_t* ids, const int64_t* mask, int64_t B, int64_t L,
+                    int64_t D, float* out) {
+  try {
+    auto* m = static_cast<SjModel*>(h);
+    std::vector<std::vector<int64_t>> vi(static_cast<size_t>(B)), vm(static_cast<size_t>(B));
+    for (int64_t b = 0; b < B; ++b) {
+      vi[b].assign(ids + b * L, ids + (b + 1) * L);
+      vm[b].assign(mask + b * L, mask + (b + 1) * L);
+    }
+    auto hs = m->encode(vi, vm);
+    for (int64_t b = 0; b < B; ++b)
+      for (int64_t i = 0; i < L; ++i)
+        std::memcpy(out + (b * L + i) * D, hs[b][i].data(), sizeof(float) * D);
+    return 0;
+  } catch (const std::exception& e) {
+    g_err = e.what();
+    return -1;
+  }
+}
+
+// act [B, 2]
+int sjref_sj_forward(void* h, const int64_t* ids, const int64_t* mask, int64_t B, int64_t L,
+                     const int64_t* marker_pos, const uint8_t* marker_mask, int64_t K,
+                     const int64_t* qtype, float* logits, float* act) {
+  try {
+    auto* m = static_cast<SjModel*>(h);
+    std::vector<std::vector<int64_t>> vi(B), vm(B), mp(B);
+    std::vector<std::vector<uint8_t>> mm(B);
+    for (int64_t b = 0; b < B; ++b) {
+      vi[b].assign(ids + b * L, ids + (b + 1) * L);
+      vm[b].assign(mask + b * L, mask + (b + 1) * L);
+      mp[b].assign(marker_pos + b * K, marker_pos + (b + 1) * K);
+      mm[b].assign(marker_mask + b * K, marker_mask + (b + 1) * K);
+    }
+    std::vector<int64_t> qt(qtype, qtype + B);
+    std::vector<std::vector<float>> lo, ao;
+    m->forward(vi, vm, mp, mm, qt, lo, ao);
+    for (int64_t b = 0; b < B; ++b) {
+      std::memcpy(logits + b * K, lo[b].data(), sizeof(float) * K);
+      std::memcpy(act + b * 2, ao[b].data(), sizeof(float) * 2);
     }
     return 0;
   } catch (const std::exception& e) {

@@ -20,6 +20,8 @@ SJ_ERR_TIMEOUT = -4
 SJ_ERR_STATE = -5
 SJ_PREC_BF16 = 0
 SJ_PREC_FP32 = 1
+SJ_ARCH_MODERNBERT = 0
+SJ_ARCH_SJMODEL = 1
 
 # every symbol declared in include/snapjudge_b200.h
 EXPORTS = ["sj_b200_version", "sj_last_error", "sj_gemm", "sj_gemm_geglu", "sj_add_ln", "sj_rope",
@@ -46,7 +48,7 @@ class FastConfig(C.Structure):
                 ("norm_eps", C.c_float), ("local_attention", C.c_int),
                 ("layer_sliding", C.POINTER(C.c_int)), ("rope_theta_full", C.c_double),
                 ("rope_theta_sliding", C.c_double), ("precision", C.c_int),
-                ("device", C.c_int), ("max_tokens", C.c_int)]
+                ("device", C.c_int), ("max_tokens", C.c_int), ("arch", C.c_int)]
 
 
 _LIB = None

@@ -188,3 +188,67 @@ def save_checkpoint(path: str, cfg: EncoderConfig, tensors: dict[str, np.ndarray
     with open(os.path.join(path, "encoder", "config.json"), "w") as f:
         json.dump(cfg.to_json(), f, indent=1)
     write_safetensors(os.path.join(path, "model.safetensors"), tensors)
+
+
+# ---------------------------------------------------------------- SjModel
+@dataclass
+class SjConfig:
+    """SjModel hyper-parameters, read as ``SjModel::load`` reads ``sj_config.json``
+    (reference ``src/sj_model.cpp:88-110``): a BERT-style pre-LN encoder with
+    learned positions, separate biased q/k/v/o projections and a biased GELU FFN."""
+    vocab_size: int
+    hidden_size: int
+    num_layers: int
+    num_heads: int
+    intermediate_size: int = 0     # 0 -> 4 * hidden_size
+    max_positions: int = 512
+    norm_eps: float = 1e-5
+    head_layers: int = 1
+    head_intermediate: int = 0     # 0 -> 4 * hidden_size
+    n_types: int = 3
+
+    def __post_init__(self):
+        if self.intermediate_size <= 0:
+            self.intermediate_size = 4 * self.hidden_size
+        if self.head_intermediate <= 0:
+            self.head_intermediate = 4 * self.hidden_size
+
+    def to_json(self) -> dict:
+        return {"vocab_size": self.vocab_size, "hidden_size": self.hidden_size,
+                "num_layers": self.num_layers, "num_heads": self.num_heads,
+                "intermediate_size": self.intermediate_size,
+                "max_positions": self.max_positions, "norm_eps": self.norm_eps,
+                "head_layers": self.head_layers, "head_intermediate": self.head_intermediate,
+                "n_types": self.n_types}
+
+    @classmethod
+    def from_json(cls, j: dict) -> "SjConfig":
+        for k in ("vocab_size", "hidden_size", "num_layers", "num_heads"):
+            if k not in j:
+                raise ValueError("config missing required keys "
+                                 "(vocab_size/hidden_size/num_layers/num_heads)")
+        D = int(j["hidden_size"])
+        return cls(vocab_size=int(j["vocab_size"]), hidden_size=D,
+                   num_layers=int(j["num_layers"]), num_heads=int(j["num_heads"]),
+                   intermediate_size=int(j.get("intermediate_size", 4 * D)),
+                   max_positions=int(j.get("max_positions", 512)),
+                   norm_eps=float(j.get("norm_eps", 1e-5)),
+                   head_layers=int(j.get("head_layers", 1)),
+                   head_intermediate=int(j.get("head_intermediate", 4 * D)),
+                   n_types=int(j.get("n_types", 3)))
+
+
+def load_sj_checkpoint(path: str) -> tuple[SjConfig, dict[str, np.ndarray]]:
+    """Load (config, fp32 tensors) from an SjModel directory (sj_config.json +
+    model.safetensors)."""
+    with open(os.path.join(path, "sj_config.json")) as f:
+        cfg = SjConfig.from_json(json.load(f))
+    return cfg, read_safetensors(os.path.join(path, "model.safetensors"))
+
+
+def save_sj_checkpoint(path: str, cfg: SjConfig, tensors: dict[str, np.ndarray]) -> None:
+    """Write an SjModel directory loadable by the reference ``SjModel::load``."""
+    os.makedirs(path, exist_ok=True)
+    with open(os.path.join(path, "sj_config.json"), "w") as f:
+        json.dump(cfg.to_json(), f, indent=1)
+    write_safetensors(os.path.join(path, "model.safetensors"), tensors)

@@ -2,7 +2,9 @@
 //
 // Device-resident replacement of the reference FastSnapjudge
 // (include/snapjudge/fast.hpp:15-31, cuda/fast.cpp) running the encoder half
-// of DecisionModel (src/model.cpp:222-307) on packed variable-length batches:
+// of DecisionModel (src/model.cpp:222-307) on packed variable-length batches
+// (and, with SJ_ARCH_SJMODEL, SjModel's encoder, src/sj_model.cpp:206-255:
+// learned positions, biased LNs and q/k/v/o, GELU FFN, no RoPE):
 //
 //   pos  = position of each packed row (rope.cu)
 //   X    = LN(emb[ids]) (fp32 residual stream), Y = act(X)       (norm.cu)
@@ -58,6 +60,10 @@ struct LayerDev {
   void* wo2 = nullptr;         // [D, F]
   int window = 0;
   bool sliding = false;
+  // SjModel (src/sj_model.cpp:127-151): LN biases, q/k/v concatenated into
+  // wqkv with bias bqkv [3D], Wo bias, wi = ffn.w1 [F, D] + b1, wo2 = ffn.w2 + b2
+  float *attn_norm_b = nullptr, *mlp_norm_b = nullptr;
+  float *bqkv = nullptr, *bo = nullptr, *b1 = nullptr, *b2 = nullptr;
 };
 
 // One pre-norm TransformerEncoderLayer of the decision head (model.cpp:134-152):
@@ -82,6 +88,7 @@ struct DmPass {
 
 struct sj_fast {
   sj_fast_config cfg{};
+  int arch = SJ_ARCH_MODERNBERT;
   std::vector<int> sliding;
   int D = 0, H = 0, Dh = 0, F = 0, V = 0, NL = 0;
   int max_tokens = 0;
@@ -105,9 +112,14 @@ struct sj_fast {
   sjb::HeadSpec spec{};
   bool has_heads = false;
   float *head_w = nullptr, *head_b = nullptr;
-  // decision-model tail of DecisionModel::forward (model.cpp:402-535)
+  // SjModel: learned positions, biased embedding and final LNs
+  float *pos_emb = nullptr, *emb_norm_b = nullptr, *final_norm_b = nullptr;
+  // decision-model tail of DecisionModel::forward (model.cpp:402-535) or
+  // SjModel::forward (sj_model.cpp:277-368)
   bool has_dm = false;
   int n_act = 0;
+  int n_types = 3;    // rows of the type embedding
+  int head_ffn = 0;   // FFN width of the head layers (4D, or SjModel's head_intermediate)
   std::vector<HeadLayerDev> hlayers;
   float* type_emb = nullptr;  // [3, D]
   float *sc_lnw = nullptr, *sc_lnb = nullptr, *sc_w1 = nullptr, *sc_b1 = nullptr,
@@ -251,6 +263,7 @@ struct sj_fast {
   }
 
   int commit();
+  int load_sjmodel();
   template <typename T>
   int forward(const int64_t* d_ids, const int32_t* d_cu, const int32_t* hcu,
               const int32_t* d_kvl, int B, int ntok, float* d_hidden, float* d_probs,
@@ -289,6 +302,9 @@ int sj_fast::commit() {
   if (rc != cudaSuccess) return cuda_fail(rc, "cudaSetDevice");
   const HostTensor* t = nullptr;
   int s;
+  if (arch == SJ_ARCH_SJMODEL) {
+    if ((s = load_sjmodel())) return s;
+  } else {
   if ((s = require("encoder.embeddings.tok_embeddings.weight", {V, D}, &t))) return s;
   if ((s = upload_f32(t, &emb))) return s;
   if ((s = require("encoder.embeddings.norm.weight", {D}, &t))) return s;
@@ -347,6 +363,7 @@ int sj_fast::commit() {
       if ((s = upload_f32(&sn, which == 0 ? &sin_f : &sin_s))) return s;
     }
   }
+  }  // SJ_ARCH_MODERNBERT
   // decision heads
   if (has_heads) {
     HostTensor w, b;
@@ -362,7 +379,8 @@ int sj_fast::commit() {
   }
   // decision-model tail (model.cpp:130-176), when the checkpoint has one: the
   // type embedding, head TransformerEncoderLayers, scorer and act head
-  if (get("type_emb.weight")) {
+  if (arch == SJ_ARCH_MODERNBERT && get("type_emb.weight")) {
+    head_ffn = 4 * D;
     if ((s = require("type_emb.weight", {3, D}, &t))) return s;
     if ((s = upload_f32(t, &type_emb))) return s;
     for (int i = 0; get("head.layers." + std::to_string(i) + ".norm1.weight"); ++i) {
@@ -423,7 +441,7 @@ int sj_fast::commit() {
   max_tiles = max_tokens / 64 + max_tokens + 1;
   if ((rc = dalloc(&X, T * D)) || (rc = dalloc((char**)&Y, T * D * es)) ||
       (rc = dalloc((char**)&QKV, T * 3 * D * es)) || (rc = dalloc((char**)&O, T * D * es)) ||
-      (rc = dalloc((char**)&G, T * (hlayers.empty() ? F : std::max(F, 4 * D)) * es)) ||
+      (rc = dalloc((char**)&G, T * (hlayers.empty() ? F : std::max(F, head_ffn)) * es)) ||
       (rc = dalloc(&pos, T)) || (rc = dalloc(&ids, T)) ||
       (rc = dalloc(&cu, T + 1)) || (rc = dalloc(&kvl, T)) || (rc = dalloc(&tiles, max_tiles)) ||
       (rc = dalloc(&Hc, T * D)) || (rc = dalloc(&probs, T * (size_t)std::max(1, spec.n_total))) ||
@@ -440,6 +458,96 @@ int sj_fast::commit() {
   if ((rc = cudaEventRecord(staged_ev, stream))) return cuda_fail(rc, "cudaEventRecord");
   staged.clear();
   committed = true;
+  return SJ_OK;
+}
+
+// SjModel weights (src/sj_model.cpp:117-202), "sj.*" names and shapes; q/k/v
+// are concatenated into one [3D, D] projection (bias [3D]) so that the QKV GEMM
+// and the attention kernel are the DecisionModel encoder's.
+int sj_fast::load_sjmodel() {
+  const HostTensor* t = nullptr;
+  int s;
+  const int64_t d = D;
+  auto f32 = [&](const std::string& n, std::vector<int64_t> shape, float** dst) -> int {
+    int r = require(n, std::move(shape), &t);
+    return r ? r : upload_f32(t, dst);
+  };
+  auto wgt = [&](const std::string& n, std::vector<int64_t> shape, void** dst) -> int {
+    int r = require(n, std::move(shape), &t);
+    return r ? r : upload_w(t, dst);
+  };
+  // q, k, v of one attention block -> [3D, D] weight + [3D] bias
+  auto qkv = [&](const std::string& p, void** w, float** b) -> int {
+    HostTensor cw, cb;
+    cw.shape = {3 * d, d};
+    cb.shape = {3 * d};
+    for (const char* x : {"q", "k", "v"}) {
+      int r = require(p + "attn." + x + ".weight", {d, d}, &t);
+      if (r) return r;
+      cw.data.insert(cw.data.end(), t->data.begin(), t->data.end());
+      if ((r = require(p + "attn." + x + ".bias", {d}, &t))) return r;
+      cb.data.insert(cb.data.end(), t->data.begin(), t->data.end());
+    }
+    int r = upload_w(&cw, w);
+    return r ? r : upload_f32(&cb, b);
+  };
+  if ((s = f32("sj.embeddings.word.weight", {V, d}, &emb)) ||
+      (s = f32("sj.embeddings.position.weight", {cfg.max_position_embeddings, d}, &pos_emb)) ||
+      (s = f32("sj.embeddings.norm.weight", {d}, &emb_norm)) ||
+      (s = f32("sj.embeddings.norm.bias", {d}, &emb_norm_b)))
+    return s;
+  layers.resize(NL);
+  for (int i = 0; i < NL; ++i) {
+    LayerDev& ly = layers[i];
+    const std::string p = "sj.encoder.layers." + std::to_string(i) + ".";
+    if ((s = f32(p + "attn_norm.weight", {d}, &ly.attn_norm)) ||
+        (s = f32(p + "attn_norm.bias", {d}, &ly.attn_norm_b)) ||
+        (s = qkv(p, &ly.wqkv, &ly.bqkv)) || (s = wgt(p + "attn.o.weight", {d, d}, &ly.wo)) ||
+        (s = f32(p + "attn.o.bias", {d}, &ly.bo)) ||
+        (s = f32(p + "ffn_norm.weight", {d}, &ly.mlp_norm)) ||
+        (s = f32(p + "ffn_norm.bias", {d}, &ly.mlp_norm_b)) ||
+        (s = wgt(p + "ffn.w1.weight", {F, d}, &ly.wi)) || (s = f32(p + "ffn.w1.bias", {F}, &ly.b1)) ||
+        (s = wgt(p + "ffn.w2.weight", {d, F}, &ly.wo2)) || (s = f32(p + "ffn.w2.bias", {d}, &ly.b2)))
+      return s;
+  }
+  if ((s = f32("sj.encoder.final_norm.weight", {d}, &final_norm)) ||
+      (s = f32("sj.encoder.final_norm.bias", {d}, &final_norm_b)))
+    return s;
+  // the forward tail (sj_model.cpp:293-368), when present
+  const HostTensor* te = get("sj.type_emb.weight");
+  if (te) {
+    if (te->shape.size() != 2 || te->shape[1] != d || te->shape[0] < 1)
+      return fail(SJ_ERR_INVALID, "Model 'sj.type_emb.weight' must be [n_types, D]");
+    n_types = (int)te->shape[0];
+    if ((s = upload_f32(te, &type_emb))) return s;
+    for (int i = 0; get("sj.head.layers." + std::to_string(i) + ".norm1.weight"); ++i) {
+      HeadLayerDev hl;
+      const std::string p = "sj.head.layers." + std::to_string(i) + ".";
+      const HostTensor* w1 = get(p + "ffn.w1.weight");
+      if (!w1 || w1->shape.size() != 2 || w1->shape[1] != d)
+        return fail(SJ_ERR_INVALID, "Model '" + p + "ffn.w1.weight' must be [head_intermediate, D]");
+      const int64_t fh = w1->shape[0];
+      if (i == 0) head_ffn = (int)fh;
+      if (fh != head_ffn) return fail(SJ_ERR_INVALID, "head layers of different FFN widths");
+      if ((s = f32(p + "norm1.weight", {d}, &hl.n1w)) || (s = f32(p + "norm1.bias", {d}, &hl.n1b)) ||
+          (s = f32(p + "norm2.weight", {d}, &hl.n2w)) || (s = f32(p + "norm2.bias", {d}, &hl.n2b)) ||
+          (s = qkv(p, &hl.in_w, &hl.in_b)) || (s = wgt(p + "attn.o.weight", {d, d}, &hl.out_w)) ||
+          (s = f32(p + "attn.o.bias", {d}, &hl.out_b)) ||
+          (s = wgt(p + "ffn.w1.weight", {fh, d}, &hl.l1w)) || (s = f32(p + "ffn.w1.bias", {fh}, &hl.l1b)) ||
+          (s = wgt(p + "ffn.w2.weight", {d, fh}, &hl.l2w)) || (s = f32(p + "ffn.w2.bias", {d}, &hl.l2b)))
+        return s;
+      hlayers.push_back(hl);
+    }
+    if ((s = f32("sj.scorer.norm.weight", {d}, &sc_lnw)) ||
+        (s = f32("sj.scorer.norm.bias", {d}, &sc_lnb)) ||
+        (s = f32("sj.scorer.w1.weight", {d, d}, &sc_w1)) ||
+        (s = f32("sj.scorer.w1.bias", {d}, &sc_b1)) ||
+        (s = f32("sj.scorer.w2.weight", {1, d}, &sc_w2)) ||
+        (s = f32("sj.scorer.w2.bias", {1}, &sc_b2)))
+      return s;
+    n_act = 2;
+    has_dm = true;
+  }
   return SJ_OK;
 }
 
@@ -511,11 +619,15 @@ int sj_fast::forward(const int64_t* d_ids, const int32_t* d_cu, const int32_t* h
   const float eps = cfg.norm_eps;
   SJ_LAUNCH(SJ_K_FINAL, sjb::positions(d_cu, B, ntok, pos, nullptr, st));
   const bool y0 = !layers.empty() && !layers[0].attn_norm;
-  SJ_LAUNCH(SJ_K_EMBED, sjb::embed_ln<T>(d_ids, ntok, emb, V, D, emb_norm, eps, X, y0 ? Yt : nullptr, dflags, st));
+  SJ_LAUNCH(SJ_K_EMBED, sjb::embed_ln<T>(d_ids, ntok, emb, V, D, emb_norm, eps, X, y0 ? Yt : nullptr,
+                                         dflags, st, pos_emb, pos, cfg.max_position_embeddings,
+                                         emb_norm_b));
+  const bool sjm = arch == SJ_ARCH_SJMODEL;
 
   auto gemm = [&](int cls, const T* A, const void* W, T* C, float* resid, int N, int K, int epi,
-                  const float* ct, const float* stb) -> int {
-    return gemm_any<T>(cls, A, W, nullptr, 0, C, resid, ntok, N, K, epi, ct, stb, st);
+                  const float* ct, const float* stb, const float* bias = nullptr,
+                  int act = 0) -> int {
+    return gemm_any<T>(cls, A, W, bias, act, C, resid, ntok, N, K, epi, ct, stb, st);
   };
 
   int s;
@@ -523,14 +635,21 @@ int sj_fast::forward(const int64_t* d_ids, const int32_t* d_cu, const int32_t* h
     const LayerDev& ly = layers[li];
     const T* Yin = Yt;
     if (ly.attn_norm) {
-      SJ_LAUNCH(SJ_K_LN, (sjb::add_ln<T, T>(X, nullptr, ly.attn_norm, nullptr, Yt, ntok, D, eps, nullptr, st)));
+      SJ_LAUNCH(SJ_K_LN, (sjb::add_ln<T, T>(X, nullptr, ly.attn_norm, ly.attn_norm_b, Yt, ntok, D, eps,
+                                          nullptr, st)));
     } else if (li > 0) {
       if constexpr (kBf16) SJ_LAUNCH(SJ_K_LN, sjb::cast_bf16(X, Yt, (int64_t)ntok * D, st));
       else Yin = reinterpret_cast<const T*>(X);
     }
     const float* ct = ly.sliding ? cos_s : cos_f;
     const float* stb = ly.sliding ? sin_s : sin_f;
-    if ((s = gemm(SJ_K_QKV, Yin, ly.wqkv, Qt, nullptr, 3 * D, D, sjb::TC_ROPE, ct, stb))) return s;
+    if (sjm) {  // SjModel: biased q/k/v, no RoPE
+      if ((s = gemm(SJ_K_QKV, Yin, ly.wqkv, Qt, nullptr, 3 * D, D, sjb::TC_STORE, nullptr, nullptr,
+                    ly.bqkv)))
+        return s;
+    } else if ((s = gemm(SJ_K_QKV, Yin, ly.wqkv, Qt, nullptr, 3 * D, D, sjb::TC_ROPE, ct, stb))) {
+      return s;
+    }
     if (tc_attn) {
       if constexpr (kBf16)
         SJ_LAUNCH(SJ_K_ATTN, sjb::attn_tc(Qt, d_cu, d_kvl, Ot, ntok, H, ly.window, tiles, nt, B, 0, dflags + 2,
@@ -538,15 +657,24 @@ int sj_fast::forward(const int64_t* d_ids, const int32_t* d_cu, const int32_t* h
     } else {
       SJ_LAUNCH(SJ_K_ATTN, sjb::attn_simt<T>(Qt, d_cu, d_kvl, Ot, H, Dh, ly.window, tiles, nt, B, 0, st));
     }
-    if ((s = gemm(SJ_K_WO, Ot, ly.wo, nullptr, X, D, D, sjb::TC_RESID, nullptr, nullptr))) return s;
-    SJ_LAUNCH(SJ_K_LN, (sjb::add_ln<T, T>(X, nullptr, ly.mlp_norm, nullptr, Yt, ntok, D, eps, nullptr, st)));
-    if ((s = gemm(SJ_K_GEGLU, Yt, ly.wi, Gt, nullptr, F, D, sjb::TC_GEGLU, nullptr, nullptr))) return s;
-    if ((s = gemm(SJ_K_WO2, Gt, ly.wo2, nullptr, X, D, F, sjb::TC_RESID, nullptr, nullptr))) return s;
+    if ((s = gemm(SJ_K_WO, Ot, ly.wo, nullptr, X, D, D, sjb::TC_RESID, nullptr, nullptr, ly.bo)))
+      return s;
+    SJ_LAUNCH(SJ_K_LN, (sjb::add_ln<T, T>(X, nullptr, ly.mlp_norm, ly.mlp_norm_b, Yt, ntok, D, eps,
+                                        nullptr, st)));
+    if (sjm) {  // SjModel: G = gelu(Y W1^T + b1), X += G W2^T + b2
+      if ((s = gemm(SJ_K_GEGLU, Yt, ly.wi, Gt, nullptr, F, D, sjb::TC_STORE, nullptr, nullptr, ly.b1,
+                    sjb::ACT_GELU)))
+        return s;
+    } else if ((s = gemm(SJ_K_GEGLU, Yt, ly.wi, Gt, nullptr, F, D, sjb::TC_GEGLU, nullptr, nullptr))) {
+      return s;
+    }
+    if ((s = gemm(SJ_K_WO2, Gt, ly.wo2, nullptr, X, D, F, sjb::TC_RESID, nullptr, nullptr, ly.b2)))
+      return s;
   }
   // final norm (+ LoRA): all rows -> d_hidden, [CLS] rows -> heads
   if (d_hidden) {
-    SJ_LAUNCH(SJ_K_FINAL, (sjb::add_ln<float, float>(X, nullptr, final_norm, nullptr, d_hidden, ntok, D, eps,
-                                         nullptr, st)));
+    SJ_LAUNCH(SJ_K_FINAL, (sjb::add_ln<float, float>(X, nullptr, final_norm, final_norm_b, d_hidden, ntok,
+                                                     D, eps, nullptr, st)));
     if (lora_r > 0) {
       SJ_LAUNCH(SJ_K_FINAL, (sjb::gemm_simt<float, float>(d_hidden, lora_a, nullptr, z, nullptr, ntok, lora_r, D,
                                               0, false, st)));
@@ -556,7 +684,8 @@ int sj_fast::forward(const int64_t* d_ids, const int32_t* d_cu, const int32_t* h
     if (dm && (s = head_forward<T>(d_cu, d_kvl, B, ntok, nt, d_hidden, *dm, st))) return s;
   }
   if (d_probs && has_heads) {
-    SJ_LAUNCH(SJ_K_FINAL, (sjb::add_ln<float, float>(X, nullptr, final_norm, nullptr, Hc, B, D, eps, d_cu, st)));
+    SJ_LAUNCH(SJ_K_FINAL, (sjb::add_ln<float, float>(X, nullptr, final_norm, final_norm_b, Hc, B, D, eps,
+                                                     d_cu, st)));
     if (lora_r > 0) {
       SJ_LAUNCH(SJ_K_FINAL, (sjb::gemm_simt<float, float>(Hc, lora_a, nullptr, z, nullptr, B, lora_r, D, 0,
                                               false, st)));
@@ -587,9 +716,14 @@ int sj_fast::head_forward(const int32_t* d_cu, const int32_t* d_kvl, int B, int 
   T* Ot = static_cast<T*>(O);
   T* Ft = static_cast<T*>(G);
   int s;
+  // DecisionModel's head: LN eps 1e-5, ReLU FFN of 4D (model.cpp:419-459);
+  // SjModel's: the config eps, GELU FFN of head_intermediate (sj_model.cpp:303-321)
+  const bool sjm = arch == SJ_ARCH_SJMODEL;
+  const float heps = sjm ? cfg.norm_eps : 1e-5f;
+  const int ffn_act = sjm ? sjb::ACT_GELU : sjb::ACT_RELU;
   SJ_LAUNCH(SJ_K_FINAL, sjb::type_emb_add(h, d_cu, B, dm.qtype, type_emb, D, ntok, st));
   for (const HeadLayerDev& hl : hlayers) {
-    SJ_LAUNCH(SJ_K_LN, (sjb::add_ln<T, T>(h, nullptr, hl.n1w, hl.n1b, Yt, ntok, D, 1e-5f, nullptr, st)));
+    SJ_LAUNCH(SJ_K_LN, (sjb::add_ln<T, T>(h, nullptr, hl.n1w, hl.n1b, Yt, ntok, D, heps, nullptr, st)));
     if ((s = gemm_any<T>(SJ_K_QKV, Yt, hl.in_w, hl.in_b, 0, Qt, nullptr, ntok, 3 * D, D,
                          sjb::TC_STORE, nullptr, nullptr, st)))
       return s;
@@ -603,11 +737,11 @@ int sj_fast::head_forward(const int32_t* d_cu, const int32_t* d_kvl, int B, int 
     if ((s = gemm_any<T>(SJ_K_WO, Ot, hl.out_w, hl.out_b, 0, nullptr, h, ntok, D, D, sjb::TC_RESID,
                          nullptr, nullptr, st)))
       return s;
-    SJ_LAUNCH(SJ_K_LN, (sjb::add_ln<T, T>(h, nullptr, hl.n2w, hl.n2b, Yt, ntok, D, 1e-5f, nullptr, st)));
-    if ((s = gemm_any<T>(SJ_K_GEGLU, Yt, hl.l1w, hl.l1b, sjb::ACT_RELU, Ft, nullptr, ntok, 4 * D, D,
+    SJ_LAUNCH(SJ_K_LN, (sjb::add_ln<T, T>(h, nullptr, hl.n2w, hl.n2b, Yt, ntok, D, heps, nullptr, st)));
+    if ((s = gemm_any<T>(SJ_K_GEGLU, Yt, hl.l1w, hl.l1b, ffn_act, Ft, nullptr, ntok, head_ffn, D,
                          sjb::TC_STORE, nullptr, nullptr, st)))
       return s;
-    if ((s = gemm_any<T>(SJ_K_WO2, Ft, hl.l2w, hl.l2b, 0, nullptr, h, ntok, D, 4 * D, sjb::TC_RESID,
+    if ((s = gemm_any<T>(SJ_K_WO2, Ft, hl.l2w, hl.l2b, 0, nullptr, h, ntok, D, head_ffn, sjb::TC_RESID,
                          nullptr, nullptr, st)))
       return s;
   }
@@ -621,7 +755,7 @@ int sj_fast::head_forward(const int32_t* d_cu, const int32_t* d_kvl, int B, int 
   SJ_LAUNCH(SJ_K_FINAL, (sjb::gemm_simt<float, float>(dm_s1, sc_w2, sc_b2, dm_s2, nullptr, BK, 1, D,
                                                       0, false, st)));
   SJ_LAUNCH(SJ_K_FINAL, sjb::act_head(h, d_cu, B, dm_s2, dm.mask, dm.K, act_w1, act_b1, act_w2,
-                                      act_b2, n_act, D, dm.logits, dm.act, st));
+                                      act_b2, n_act, D, dm.logits, dm.act, sjm, st));
   return SJ_OK;
 }
 
@@ -635,7 +769,9 @@ int sj_fast::run(const int64_t* d_ids, const int32_t* d_cu, const int32_t* hcu,
   for (int b = 0; b < B; ++b) {
     const int n = hcu[b + 1] - hcu[b];
     if (n < 0) return fail(SJ_ERR_INVALID, "cu_seqlens must be non-decreasing");
-    if (n > cfg.max_position_embeddings)
+    // RoPE tables end at max_position_embeddings; SjModel clamps its learned
+    // positions to the last row instead (sj_model.cpp:228-230)
+    if (arch == SJ_ARCH_MODERNBERT && n > cfg.max_position_embeddings)
       return fail(SJ_ERR_INVALID, "sequence " + std::to_string(b) + " has " + std::to_string(n) +
                                       " tokens > max_position_embeddings " +
                                       std::to_string(cfg.max_position_embeddings));
@@ -732,8 +868,8 @@ int sj_fast::dm_call(const int64_t* ids_h, const int32_t* cu_h, const int32_t* k
                      float* logits_h, float* act_h) {
   if (!committed) return fail(SJ_ERR_STATE, "forward before sj_fast_commit");
   if (!has_dm)
-    return fail(SJ_ERR_STATE, "the checkpoint has no decision-model head (type_emb, head, scorer, "
-                              "act_head)");
+    return fail(SJ_ERR_STATE, "the checkpoint has no decision-model head (type_emb, head, scorer"
+                              "; act_head for DecisionModel)");
   if (B <= 0) return B == 0 ? SJ_OK : fail(SJ_ERR_INVALID, "negative batch");
   if (K < 1 || K > 4096) return fail(SJ_ERR_INVALID, "K (markers per sequence) must be in [1, 4096]");
   if (!cu_h || !ids_h || !pos_h || !mask_h || !qtype_h || !logits_h || !act_h)
@@ -745,8 +881,9 @@ int sj_fast::dm_call(const int64_t* ids_h, const int32_t* cu_h, const int32_t* k
     if (n > max_tokens) return fail(SJ_ERR_INVALID, "sequence longer than max_tokens");
     if (kvl_h && (kvl_h[b] < 0 || kvl_h[b] > n))
       return fail(SJ_ERR_INVALID, "kv_lens[b] must lie in [0, length of segment b]");
-    if (qtype_h[b] < 0 || qtype_h[b] >= 3)
-      return fail(SJ_ERR_INVALID, "qtype " + std::to_string(qtype_h[b]) + " outside [0, 3)");
+    if (qtype_h[b] < 0 || qtype_h[b] >= n_types)
+      return fail(SJ_ERR_INVALID, "qtype " + std::to_string(qtype_h[b]) + " outside [0, " +
+                                      std::to_string(n_types) + ")");
   }
   for (int64_t r = 0; r < cu_h[B]; ++r)
     if (ids_h[r] < 0 || ids_h[r] >= V)
@@ -828,6 +965,10 @@ int sj_fast_create(const sj_fast_config* cfg, sj_fast** out) {
       (c.hidden_size / c.num_attention_heads) % 2 != 0)
     return SJ_ERR_INVALID;
   if (c.precision != SJ_PREC_BF16 && c.precision != SJ_PREC_FP32) return SJ_ERR_UNSUPPORTED;
+  if (c.arch != SJ_ARCH_MODERNBERT && c.arch != SJ_ARCH_SJMODEL) return SJ_ERR_UNSUPPORTED;
+  // SjModel's learned positions are added in the warp-per-row embedding kernel
+  if (c.arch == SJ_ARCH_SJMODEL && (c.hidden_size > 1024 || c.hidden_size % 4 != 0))
+    return SJ_ERR_UNSUPPORTED;
   e->D = c.hidden_size;
   e->H = c.num_attention_heads;
   e->Dh = e->D / e->H;
@@ -837,8 +978,9 @@ int sj_fast_create(const sj_fast_config* cfg, sj_fast** out) {
   e->bf16_mode = c.precision == SJ_PREC_BF16;
   e->max_tokens = c.max_tokens > 0 ? c.max_tokens : (e->bf16_mode ? 262144 : 65536);
   e->max_tokens = std::max(e->max_tokens, 128);
+  e->arch = c.arch;
   e->sliding.assign(e->NL, 0);
-  if (c.layer_sliding)
+  if (c.layer_sliding && c.arch == SJ_ARCH_MODERNBERT)
     for (int i = 0; i < e->NL; ++i) e->sliding[i] = c.layer_sliding[i];
   e->cfg.layer_sliding = nullptr;  // not retained
   if (e->bf16_mode && (e->D % 8 != 0 || e->F % 8 != 0)) return SJ_ERR_UNSUPPORTED;

@@ -41,13 +41,14 @@ __global__ void gather_markers_kernel(const float* __restrict__ h, const int32_t
 // (fp64 sums of fp32 exponentials, model.cpp:490-508), the act features
 // [CLS row, top1, top1 - top2, normalised entropy, k / 255] and the act MLP
 // (Linear(D+4, 256) + GELU, Linear(256, n_act)) with its softmax (:510-533).
+// top1_only: SjModel's act, [top1, 1 - top1] (sj_model.cpp:355-366).
 constexpr int kActThreads = 256;
 __global__ void __launch_bounds__(kActThreads)
     act_head_kernel(const float* __restrict__ h, const int32_t* __restrict__ cu,
                     const float* __restrict__ score, const uint8_t* __restrict__ mask, int K,
                     const float* __restrict__ w1, const float* __restrict__ b1,
                     const float* __restrict__ w2, const float* __restrict__ b2, int n_act, int D,
-                    float* __restrict__ logits, float* __restrict__ act) {
+                    float* __restrict__ logits, float* __restrict__ act, int top1_only) {
   extern __shared__ unsigned char sm_raw[];
   double* p = reinterpret_cast<double*>(sm_raw);       // [K]
   float* feats = reinterpret_cast<float*>(p + K);      // [D + 4]
@@ -84,6 +85,10 @@ __global__ void __launch_bounds__(kActThreads)
       ent -= v * log(v > 1e-9 ? v : 1e-9);
       ks += mask[b * K + k];
     }
+    if (top1_only) {  // SjModel (src/sj_model.cpp:355-366): act = [top1, 1 - top1]
+      act[(int64_t)b * 2] = static_cast<float>(top1);
+      act[(int64_t)b * 2 + 1] = static_cast<float>(1.0 - top1);
+    }
     const double kf = ks > 2.0 ? ks : 2.0;
     ent /= log(kf);
     feats[D] = static_cast<float>(top1);
@@ -92,6 +97,7 @@ __global__ void __launch_bounds__(kActThreads)
     feats[D + 3] = static_cast<float>(kf / 255.0);
   }
   __syncthreads();
+  if (top1_only) return;
   // a1 = gelu(W1 feats + b1): one warp per output, lanes across the D+4 inputs
   for (int j = warp; j < 256; j += kWarps) {
     const float* wr = w1 + (int64_t)j * (D + 4);
@@ -145,7 +151,7 @@ size_t act_head_smem(int K, int D, int n_act) {
 cudaError_t act_head(const float* h, const int32_t* cu, int B, const float* score,
                      const uint8_t* mask, int K, const float* w1, const float* b1,
                      const float* w2, const float* b2, int n_act, int D, float* logits,
-                     float* act, cudaStream_t st) {
+                     float* act, bool top1_only, cudaStream_t st) {
   if (B <= 0) return cudaSuccess;
   const size_t smem = act_head_smem(K, D, n_act);
   if (smem > 48 * 1024) {
@@ -154,7 +160,7 @@ cudaError_t act_head(const float* h, const int32_t* cu, int B, const float* scor
     if (rc != cudaSuccess) return rc;
   }
   act_head_kernel<<<B, kActThreads, smem, st>>>(h, cu, score, mask, K, w1, b1, w2, b2, n_act, D,
-                                                logits, act);
+                                                logits, act, top1_only ? 1 : 0);
   return cudaGetLastError();
 }
 

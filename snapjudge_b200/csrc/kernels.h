@@ -20,11 +20,14 @@ using bf16 = __nv_bfloat16;
 enum Act { ACT_NONE = 0, ACT_GELU = 1, ACT_RELU = 2 };
 
 // ---- norms (norm.cu) ------------------------------------------------------
-// X[T, D] (fp32) = LN(emb[ids]) * w ; Y = cast(X) when Y != null.
-// Out-of-vocabulary ids produce a zero row and set *bad = 1.
+// X[T, D] (fp32) = LN(emb[ids] (+ pos_emb[min(pos, max_pos - 1)])) * w (+ b);
+// Y = cast(X) when Y != null.  Out-of-vocabulary ids produce a zero row and set
+// *bad = 1.  Positions and bias need D <= 1024 (D % 4 == 0).
 template <typename TY>
 cudaError_t embed_ln(const int64_t* ids, int T, const float* emb, int V, int D,
-                     const float* w, float eps, float* X, TY* Y, int* bad, cudaStream_t st);
+                     const float* w, float eps, float* X, TY* Y, int* bad, cudaStream_t st,
+                     const float* pos_emb = nullptr, const int32_t* pos = nullptr,
+                     int max_pos = 0, const float* b = nullptr);
 
 // Optional residual add (X += R), then Y = LN(X) * w (+ b).  With `rows`
 // (length M), output row i normalises X[rows[i]] and no residual is applied.
@@ -91,7 +94,7 @@ size_t act_head_smem(int K, int D, int n_act);
 cudaError_t act_head(const float* h, const int32_t* cu, int B, const float* score,
                      const uint8_t* mask, int K, const float* w1, const float* b1,
                      const float* w2, const float* b2, int n_act, int D, float* logits,
-                     float* act, cudaStream_t st);
+                     float* act, bool top1_only, cudaStream_t st);
 
 // ---- tcgen05 GEMM (gemm_tc.cu) ------------------------------------------------
 // True when the tensor-core GEMM takes this shape (K % 64 == 0, N tiles of 256

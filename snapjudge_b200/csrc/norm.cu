@@ -72,7 +72,10 @@ __global__ void __launch_bounds__(256) embed_ln_warp(const int64_t* __restrict__
                                                      const float* __restrict__ emb, int V, int D,
                                                      const float* __restrict__ w, float eps,
                                                      float* __restrict__ X, TY* __restrict__ Y,
-                                                     int* __restrict__ bad) {
+                                                     int* __restrict__ bad,
+                                                     const float* __restrict__ pos_emb,
+                                                     const int32_t* __restrict__ pos, int max_pos,
+                                                     const float* __restrict__ b) {
   const int lane = threadIdx.x & 31;
   const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (r >= T) return;
@@ -87,6 +90,21 @@ __global__ void __launch_bounds__(256) embed_ln_warp(const int64_t* __restrict__
     v[k] = (ok && c < nc4) ? load4<float>(emb + id * (int64_t)D + 4 * c)
                            : make_float4(0.f, 0.f, 0.f, 0.f);
   }
+  if (pos_emb) {  // learned absolute positions, clamped to the table
+    int p = pos[r];
+    p = p < max_pos ? p : max_pos - 1;
+#pragma unroll
+    for (int k = 0; k < kMaxChunks; ++k) {
+      const int c = lane + 32 * k;
+      if (ok && c < nc4) {
+        const float4 e = load4<float>(pos_emb + (int64_t)p * D + 4 * c);
+        v[k].x += e.x;
+        v[k].y += e.y;
+        v[k].z += e.z;
+        v[k].w += e.w;
+      }
+    }
+  }
   float mean, inv;
   row_stats(v, lane, nc4, D, eps, mean, inv);
 #pragma unroll
@@ -96,6 +114,13 @@ __global__ void __launch_bounds__(256) embed_ln_warp(const int64_t* __restrict__
     float4 g = load4<float>(w + 4 * c);
     float4 o = make_float4((v[k].x - mean) * inv * g.x, (v[k].y - mean) * inv * g.y,
                            (v[k].z - mean) * inv * g.z, (v[k].w - mean) * inv * g.w);
+    if (b) {
+      const float4 bb = load4<float>(b + 4 * c);
+      o.x += bb.x;
+      o.y += bb.y;
+      o.z += bb.z;
+      o.w += bb.w;
+    }
     store4<float>(X + (int64_t)r * D + 4 * c, o);
     if (Y) store4<TY>(Y + (int64_t)r * D + 4 * c, o);
   }
@@ -220,10 +245,14 @@ bool warp_path(int D) { return D % 4 == 0 && D <= 4 * 32 * kMaxChunks; }
 
 template <typename TY>
 cudaError_t embed_ln(const int64_t* ids, int T, const float* emb, int V, int D, const float* w,
-                     float eps, float* X, TY* Y, int* bad, cudaStream_t st) {
+                     float eps, float* X, TY* Y, int* bad, cudaStream_t st, const float* pos_emb,
+                     const int32_t* pos, int max_pos, const float* b) {
   if (T <= 0) return cudaSuccess;
   if (warp_path(D)) {
-    embed_ln_warp<TY><<<(T + 7) / 8, 256, 0, st>>>(ids, T, emb, V, D, w, eps, X, Y, bad);
+    embed_ln_warp<TY><<<(T + 7) / 8, 256, 0, st>>>(ids, T, emb, V, D, w, eps, X, Y, bad, pos_emb,
+                                                    pos, max_pos, b);
+  } else if (pos_emb || b) {
+    return cudaErrorInvalidValue;  // positions / bias: the warp-per-row form (D <= 1024) only
   } else {
     add_ln_block<float, TY><<<T, 128, D * sizeof(float), st>>>(X, nullptr, w, nullptr, Y, T, D,
                                                                eps, nullptr, ids, emb, V, bad);
@@ -251,9 +280,11 @@ cudaError_t cast_bf16(const float* X, bf16* Y, int64_t n, cudaStream_t st) {
 }
 
 template cudaError_t embed_ln<float>(const int64_t*, int, const float*, int, int, const float*,
-                                     float, float*, float*, int*, cudaStream_t);
+                                     float, float*, float*, int*, cudaStream_t,
+                                     const float*, const int32_t*, int, const float*);
 template cudaError_t embed_ln<bf16>(const int64_t*, int, const float*, int, int, const float*,
-                                    float, float*, bf16*, int*, cudaStream_t);
+                                     float, float*, bf16*, int*, cudaStream_t,
+                                     const float*, const int32_t*, int, const float*);
 template cudaError_t add_ln<float, float>(float*, const float*, const float*, const float*,
                                           float*, int, int, float, const int32_t*, cudaStream_t);
 template cudaError_t add_ln<bf16, bf16>(float*, const bf16*, const float*, const float*, bf16*,

@@ -24,7 +24,7 @@ import numpy as np
 
 from . import _lib
 from ._lib import SnapjudgeError, check  # noqa: F401  (re-exported)
-from .checkpoint import EncoderConfig, load_checkpoint
+from .checkpoint import EncoderConfig, SjConfig, load_checkpoint, load_sj_checkpoint
 
 _I64P = C.POINTER(C.c_int64)
 
@@ -36,20 +36,29 @@ def _ptr(a: np.ndarray):
 class FastSnapjudge:
     """One encoder engine resident on one GPU."""
 
-    def __init__(self, cfg: EncoderConfig, tensors: dict[str, np.ndarray], *,
+    def __init__(self, cfg: EncoderConfig | SjConfig, tensors: dict[str, np.ndarray], *,
                  precision: str = "bf16", heads=None, device: int = 0, max_tokens: int = 0):
+        """`cfg` is a DecisionModel encoder config (``EncoderConfig``, tensors
+        "encoder.*" ...) or an SjModel config (``SjConfig``, tensors "sj.*")."""
         L = _lib.lib()
         self.cfg = cfg
         self.precision = precision
         self.D = cfg.hidden_size
-        sl = (C.c_int * max(1, cfg.num_hidden_layers))(
-            *[int(cfg.layer_sliding(i)) for i in range(cfg.num_hidden_layers)])
-        c = _lib.FastConfig(cfg.hidden_size, cfg.num_hidden_layers, cfg.num_attention_heads,
-                            cfg.intermediate_size, cfg.vocab_size, cfg.max_position_embeddings,
-                            cfg.norm_eps, cfg.local_attention, sl, cfg.rope_theta_full,
-                            cfg.rope_theta_sliding,
-                            _lib.SJ_PREC_BF16 if precision == "bf16" else _lib.SJ_PREC_FP32,
-                            device, max_tokens)
+        prec = _lib.SJ_PREC_BF16 if precision == "bf16" else _lib.SJ_PREC_FP32
+        if isinstance(cfg, SjConfig):
+            sl = None
+            c = _lib.FastConfig(cfg.hidden_size, cfg.num_layers, cfg.num_heads,
+                                cfg.intermediate_size, cfg.vocab_size, cfg.max_positions,
+                                cfg.norm_eps, 0, sl, 10000.0, 10000.0, prec, device, max_tokens,
+                                _lib.SJ_ARCH_SJMODEL)
+        else:
+            sl = (C.c_int * max(1, cfg.num_hidden_layers))(
+                *[int(cfg.layer_sliding(i)) for i in range(cfg.num_hidden_layers)])
+            c = _lib.FastConfig(cfg.hidden_size, cfg.num_hidden_layers, cfg.num_attention_heads,
+                                cfg.intermediate_size, cfg.vocab_size, cfg.max_position_embeddings,
+                                cfg.norm_eps, cfg.local_attention, sl, cfg.rope_theta_full,
+                                cfg.rope_theta_sliding, prec, device, max_tokens,
+                                _lib.SJ_ARCH_MODERNBERT)
         if precision not in ("bf16", "fp32"):
             raise ValueError(f"precision must be 'bf16' or 'fp32', got {precision!r}")
         h = C.c_void_p()
@@ -76,6 +85,12 @@ class FastSnapjudge:
     @classmethod
     def from_checkpoint(cls, path: str, **kw) -> "FastSnapjudge":
         cfg, tensors = load_checkpoint(path)
+        return cls(cfg, tensors, **kw)
+
+    @classmethod
+    def from_sj_checkpoint(cls, path: str, **kw) -> "FastSnapjudge":
+        """An SjModel directory (sj_config.json + model.safetensors)."""
+        cfg, tensors = load_sj_checkpoint(path)
         return cls(cfg, tensors, **kw)
 
     def close(self) -> None:

@@ -25,7 +25,7 @@ from dataclasses import dataclass
 
 import numpy as np
 
-from .checkpoint import EncoderConfig
+from .checkpoint import EncoderConfig, SjConfig
 
 # task head kinds
 SOFTMAX = 0
@@ -131,6 +131,63 @@ def make_weights(spec: SynthSpec, std: float = 0.02) -> dict[str, np.ndarray]:
         t[f"task_heads.{i}.weight"] = (rng.standard_normal((h.n_out, D), dtype=np.float32)
                                        * np.float32(1.0 / np.sqrt(D)))
         t[f"task_heads.{i}.bias"] = rng.standard_normal((h.n_out,), dtype=np.float32) * s
+    return t
+
+
+# SjModel (reference src/sj_model.cpp) checkpoints: a tiny one for the committed
+# goldens and one at the C3 width for the tensor-core paths.
+SJ_SPECS: dict[str, tuple[SjConfig, int]] = {
+    "sj_tiny": (SjConfig(vocab_size=500, hidden_size=32, num_layers=2, num_heads=2,
+                         intermediate_size=64, max_positions=64, head_layers=1,
+                         head_intermediate=128), 21),
+    "sj_base": (SjConfig(vocab_size=32768, hidden_size=768, num_layers=12, num_heads=12,
+                         intermediate_size=3072, max_positions=512, head_layers=1), 22),
+}
+
+
+def make_sj_weights(cfg: SjConfig, seed: int, std: float = 0.02) -> dict[str, np.ndarray]:
+    """Seeded fp32 SjModel weights in its schema (sj.* names, src/sj_model.cpp:117-202);
+    LN weights 1, every bias drawn like the weights so the bias paths are exercised."""
+    D, F, V = cfg.hidden_size, cfg.intermediate_size, cfg.vocab_size
+    rng = np.random.default_rng(seed)
+    s = np.float32(std)
+
+    def n(*shape):
+        return rng.standard_normal(shape, dtype=np.float32) * s
+
+    ones = lambda k: np.ones(k, dtype=np.float32)  # noqa: E731
+    t: dict[str, np.ndarray] = {}
+    t["sj.embeddings.word.weight"] = n(V, D)
+    t["sj.embeddings.position.weight"] = n(cfg.max_positions, D)
+    t["sj.embeddings.norm.weight"] = ones(D)
+    t["sj.embeddings.norm.bias"] = n(D)
+
+    def layer(p, ffn, norms):
+        t[p + norms[0] + ".weight"] = ones(D)
+        t[p + norms[0] + ".bias"] = n(D)
+        for x in "qkvo":
+            t[p + f"attn.{x}.weight"] = n(D, D)
+            t[p + f"attn.{x}.bias"] = n(D)
+        t[p + norms[1] + ".weight"] = ones(D)
+        t[p + norms[1] + ".bias"] = n(D)
+        t[p + "ffn.w1.weight"] = n(ffn, D)
+        t[p + "ffn.w1.bias"] = n(ffn)
+        t[p + "ffn.w2.weight"] = n(D, ffn)
+        t[p + "ffn.w2.bias"] = n(D)
+
+    for i in range(cfg.num_layers):
+        layer(f"sj.encoder.layers.{i}.", F, ("attn_norm", "ffn_norm"))
+    t["sj.encoder.final_norm.weight"] = ones(D)
+    t["sj.encoder.final_norm.bias"] = n(D)
+    t["sj.type_emb.weight"] = n(cfg.n_types, D)
+    for i in range(cfg.head_layers):
+        layer(f"sj.head.layers.{i}.", cfg.head_intermediate, ("norm1", "norm2"))
+    t["sj.scorer.norm.weight"] = ones(D)
+    t["sj.scorer.norm.bias"] = n(D)
+    t["sj.scorer.w1.weight"] = n(D, D)
+    t["sj.scorer.w1.bias"] = n(D)
+    t["sj.scorer.w2.weight"] = n(1, D)
+    t["sj.scorer.w2.bias"] = n(1)
     return t
 
 

@@ -13,6 +13,10 @@ Writes, next to this script:
   checkpoints (``snapjudge_b200.synth``): the ``tiny`` shape (D=16, Dh=8,
   sliding layer) and config ``c1`` (D=64, Dh=16), on packed-equivalent single
   sequences and on a right-padded ragged batch (padded rows included).
+* ``sjmodel_ref.npz`` — outputs of the reference's own ``SjModel::encode`` and
+  ``SjModel::forward`` (``src/sj_model.cpp``, compiled into the same library)
+  on the seeded ``sj_tiny`` checkpoint: single sequences and a ragged padded
+  batch.
 
 Usage:  python tests/golden/make_golden.py [--reference /path/to/snapjudge]
 """
@@ -32,7 +36,7 @@ sys.path.insert(0, ROOT)
 
 from oracle import oracle  # noqa: E402
 from snapjudge_b200 import synth  # noqa: E402
-from snapjudge_b200.checkpoint import save_checkpoint  # noqa: E402
+from snapjudge_b200.checkpoint import save_checkpoint, save_sj_checkpoint  # noqa: E402
 
 
 def convert_tensor_ops(ref_root: str) -> None:
@@ -88,6 +92,37 @@ def encoder_goldens() -> None:
     print("wrote encoder_ref.npz:", len(out), "arrays")
 
 
+def sjmodel_goldens() -> None:
+    cfg, seed = synth.SJ_SPECS["sj_tiny"]
+    tensors = synth.make_sj_weights(cfg, seed)
+    out = {}
+    with tempfile.TemporaryDirectory() as d:
+        save_sj_checkpoint(d, cfg, tensors)
+        ref = oracle.RefSjModel(d, cfg.hidden_size)
+        rng = np.random.default_rng(321)
+        for ci, lens in enumerate([[7], [40], [40, 23, 1, 64]]):
+            lengths = np.asarray(lens, np.int64)
+            L = int(lengths.max())
+            ids = rng.integers(0, cfg.vocab_size, size=int(lengths.sum())).astype(np.int64)
+            pid, mask = synth.pad_batch(ids, lengths)
+            h = ref.encode(pid, mask)
+            pos, mm = markers(rng, lengths, 4)
+            qt = rng.integers(0, cfg.n_types, size=len(lengths)).astype(np.int64)
+            logits, act = ref.forward(pid, mask, pos, mm, qt)
+            p = f"sj_tiny.{ci}."
+            out[p + "lengths"] = lengths
+            out[p + "ids"] = ids
+            out[p + "hidden"] = h
+            out[p + "marker_pos"] = pos
+            out[p + "marker_mask"] = mm
+            out[p + "qtype"] = qt
+            out[p + "logits"] = logits
+            out[p + "act"] = act
+            assert L <= cfg.max_positions
+    np.savez_compressed(os.path.join(HERE, "sjmodel_ref.npz"), **out)
+    print("wrote sjmodel_ref.npz:", len(out), "arrays")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -95,6 +130,7 @@ def main():
     oracle.build()
     convert_tensor_ops(a.reference)
     encoder_goldens()
+    sjmodel_goldens()
 
 
 if __name__ == "__main__":

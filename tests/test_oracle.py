@@ -108,3 +108,22 @@ def test_ops_match_compiled_reference():
     c, s = oracle.rope_table(10000.0, 16, 64)
     qkv = rng.standard_normal((50, 3 * 2 * 16), dtype=np.float32)
     close(oracle.rope(qkv, c, s, 25, 2, 16), oracle.ref_rope(qkv, c, s, 25, 2, 16), 0)
+
+
+def test_sjmodel_restatement_matches_reference_goldens(golden_dir):
+    """The NumPy SjModel restatement against the reference's own SjModel::encode /
+    forward outputs (tests/golden/sjmodel_ref.npz, ragged padded batches)."""
+    E = np.load(os.path.join(golden_dir, "sjmodel_ref.npz"))
+    cfg, seed = synth.SJ_SPECS["sj_tiny"]
+    orc = oracle.SjOracle(cfg, synth.make_sj_weights(cfg, seed))
+    ci = 0
+    while f"sj_tiny.{ci}.lengths" in E:
+        g = {k.split(".", 2)[2]: E[k] for k in E.files if k.startswith(f"sj_tiny.{ci}.")}
+        pid, mask = synth.pad_batch(g["ids"], g["lengths"])
+        h = orc.encode_padded(pid, mask)
+        assert np.abs(h - g["hidden"]).max() <= 1e-5 * max(1.0, np.abs(g["hidden"]).max())
+        lg, act = orc.forward_padded(pid, mask, g["marker_pos"], g["marker_mask"], g["qtype"])
+        assert np.abs(lg - g["logits"]).max() <= 1e-5
+        assert np.abs(act - g["act"]).max() <= 1e-6
+        ci += 1
+    assert ci == 3
