@@ -163,6 +163,14 @@ int sj_fast_commit(sj_fast* e);
 int sj_fast_encode(sj_fast* e, const int64_t* ids, const int32_t* cu_seqlens,
                    const int32_t* kv_lens, int B, float* hidden);
 
+/* Mean-pooled embeddings, host buffers (synchronous): pooled fp32 [B, D] =
+ * the mean of segment b's final-norm hidden states over its rows (zeros for an
+ * empty segment), summed in row order in fp32.  Replaces the encode + pooling
+ * loop of Agent::embed (src/agent.cpp:315-357); tokenisation and truncation to
+ * max_length stay with the caller.  Only [B, D] crosses back to the host. */
+int sj_fast_embed(sj_fast* e, const int64_t* ids, const int32_t* cu_seqlens, int B,
+                  float* pooled);
+
 /* Encoder + [CLS] decision heads, host buffers (synchronous):
  * probs fp32 [B, sum n_out] (heads in declaration order). */
 int sj_fast_decide(sj_fast* e, const int64_t* ids, const int32_t* cu_seqlens, int B,

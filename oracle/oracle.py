@@ -283,6 +283,22 @@ class Oracle:
         return logits, act
 
 
+def embed_mean(hidden, mask):
+    """Agent::embed's pooling (src/agent.cpp:347-354): per row, the fp32 sum of
+    the hidden states at its valid positions in position order, divided by
+    max(1, n).  hidden [B, L, D], mask [B, L] (right-padded) -> [B, D]."""
+    hidden = np.asarray(hidden, np.float32)
+    lens = np.asarray(mask).astype(np.int64).sum(axis=1)
+    B, _, D = hidden.shape
+    out = np.zeros((B, D), np.float32)
+    for b in range(B):
+        acc = np.zeros(D, np.float32)
+        for i in range(int(lens[b])):
+            acc += hidden[b, i]
+        out[b] = acc / np.float32(max(1, int(lens[b])))
+    return out
+
+
 def task_heads(cls_hidden, tensors, heads):
     """Config decision heads on the [CLS] rows, fp64: list of [B, n_out] probabilities."""
     x = np.asarray(cls_hidden, np.float64)

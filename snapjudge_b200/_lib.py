@@ -26,7 +26,7 @@ SJ_ARCH_SJMODEL = 1
 # every symbol declared in include/snapjudge_b200.h
 EXPORTS = ["sj_b200_version", "sj_last_error", "sj_gemm", "sj_gemm_geglu", "sj_add_ln", "sj_rope",
            "sj_attn", "sj_attn_noalloc", "sj_fast_create", "sj_fast_set_tensor", "sj_fast_set_heads",
-           "sj_fast_commit", "sj_fast_encode", "sj_fast_decide", "sj_fast_forward", "sj_fast_n_act",
+           "sj_fast_commit", "sj_fast_encode", "sj_fast_embed", "sj_fast_decide", "sj_fast_forward", "sj_fast_n_act",
            "sj_fast_encode_device",
            "sj_fast_sync", "sj_fast_launch_count", "sj_fast_set_profiling", "sj_fast_profile",
            "sj_fast_last_error", "sj_fast_destroy"]
@@ -78,6 +78,7 @@ def lib() -> C.CDLL:
         L.sj_fast_commit.argtypes = [_P]
         L.sj_fast_encode.argtypes = [_P, _P, _P, _P, _I, _P]
         L.sj_fast_decide.argtypes = [_P, _P, _P, _I, _P]
+        L.sj_fast_embed.argtypes = [_P, _P, _P, _I, _P]
         L.sj_fast_forward.argtypes = [_P, _P, _P, _P, _I, _P, _P, _I, _P, _P, _P]
         L.sj_fast_n_act.argtypes = [_P]
         L.sj_fast_encode_device.argtypes = [_P, _P, _P, _P, _P, _I, _P, _P, _P]

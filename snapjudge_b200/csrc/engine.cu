@@ -279,7 +279,7 @@ struct sj_fast {
           int B, float* d_hidden, float* d_probs, const DmPass* dm, cudaStream_t st);
   int check_flags(cudaStream_t st);
   int host_call(const int64_t* ids_h, const int32_t* cu_h, const int32_t* kvl_h, int B,
-                float* hidden_h, float* probs_h);
+                float* hidden_h, float* probs_h, float* pooled_h = nullptr);
   int dm_call(const int64_t* ids_h, const int32_t* cu_h, const int32_t* kvl_h, int B,
               const int64_t* pos_h, const uint8_t* mask_h, int K, const int64_t* qtype_h,
               float* logits_h, float* act_h);
@@ -807,7 +807,7 @@ int sj_fast::check_flags(cudaStream_t st) {
 }
 
 int sj_fast::host_call(const int64_t* ids_h, const int32_t* cu_h, const int32_t* kvl_h, int B,
-                       float* hidden_h, float* probs_h) {
+                       float* hidden_h, float* probs_h, float* pooled_h) {
   if (!committed) return fail(SJ_ERR_STATE, "forward before sj_fast_commit");
   if (B <= 0) return B == 0 ? SJ_OK : fail(SJ_ERR_INVALID, "negative batch");
   if (!cu_h || (!ids_h && cu_h[B] > 0)) return fail(SJ_ERR_INVALID, "null input");
@@ -827,9 +827,10 @@ int sj_fast::host_call(const int64_t* ids_h, const int32_t* cu_h, const int32_t*
   const int nout = std::max(1, spec.n_total);
   int b0 = 0;
   while (b0 < B) {
-    // largest run of whole sequences that fits the workspace
+    // largest run of whole sequences that fits the workspace (at most
+    // max_tokens rows and max_tokens sequences: empty ones take no rows)
     int b1 = b0;
-    while (b1 < B && cu_h[b1 + 1] - cu_h[b0] <= max_tokens) ++b1;
+    while (b1 < B && b1 - b0 < max_tokens && cu_h[b1 + 1] - cu_h[b0] <= max_tokens) ++b1;
     if (b1 == b0)
       return fail(SJ_ERR_INVALID, "sequence longer than max_tokens");
     const int nb = b1 - b0, base = cu_h[b0], T = cu_h[b1] - base;
@@ -846,9 +847,16 @@ int sj_fast::host_call(const int64_t* ids_h, const int32_t* cu_h, const int32_t*
       return cuda_fail(rc, "cudaMemcpyAsync (inputs)");
     // h_cu is read by run() for the schedule; it is pinned host memory that
     // stays untouched until the next pass's event wait above.
-    int s = run(ids, cu, h_cu, kvl_h ? kvl : nullptr, nb, hidden_h ? hid : nullptr,
+    int s = run(ids, cu, h_cu, kvl_h ? kvl : nullptr, nb, (hidden_h || pooled_h) ? hid : nullptr,
                 probs_h ? probs : nullptr, nullptr, stream);
     if (s) return s;
+    if (pooled_h) {  // per-segment means into Hc ([nb, D] <= [max_tokens, D])
+      cudaStream_t st = stream;
+      SJ_LAUNCH(SJ_K_FINAL, sjb::mean_pool(hid, cu, nb, D, Hc, stream));
+      if ((rc = cudaMemcpyAsync(pooled_h + (int64_t)b0 * D, Hc, (size_t)nb * D * sizeof(float),
+                                cudaMemcpyDeviceToHost, stream)))
+        return cuda_fail(rc, "cudaMemcpyAsync (pooled)");
+    }
     if (hidden_h && (rc = cudaMemcpyAsync(hidden_h + (int64_t)base * D, hid,
                                           (size_t)T * D * sizeof(float), cudaMemcpyDeviceToHost,
                                           stream)))
@@ -1038,6 +1046,13 @@ int sj_fast_encode(sj_fast* e, const int64_t* ids, const int32_t* cu_seqlens,
   if (!e) return SJ_ERR_INVALID;
   if (!hidden && B > 0) return e->fail(SJ_ERR_INVALID, "null hidden output");
   return e->host_call(ids, cu_seqlens, kv_lens, B, hidden, nullptr);
+}
+
+int sj_fast_embed(sj_fast* e, const int64_t* ids, const int32_t* cu_seqlens, int B,
+                  float* pooled) {
+  if (!e) return SJ_ERR_INVALID;
+  if (!pooled && B > 0) return e->fail(SJ_ERR_INVALID, "null pooled output");
+  return e->host_call(ids, cu_seqlens, nullptr, B, nullptr, nullptr, pooled);
 }
 
 int sj_fast_decide(sj_fast* e, const int64_t* ids, const int32_t* cu_seqlens, int B,

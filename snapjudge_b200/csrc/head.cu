@@ -37,6 +37,21 @@ __global__ void gather_markers_kernel(const float* __restrict__ h, const int32_t
   for (int j = threadIdx.x & 31; j < D; j += 32) dst[j] = src[j];
 }
 
+// pooled[b, d] = sum over rows i < n_b of h[cu[b] + i, d], then / max(1, n_b):
+// Agent::embed's mean over non-padding positions (agent.cpp:347-354), summed
+// in row order in fp32 as there.  Block (b, column slab): one thread per column.
+__global__ void mean_pool_kernel(const float* __restrict__ h, const int32_t* __restrict__ cu,
+                                 int D, float* __restrict__ pooled) {
+  const int b = blockIdx.x;
+  const int d = blockIdx.y * blockDim.x + threadIdx.x;
+  if (d >= D) return;
+  const int s0 = cu[b], n = cu[b + 1] - s0;
+  const float* src = h + (int64_t)s0 * D + d;
+  float acc = 0.f;
+  for (int i = 0; i < n; ++i) acc += src[(int64_t)i * D];
+  pooled[(int64_t)b * D + d] = acc / (float)max(1, n);
+}
+
 // One block per segment: the masked scorer logits, their softmax statistics
 // (fp64 sums of fp32 exponentials, model.cpp:490-508), the act features
 // [CLS row, top1, top1 - top2, normalised entropy, k / 255] and the act MLP
@@ -141,6 +156,14 @@ cudaError_t gather_markers(const float* h, const int32_t* cu, const int64_t* pos
   const int BK = B * K;
   if (BK <= 0) return cudaSuccess;
   gather_markers_kernel<<<(BK + 7) / 8, 256, 0, st>>>(h, cu, pos, K, D, BK, m);
+  return cudaGetLastError();
+}
+
+cudaError_t mean_pool(const float* h, const int32_t* cu, int B, int D, float* pooled,
+                      cudaStream_t st) {
+  if (B <= 0 || D <= 0) return cudaSuccess;
+  const dim3 grid(B, (D + 127) / 128);
+  mean_pool_kernel<<<grid, 128, 0, st>>>(h, cu, D, pooled);
   return cudaGetLastError();
 }
 

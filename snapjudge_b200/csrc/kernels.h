@@ -95,6 +95,9 @@ cudaError_t act_head(const float* h, const int32_t* cu, int B, const float* scor
                      const uint8_t* mask, int K, const float* w1, const float* b1,
                      const float* w2, const float* b2, int n_act, int D, float* logits,
                      float* act, bool top1_only, cudaStream_t st);
+// pooled[b] = mean of h over segment b's rows (zeros for an empty segment)
+cudaError_t mean_pool(const float* h, const int32_t* cu, int B, int D, float* pooled,
+                      cudaStream_t st);
 
 // ---- tcgen05 GEMM (gemm_tc.cu) ------------------------------------------------
 // True when the tensor-core GEMM takes this shape (K % 64 == 0, N tiles of 256

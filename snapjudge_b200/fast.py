@@ -122,6 +122,28 @@ class FastSnapjudge:
         out = self.encode_packed(ids.reshape(-1), np.full(B, L, np.int64), kv_lens=lens)
         return out.reshape(B, L, self.D)
 
+    def embed_packed(self, ids, lengths) -> np.ndarray:
+        """Mean-pooled final hidden states per segment, [B, D] (zeros for an
+        empty segment); pooled on the device."""
+        ids = np.ascontiguousarray(ids, dtype=np.int64)
+        lengths = np.asarray(lengths, dtype=np.int64)
+        cu = np.zeros(len(lengths) + 1, np.int32)
+        np.cumsum(lengths, out=cu[1:])
+        out = np.empty((len(lengths), self.D), np.float32)
+        check(_lib.lib().sj_fast_embed(self._h, _ptr(ids), _ptr(cu), len(lengths), _ptr(out)),
+              self._h)
+        return out
+
+    def embed(self, input_ids, attention_mask) -> np.ndarray:
+        """Agent::embed's pooling (src/agent.cpp:315-357) on a tokenised,
+        right-padded batch: the mean of each row's final hidden states over its
+        valid positions, [B, D].  Valid rows do not see the padding, so the
+        batch is packed to them first."""
+        ids = np.ascontiguousarray(input_ids, dtype=np.int64)
+        lens = np.asarray(attention_mask, dtype=np.int64).sum(axis=1)
+        rows = np.arange(ids.shape[1])[None, :] < lens[:, None]
+        return self.embed_packed(ids[rows], lens)
+
     @property
     def n_act(self) -> int:
         """Outputs of the act head (0 without a decision-model head)."""

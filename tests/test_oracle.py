@@ -127,3 +127,16 @@ def test_sjmodel_restatement_matches_reference_goldens(golden_dir):
         assert np.abs(act - g["act"]).max() <= 1e-6
         ci += 1
     assert ci == 3
+
+
+def test_embed_mean_known_answer():
+    """Agent::embed's pooling (agent.cpp:347-354): valid positions only, in fp32,
+    divided by max(1, n) — an empty row gives zeros."""
+    h = np.arange(2 * 3 * 2, dtype=np.float32).reshape(2, 3, 2)
+    mask = np.array([[1, 1, 0], [0, 0, 0]])
+    got = oracle.embed_mean(h, mask)
+    assert np.array_equal(got, np.array([[1.0, 2.0], [0.0, 0.0]], np.float32))
+    # rows past the mask do not enter the sum, whatever they hold
+    h2 = h.copy()
+    h2[0, 2] = np.nan
+    assert np.array_equal(oracle.embed_mean(h2, mask), got)
