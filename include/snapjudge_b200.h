@@ -39,6 +39,10 @@ extern "C" {
 
 #define SJ_PREC_BF16 0 /* bf16 activations/weights, fp32 accumulation, fp32 residual stream */
 #define SJ_PREC_FP32 1 /* fp32 everywhere (parity mode: 1e-4 relative to the CPU forward) */
+#define SJ_PREC_FP8 2  /* SJ_PREC_BF16 with the QKV and Wi (GEGLU) projections on e4m3
+                          operands: per-token activation scales, per-channel weight scales,
+                          fp32 accumulation (DecisionModel encoder only; reported separately,
+                          not held to the bf16 tolerances) */
 
 #define SJ_HEAD_SOFTMAX 0
 #define SJ_HEAD_SIGMOID 1
@@ -101,6 +105,23 @@ int sj_attn_noalloc(const sj_bf16* qkv, const int32_t* cu_seqlens, const int32_t
                     const int32_t* kv_lens, sj_bf16* O, int B, int H, int Dh, int window,
                     void* stream);
 
+/* The FP8 variant's two kernels (no counterpart in the reference, which has
+ * no FP8 path; SJ_PREC_FP8 runs them inside the engine).
+ *
+ * sj_quant_e4m3: per row of x (fp32 [rows, cols], cols % 4 == 0):
+ * scale[r] = amax_r / 448 (1 for an all-zero row) and q[r, :] = e4m3 codes of
+ * x * (448 / amax_r), rounded to nearest even, saturating. */
+int sj_quant_e4m3(const float* x, int64_t rows, int cols, uint8_t* q, float* scale, void* stream);
+
+/* C = act(sa[m] sw[n] sum_k A[m,k] W[n,k] + bias) on tcgen05 kind::f8f6f4:
+ * A [M, K] and W [N, K] e4m3 codes with their row scales sa [M], sw [N]
+ * (16-byte aligned), fp32 accumulation, bf16 C [M, N]; K % 128 == 0,
+ * N % 64 == 0.  geglu != 0: W = [Wg; Wu] [2N, K], sw [2N] and
+ * C = gelu(g) * u (act and bias ignored), as sj_gemm_geglu. */
+int sj_gemm_e4m3(const uint8_t* A, const uint8_t* W, const float* sa, const float* sw,
+                 const float* bias, sj_bf16* C, int M, int N, int K, int has_bias, int act,
+                 int geglu, void* stream);
+
 /* ------------------------------------------------------------------------- */
 /* 2. Encoder engine (replaces FastSnapjudge, include/snapjudge/fast.hpp).    */
 /* ------------------------------------------------------------------------- */
@@ -120,7 +141,7 @@ typedef struct sj_fast_config {
   double rope_theta_full;
   double rope_theta_sliding;
   /* engine options */
-  int precision;                /* SJ_PREC_BF16 or SJ_PREC_FP32 */
+  int precision;                /* SJ_PREC_BF16, SJ_PREC_FP32 or SJ_PREC_FP8 */
   int device;                   /* CUDA device ordinal */
   int max_tokens;               /* tokens per device pass (workspace size); 0 = default */
   int arch;                     /* SJ_ARCH_MODERNBERT (0) or SJ_ARCH_SJMODEL (1) */

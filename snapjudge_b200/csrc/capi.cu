@@ -132,4 +132,33 @@ int sj_attn(const sj_bf16* qkv, const int32_t* cu_seqlens, const int32_t* cu_seq
                   "attn_simt");
 }
 
+int sj_quant_e4m3(const float* x, int64_t rows, int cols, uint8_t* q, float* scale,
+                  void* stream) {
+  if (rows < 0 || cols <= 0 || cols % 4 != 0)
+    return fail(SJ_ERR_INVALID, "rows must be >= 0 and cols a positive multiple of 4");
+  if (rows && (!x || !q || !scale)) return fail(SJ_ERR_INVALID, "null quantisation operand");
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(q) & 3))
+    return fail(SJ_ERR_INVALID, "x must be 16-byte and q 4-byte aligned");
+  return launched(sjb::quant_rows_e4m3<float>(x, rows, cols, q, scale,
+                                              static_cast<cudaStream_t>(stream)),
+                  "quant_rows_e4m3");
+}
+
+int sj_gemm_e4m3(const uint8_t* A, const uint8_t* W, const float* sa, const float* sw,
+                 const float* bias, sj_bf16* C, int M, int N, int K, int has_bias, int act,
+                 int geglu, void* stream) {
+  if (M < 0 || N < 0 || K < 0) return fail(SJ_ERR_INVALID, "negative GEMM size");
+  if (act < 0 || act > 2) return fail(SJ_ERR_INVALID, "act must be 0, 1 or 2");
+  if (M == 0 || N == 0) return SJ_OK;
+  const int epi = geglu ? sjb::TC_GEGLU : sjb::TC_STORE;
+  if (!sjb::gemm_tc_f8_supported(M, N, K, epi))
+    return fail(SJ_ERR_UNSUPPORTED, "the e4m3 GEMM needs K % 128 == 0 and N % 64 == 0");
+  if (!A || !W || !sa || !sw || !C || (has_bias && !geglu && !bias))
+    return fail(SJ_ERR_INVALID, "null GEMM operand");
+  return launched(sjb::gemm_tc_f8(A, W, sa, sw, (has_bias && !geglu) ? bias : nullptr,
+                                  reinterpret_cast<bf16*>(C), M, N, K, epi, geglu ? 0 : act,
+                                  sjb::TcRope{}, nullptr, static_cast<cudaStream_t>(stream)),
+                  "gemm_tc_f8");
+}
+
 }  // extern "C"

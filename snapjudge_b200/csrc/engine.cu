@@ -64,6 +64,9 @@ struct LayerDev {
   // wqkv with bias bqkv [3D], Wo bias, wi = ffn.w1 [F, D] + b1, wo2 = ffn.w2 + b2
   float *attn_norm_b = nullptr, *mlp_norm_b = nullptr;
   float *bqkv = nullptr, *bo = nullptr, *b1 = nullptr, *b2 = nullptr;
+  // SJ_PREC_FP8: e4m3 copies of wqkv and wi with a scale per row
+  uint8_t *wqkv8 = nullptr, *wi8 = nullptr;
+  float *sqkv = nullptr, *si = nullptr;
 };
 
 // One pre-norm TransformerEncoderLayer of the decision head (model.cpp:134-152):
@@ -93,6 +96,7 @@ struct sj_fast {
   int D = 0, H = 0, Dh = 0, F = 0, V = 0, NL = 0;
   int max_tokens = 0;
   bool bf16_mode = true;
+  bool fp8 = false;  // SJ_PREC_FP8: QKV and Wi projections on e4m3 operands
   bool committed = false;
   cudaStream_t stream = nullptr;
   std::string err;
@@ -146,6 +150,8 @@ struct sj_fast {
   float* probs = nullptr; // [max_tokens, n_total]
   float* hid = nullptr;   // [max_tokens, D] fp32 hidden (host-API staging)
   float* z = nullptr;     // LoRA [max_tokens, r]
+  uint8_t* Y8 = nullptr;  // SJ_PREC_FP8: LN output as e4m3 [max_tokens, D]
+  float* sa8 = nullptr;   //   and its row scales [max_tokens]
   int* dflags = nullptr;  // device error flags: [0] bad id, [1] gemm wait, [2] attn wait
   // pinned host staging
   int2* h_tiles = nullptr;
@@ -262,6 +268,23 @@ struct sj_fast {
     return rc == cudaSuccess ? SJ_OK : cuda_fail(rc, "cudaMemcpy");
   }
 
+  // e4m3 codes and row scales of a [rows, cols] weight (quantised on the device
+  // from its fp32 values, as quant_rows_e4m3)
+  int upload_e4m3(const HostTensor* t, uint8_t** q, float** scale) {
+    const int64_t rows = t->shape[0], cols = t->shape[1];
+    float* tmp = nullptr;
+    cudaError_t rc = cudaMalloc(&tmp, t->data.size() * sizeof(float));
+    if (rc != cudaSuccess) return cuda_fail(rc, "cudaMalloc");
+    if ((rc = cudaMemcpy(tmp, t->data.data(), t->data.size() * sizeof(float),
+                         cudaMemcpyHostToDevice)) == cudaSuccess &&
+        (rc = dalloc(q, t->data.size())) == cudaSuccess && (rc = dalloc(scale, rows)) == cudaSuccess &&
+        (rc = sjb::quant_rows_e4m3<float>(tmp, rows, (int)cols, *q, *scale, nullptr)) ==
+            cudaSuccess)
+      rc = cudaDeviceSynchronize();
+    cudaFree(tmp);
+    return rc == cudaSuccess ? SJ_OK : cuda_fail(rc, "e4m3 weight upload");
+  }
+
   int commit();
   int load_sjmodel();
   template <typename T>
@@ -324,12 +347,14 @@ int sj_fast::commit() {
     }
     if ((s = require(p + "attn.Wqkv.weight", {3 * (int64_t)D, D}, &t))) return s;
     if ((s = upload_w(t, &ly.wqkv))) return s;
+    if (fp8 && (s = upload_e4m3(t, &ly.wqkv8, &ly.sqkv))) return s;
     if ((s = require(p + "attn.Wo.weight", {D, D}, &t))) return s;
     if ((s = upload_w(t, &ly.wo))) return s;
     if ((s = require(p + "mlp_norm.weight", {D}, &t))) return s;
     if ((s = upload_f32(t, &ly.mlp_norm))) return s;
     if ((s = require(p + "mlp.Wi.weight", {2 * (int64_t)F, D}, &t))) return s;
     if ((s = upload_w(t, &ly.wi))) return s;
+    if (fp8 && (s = upload_e4m3(t, &ly.wi8, &ly.si))) return s;
     if ((s = require(p + "mlp.Wo.weight", {D, F}, &t))) return s;
     if ((s = upload_w(t, &ly.wo2))) return s;
   }
@@ -446,7 +471,7 @@ int sj_fast::commit() {
       (rc = dalloc(&cu, T + 1)) || (rc = dalloc(&kvl, T)) || (rc = dalloc(&tiles, max_tiles)) ||
       (rc = dalloc(&Hc, T * D)) || (rc = dalloc(&probs, T * (size_t)std::max(1, spec.n_total))) ||
       (rc = dalloc(&hid, T * D)) || (rc = dalloc(&z, T * (size_t)std::max(1, lora_r))) ||
-      (rc = dalloc(&dflags, 8)))
+      (rc = dalloc(&dflags, 8)) || (fp8 && ((rc = dalloc(&Y8, T * D)) || (rc = dalloc(&sa8, T)))))
     return cuda_fail(rc, "cudaMalloc (workspace)");
   if ((rc = cudaMemset(dflags, 0, 8 * sizeof(int)))) return cuda_fail(rc, "cudaMemset");
   if ((rc = cudaMallocHost(&h_tiles, max_tiles * sizeof(int2))) ||
@@ -630,11 +655,19 @@ int sj_fast::forward(const int64_t* d_ids, const int32_t* d_cu, const int32_t* h
     return gemm_any<T>(cls, A, W, bias, act, C, resid, ntok, N, K, epi, ct, stb, st);
   };
 
+  // SJ_PREC_FP8: the attn_norm and mlp_norm outputs are e4m3 rows with their
+  // scales (Y8, sa8), the QKV and Wi GEMMs run on the e4m3 weights
+  const bool f8 = kBf16 && fp8 && !sjm;
   int s;
   for (int li = 0; li < NL; ++li) {
     const LayerDev& ly = layers[li];
     const T* Yin = Yt;
-    if (ly.attn_norm) {
+    if (f8) {
+      if (ly.attn_norm)
+        SJ_LAUNCH(SJ_K_LN, sjb::ln_e4m3(X, ly.attn_norm, ly.attn_norm_b, Y8, sa8, ntok, D, eps, st));
+      else
+        SJ_LAUNCH(SJ_K_LN, sjb::quant_rows_e4m3<float>(X, ntok, D, Y8, sa8, st));
+    } else if (ly.attn_norm) {
       SJ_LAUNCH(SJ_K_LN, (sjb::add_ln<T, T>(X, nullptr, ly.attn_norm, ly.attn_norm_b, Yt, ntok, D, eps,
                                           nullptr, st)));
     } else if (li > 0) {
@@ -647,6 +680,12 @@ int sj_fast::forward(const int64_t* d_ids, const int32_t* d_cu, const int32_t* h
       if ((s = gemm(SJ_K_QKV, Yin, ly.wqkv, Qt, nullptr, 3 * D, D, sjb::TC_STORE, nullptr, nullptr,
                     ly.bqkv)))
         return s;
+    } else if (f8) {
+      if constexpr (kBf16) {
+        sjb::TcRope rp{ct, stb, pos, H};
+        SJ_LAUNCH(SJ_K_QKV, sjb::gemm_tc_f8(Y8, ly.wqkv8, sa8, ly.sqkv, nullptr, Qt, ntok, 3 * D, D,
+                                            sjb::TC_ROPE, 0, rp, dflags + 1, st));
+      }
     } else if ((s = gemm(SJ_K_QKV, Yin, ly.wqkv, Qt, nullptr, 3 * D, D, sjb::TC_ROPE, ct, stb))) {
       return s;
     }
@@ -659,12 +698,19 @@ int sj_fast::forward(const int64_t* d_ids, const int32_t* d_cu, const int32_t* h
     }
     if ((s = gemm(SJ_K_WO, Ot, ly.wo, nullptr, X, D, D, sjb::TC_RESID, nullptr, nullptr, ly.bo)))
       return s;
-    SJ_LAUNCH(SJ_K_LN, (sjb::add_ln<T, T>(X, nullptr, ly.mlp_norm, ly.mlp_norm_b, Yt, ntok, D, eps,
-                                        nullptr, st)));
+    if (f8)
+      SJ_LAUNCH(SJ_K_LN, sjb::ln_e4m3(X, ly.mlp_norm, ly.mlp_norm_b, Y8, sa8, ntok, D, eps, st));
+    else
+      SJ_LAUNCH(SJ_K_LN, (sjb::add_ln<T, T>(X, nullptr, ly.mlp_norm, ly.mlp_norm_b, Yt, ntok, D, eps,
+                                            nullptr, st)));
     if (sjm) {  // SjModel: G = gelu(Y W1^T + b1), X += G W2^T + b2
       if ((s = gemm(SJ_K_GEGLU, Yt, ly.wi, Gt, nullptr, F, D, sjb::TC_STORE, nullptr, nullptr, ly.b1,
                     sjb::ACT_GELU)))
         return s;
+    } else if (f8) {
+      if constexpr (kBf16)
+        SJ_LAUNCH(SJ_K_GEGLU, sjb::gemm_tc_f8(Y8, ly.wi8, sa8, ly.si, nullptr, Gt, ntok, F, D,
+                                              sjb::TC_GEGLU, 0, sjb::TcRope{}, dflags + 1, st));
     } else if ((s = gemm(SJ_K_GEGLU, Yt, ly.wi, Gt, nullptr, F, D, sjb::TC_GEGLU, nullptr, nullptr))) {
       return s;
     }
@@ -972,7 +1018,14 @@ int sj_fast_create(const sj_fast_config* cfg, sj_fast** out) {
       c.hidden_size % c.num_attention_heads != 0 ||
       (c.hidden_size / c.num_attention_heads) % 2 != 0)
     return SJ_ERR_INVALID;
-  if (c.precision != SJ_PREC_BF16 && c.precision != SJ_PREC_FP32) return SJ_ERR_UNSUPPORTED;
+  if (c.precision != SJ_PREC_BF16 && c.precision != SJ_PREC_FP32 && c.precision != SJ_PREC_FP8)
+    return SJ_ERR_UNSUPPORTED;
+  // the FP8 variant: the DecisionModel encoder, e4m3 GEMMs need K = D % 128 == 0,
+  // the quantising LN D <= 1024, the attention head_dim 64 and N % 64 == 0
+  if (c.precision == SJ_PREC_FP8 &&
+      (c.arch != SJ_ARCH_MODERNBERT || c.hidden_size % 128 != 0 || c.hidden_size > 1024 ||
+       c.hidden_size / c.num_attention_heads != 64 || c.intermediate_size % 64 != 0))
+    return SJ_ERR_UNSUPPORTED;
   if (c.arch != SJ_ARCH_MODERNBERT && c.arch != SJ_ARCH_SJMODEL) return SJ_ERR_UNSUPPORTED;
   // SjModel's learned positions are added in the warp-per-row embedding kernel
   if (c.arch == SJ_ARCH_SJMODEL && (c.hidden_size > 1024 || c.hidden_size % 4 != 0))
@@ -983,7 +1036,8 @@ int sj_fast_create(const sj_fast_config* cfg, sj_fast** out) {
   e->F = c.intermediate_size;
   e->V = c.vocab_size;
   e->NL = c.num_hidden_layers;
-  e->bf16_mode = c.precision == SJ_PREC_BF16;
+  e->bf16_mode = c.precision == SJ_PREC_BF16 || c.precision == SJ_PREC_FP8;
+  e->fp8 = c.precision == SJ_PREC_FP8;
   e->max_tokens = c.max_tokens > 0 ? c.max_tokens : (e->bf16_mode ? 262144 : 65536);
   e->max_tokens = std::max(e->max_tokens, 128);
   e->arch = c.arch;

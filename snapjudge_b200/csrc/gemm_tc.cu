@@ -18,6 +18,9 @@
 //                                                             + 128 up rows of [Wg; Wu];
 //                                                             erf per A&S 7.1.26, packed fp32)
 //                 ROPE   QKV = bf16(rotate-half(acc)) on q/k heads of 64, v as is
+// F8 instances take e4m3 A and W (tcgen05 kind::f8f6f4, 128-element k-blocks:
+// the same 128-byte swizzled rows) with a scale per A row and per W row; the
+// epilogue multiplies the fp32 accumulator by both before its own work.
 // The epilogue of tile i overlaps the MMAs of tile i+1 (double-buffered TMEM).
 // Every mbarrier wait is bounded; a wait that runs out records an error code
 // and the CTA winds down (no trap).
@@ -50,6 +53,8 @@ struct EpiArgs {
   const float* sin_t;
   const int32_t* pos;    // [M]
   int rope_cols;         // columns [0, rope_cols) are rotated q/k heads
+  const float* sa;       // F8: [M] scale of each A row
+  const float* sw;       // F8: [w_rows] scale of each W row
   int* err;
 };
 
@@ -158,7 +163,21 @@ __device__ __forceinline__ void store_bf16x32(bf16* dst, const float* v) {
   }
 }
 
-template <int BN, int EPI, bool PAIR>
+// r[j] *= sa * sw[j] for 32 accumulator columns (sw 16-byte aligned): the
+// e4m3 operands' row and channel scales
+__device__ __forceinline__ void unscale32(uint32_t (&r)[32], float sa, const float* sw) {
+  const float4* s4 = reinterpret_cast<const float4*>(sw);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const float4 w = __ldg(s4 + k);
+    r[4 * k] = __float_as_uint(__uint_as_float(r[4 * k]) * (sa * w.x));
+    r[4 * k + 1] = __float_as_uint(__uint_as_float(r[4 * k + 1]) * (sa * w.y));
+    r[4 * k + 2] = __float_as_uint(__uint_as_float(r[4 * k + 2]) * (sa * w.z));
+    r[4 * k + 3] = __float_as_uint(__uint_as_float(r[4 * k + 3]) * (sa * w.w));
+  }
+}
+
+template <int BN, int EPI, bool PAIR, bool F8>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
                    const __grid_constant__ CUtensorMap mapC, int M, int n_tiles, int K, int up_row0,
@@ -175,7 +194,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   constexpr uint32_t TMEM_COLS = 2 * BN;
   constexpr int TILE_M = PAIR ? 2 * BM : BM;
-  constexpr uint32_t IDESC = idesc_bf16(TILE_M, BN, false, false);
+  constexpr uint32_t IDESC = F8 ? idesc_e4m3(TILE_M, BN) : idesc_bf16(TILE_M, BN, false, false);
+  constexpr int BKE = F8 ? 2 * BK : BK;  // elements per k-block (128 bytes per row either way)
 
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t full_bar[STAGES], empty_bar[STAGES], tfull_bar[2], tempty_bar[2], drain_bar;
@@ -190,7 +210,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
   const int m_tiles = (M + TILE_M - 1) / TILE_M;
   const int num_tiles = m_tiles * n_tiles;
-  const int k_blocks = K / BK;
+  const int k_blocks = K / BKE;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -241,19 +261,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           // both CTAs' bytes are counted on rank 0's barrier
           const uint32_t bar0 = mapa_shared(smem_u32(&full_bar[stage]), 0);
           if (rank == 0) mbar_expect_tx(&full_bar[stage], 2 * STAGE_BYTES);
-          tma_load_2d_pair(sa, &mapA, bar0, kb * BK, m0);
+          tma_load_2d_pair(sa, &mapA, bar0, kb * BKE, m0);
           const int brow = EPI == TC_GEGLU ? (rank == 0 ? nb * BROWS : up_row0 + nb * BROWS)
                                            : nb * BN + (int)rank * BROWS;
-          tma_load_2d_pair(sb, &mapB, bar0, kb * BK, brow);
+          tma_load_2d_pair(sb, &mapB, bar0, kb * BKE, brow);
         } else {
           mbar_expect_tx(&full_bar[stage], STAGE_BYTES);
-          tma_load_2d(sa, &mapA, &full_bar[stage], kb * BK, m0);
+          tma_load_2d(sa, &mapA, &full_bar[stage], kb * BKE, m0);
           if (EPI == TC_GEGLU) {
-            tma_load_2d(sb, &mapB, &full_bar[stage], kb * BK, nb * (BN / 2));
-            tma_load_2d(sb + B_BYTES / 2, &mapB, &full_bar[stage], kb * BK,
+            tma_load_2d(sb, &mapB, &full_bar[stage], kb * BKE, nb * (BN / 2));
+            tma_load_2d(sb + B_BYTES / 2, &mapB, &full_bar[stage], kb * BKE,
                         up_row0 + nb * (BN / 2));
           } else {
-            tma_load_2d(sb, &mapB, &full_bar[stage], kb * BK, nb * BN);
+            tma_load_2d(sb, &mapB, &full_bar[stage], kb * BKE, nb * BN);
           }
         }
         ++issued;
@@ -295,12 +315,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t b_addr = a_addr + A_BYTES;
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk) {
-          if (PAIR)
-            mma_bf16_pair(d, desc_kmajor_sw128(a_addr + kk * 32),
-                          desc_kmajor_sw128(b_addr + kk * 32), IDESC, (kb | kk) != 0);
-          else
-            mma_bf16(d, desc_kmajor_sw128(a_addr + kk * 32), desc_kmajor_sw128(b_addr + kk * 32),
-                     IDESC, (kb | kk) != 0);
+          // 32 bytes of K per instruction: 16 bf16 or 32 e4m3
+          const uint64_t ad = desc_kmajor_sw128(a_addr + kk * 32);
+          const uint64_t bd = desc_kmajor_sw128(b_addr + kk * 32);
+          if (F8) {
+            if (PAIR) mma_e4m3_pair(d, ad, bd, IDESC, (kb | kk) != 0);
+            else mma_e4m3(d, ad, bd, IDESC, (kb | kk) != 0);
+          } else {
+            if (PAIR) mma_bf16_pair(d, ad, bd, IDESC, (kb | kk) != 0);
+            else mma_bf16(d, ad, bd, IDESC, (kb | kk) != 0);
+          }
         }
         if (PAIR) mma_commit_pair(&empty_bar[stage], 0x3);
         else mma_commit(&empty_bar[stage]);
@@ -377,6 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_after_sync();
       const int row = m0 + q * 32 + lane;
       const bool live = row < M;
+      const float sa = F8 && live ? ep.sa[row] : 0.f;
       const uint32_t tacc = tmem_base + ((uint32_t)(q * 32) << 16) + b * BN;
       uint32_t r0[32], r1[32];
       if (EPI == TC_GEGLU && STAGED) {
@@ -390,6 +415,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_ld32(tacc + c + 32 * k2, r0);
             tmem_ld32(tacc + HALF + c + 32 * k2, r1);
             tmem_ld_wait();
+            if constexpr (F8) {
+              unscale32(r0, sa, ep.sw + col_base + c + 32 * k2);
+              unscale32(r1, sa, ep.sw + up_row0 + col_base + c + 32 * k2);
+            }
 #pragma unroll
             for (int j = 0; j < 32; j += 2) {
               const float2 o = geglu_pair(__uint_as_float(r0[j]), __uint_as_float(r0[j + 1]),
@@ -408,6 +437,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld32(tacc + c, r0);
           tmem_ld32(tacc + HALF + c, r1);
           tmem_ld_wait();
+          if constexpr (F8) {
+            unscale32(r0, sa, ep.sw + col_base + c);
+            unscale32(r1, sa, ep.sw + up_row0 + col_base + c);
+          }
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; j += 2) {
@@ -444,6 +477,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld32(tacc + c, r0);
           tmem_ld32(tacc + c + 32, r1);
           tmem_ld_wait();
+          if constexpr (F8) {
+            unscale32(r0, sa, ep.sw + col_base + c);
+            unscale32(r1, sa, ep.sw + col_base + c + 32);
+          }
           float v[64];
           const bool rot = col_base + c < ep.rope_cols;
 #pragma unroll
@@ -569,6 +606,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int k2 = 0; k2 < 2; ++k2) {
             tmem_ld32(tacc + c + 32 * k2, r0);
             tmem_ld_wait();
+            if constexpr (F8) unscale32(r0, sa, ep.sw + col_base + c + 32 * k2);
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
               float a = __uint_as_float(r0[j]);
@@ -585,6 +623,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld32(tacc + c, r0);
           tmem_ld_wait();
           if (!live) continue;
+          if constexpr (F8) unscale32(r0, sa, ep.sw + col_base + c);
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
@@ -611,24 +650,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int BN, int EPI, bool PAIR>
-cudaError_t launch(const bf16* A, const bf16* W, int M, int N_out, int K, int w_rows, EpiArgs ep,
+template <int BN, int EPI, bool PAIR, bool F8>
+cudaError_t launch(const void* A, const void* W, int M, int N_out, int K, int w_rows, EpiArgs ep,
                    cudaStream_t st) {
   constexpr int STAGES = stages_for<BN, EPI, PAIR>();
   constexpr int BROWS = PAIR ? BN / 2 : BN;
   constexpr int SMEM = STAGES * (BM * BK * 2 + BROWS * BK * 2) + out_bytes<BN, EPI>() + 1024;
   static bool attr_set = false;
   if (!attr_set) {
-    cudaError_t rc = cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI, PAIR>,
+    cudaError_t rc = cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI, PAIR, F8>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
     if (rc != cudaSuccess) return rc;
     attr_set = true;
   }
   CUtensorMap ma, mb, mc;
   const int b_box = PAIR ? BROWS : (EPI == TC_GEGLU ? BN / 2 : BN);
-  if (!make_map_bf16(&ma, A, K, M, (uint64_t)K * 2, BK, BM) ||
-      !make_map_bf16(&mb, W, K, w_rows, (uint64_t)K * 2, BK, b_box))
+  if (F8) {
+    if (!make_map_u8(&ma, A, K, M, (uint64_t)K, 2 * BK, BM) ||
+        !make_map_u8(&mb, W, K, w_rows, (uint64_t)K, 2 * BK, b_box))
+      return cudaErrorInvalidValue;
+  } else if (!make_map_bf16(&ma, A, K, M, (uint64_t)K * 2, BK, BM) ||
+             !make_map_bf16(&mb, W, K, w_rows, (uint64_t)K * 2, BK, b_box)) {
     return cudaErrorInvalidValue;
+  }
   if (staged<BN, EPI>() && EPI == TC_RESID) {
     if (!make_map_f32(&mc, ep.resid, N_out, M, (uint64_t)N_out * 4, 32, 32))
       return cudaErrorInvalidValue;
@@ -644,8 +688,8 @@ cudaError_t launch(const bf16* A, const bf16* W, int M, int N_out, int K, int w_
   const int up_row0 = EPI == TC_GEGLU ? N_out : 0;
   if (!PAIR) {
     const int grid = std::min(tiles, sm_count());
-    gemm_tc_kernel<BN, EPI, false><<<grid, kThreads, SMEM, st>>>(ma, mb, mc, M, n_tiles, K, up_row0,
-                                                                  ep);
+    gemm_tc_kernel<BN, EPI, false, F8><<<grid, kThreads, SMEM, st>>>(ma, mb, mc, M, n_tiles, K,
+                                                                      up_row0, ep);
     return cudaGetLastError();
   }
   const int pairs = std::min(tiles, sm_count() / 2);
@@ -661,29 +705,29 @@ cudaError_t launch(const bf16* A, const bf16* W, int M, int N_out, int K, int w_
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, EPI, true>, ma, mb, mc, M, n_tiles, K,
+  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, EPI, true, F8>, ma, mb, mc, M, n_tiles, K,
                             up_row0, ep);
 }
 
 // Pair tiles (256 x 256) for large GEMMs; single-CTA tiles otherwise.
 constexpr int kPairMinRows = 2048;
 
-template <int EPI>
-cudaError_t dispatch_bn(const bf16* A, const bf16* W, int M, int N, int K, int w_rows, EpiArgs ep,
+template <int EPI, bool F8 = false>
+cudaError_t dispatch_bn(const void* A, const void* W, int M, int N, int K, int w_rows, EpiArgs ep,
                         cudaStream_t st) {
   if (EPI == TC_GEGLU) {
     if (N % 128 == 0) {
-      if (M >= kPairMinRows) return launch<256, EPI, true>(A, W, M, N, K, w_rows, ep, st);
-      return launch<256, EPI, false>(A, W, M, N, K, w_rows, ep, st);
+      if (M >= kPairMinRows) return launch<256, EPI, true, F8>(A, W, M, N, K, w_rows, ep, st);
+      return launch<256, EPI, false, F8>(A, W, M, N, K, w_rows, ep, st);
     }
-    return launch<128, EPI, false>(A, W, M, N, K, w_rows, ep, st);
+    return launch<128, EPI, false, F8>(A, W, M, N, K, w_rows, ep, st);
   }
   if (N % 256 == 0) {
-    if (M >= kPairMinRows) return launch<256, EPI, true>(A, W, M, N, K, w_rows, ep, st);
-    return launch<256, EPI, false>(A, W, M, N, K, w_rows, ep, st);
+    if (M >= kPairMinRows) return launch<256, EPI, true, F8>(A, W, M, N, K, w_rows, ep, st);
+    return launch<256, EPI, false, F8>(A, W, M, N, K, w_rows, ep, st);
   }
-  if (N % 128 == 0) return launch<128, EPI, false>(A, W, M, N, K, w_rows, ep, st);
-  return launch<64, EPI, false>(A, W, M, N, K, w_rows, ep, st);
+  if (N % 128 == 0) return launch<128, EPI, false, F8>(A, W, M, N, K, w_rows, ep, st);
+  return launch<64, EPI, false, F8>(A, W, M, N, K, w_rows, ep, st);
 }
 
 }  // namespace
@@ -713,6 +757,36 @@ cudaError_t gemm_tc(const bf16* A, const bf16* W, const float* bias, bf16* C, fl
     case TC_RESID: return dispatch_bn<TC_RESID>(A, W, M, N, K, N, ep, st);
     case TC_GEGLU: return dispatch_bn<TC_GEGLU>(A, W, M, N, K, 2 * N, ep, st);
     case TC_ROPE: return dispatch_bn<TC_ROPE>(A, W, M, N, K, N, ep, st);
+  }
+  return cudaErrorInvalidValue;
+}
+
+bool gemm_tc_f8_supported(int M, int N, int K, int epi) {
+  if (M <= 0 || K < 2 * BK || K % (2 * BK) != 0 || N % 64 != 0) return false;
+  return epi == TC_STORE || epi == TC_GEGLU || epi == TC_ROPE;
+}
+
+cudaError_t gemm_tc_f8(const uint8_t* A, const uint8_t* W, const float* sa, const float* sw,
+                       const float* bias, bf16* C, int M, int N, int K, int epi, int act,
+                       TcRope rope, int* err, cudaStream_t st) {
+  if (!gemm_tc_f8_supported(M, N, K, epi) || !sa || !sw) return cudaErrorInvalidValue;
+  if (reinterpret_cast<uintptr_t>(sw) & 15) return cudaErrorInvalidValue;
+  EpiArgs ep{};
+  ep.bias = bias;
+  ep.act = act;
+  ep.C = C;
+  ep.ldc = N;
+  ep.cos_t = rope.cos_t;
+  ep.sin_t = rope.sin_t;
+  ep.pos = rope.pos;
+  ep.rope_cols = 2 * rope.H * 64;
+  ep.sa = sa;
+  ep.sw = sw;
+  ep.err = err;
+  switch (epi) {
+    case TC_STORE: return dispatch_bn<TC_STORE, true>(A, W, M, N, K, N, ep, st);
+    case TC_GEGLU: return dispatch_bn<TC_GEGLU, true>(A, W, M, N, K, 2 * N, ep, st);
+    case TC_ROPE: return dispatch_bn<TC_ROPE, true>(A, W, M, N, K, N, ep, st);
   }
   return cudaErrorInvalidValue;
 }

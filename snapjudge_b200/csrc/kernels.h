@@ -116,6 +116,25 @@ struct TcRope {
 cudaError_t gemm_tc(const bf16* A, const bf16* W, const float* bias, bf16* C, float* resid,
                     int M, int N, int K, int epi, int act, TcRope rope, int* err,
                     cudaStream_t st);
+// The FP8 variant (tcgen05 kind::f8f6f4): A [M, K] and W [N_w, K] are e4m3
+// codes with a scale per A row (sa [M]) and per W row (sw [N_w], 16-byte
+// aligned); acc = sa[m] sw[n] sum_k A[m, k] W[n, k] in fp32, then the epilogue
+// as gemm_tc.  Epilogues TC_STORE, TC_GEGLU, TC_ROPE; K % 128 == 0.
+bool gemm_tc_f8_supported(int M, int N, int K, int epi);
+cudaError_t gemm_tc_f8(const uint8_t* A, const uint8_t* W, const float* sa, const float* sw,
+                       const float* bias, bf16* C, int M, int N, int K, int epi, int act,
+                       TcRope rope, int* err, cudaStream_t st);
+
+// ---- e4m3 quantisation (quant.cu) --------------------------------------------
+// Per row: scale = amax / 448 (1 for an all-zero row), q = e4m3(x * (448 / amax))
+// rounded to nearest even, saturating.  T = float or bf16.
+template <typename T>
+cudaError_t quant_rows_e4m3(const T* x, int64_t rows, int cols, uint8_t* q, float* scale,
+                            cudaStream_t st);
+// Y = LN(X) * w (+ b) quantised as quant_rows_e4m3 (X fp32 [rows, D], D % 128 == 0,
+// D <= 1024): the FP8 variant's attn_norm / mlp_norm.
+cudaError_t ln_e4m3(const float* X, const float* w, const float* b, uint8_t* q, float* scale,
+                    int64_t rows, int D, float eps, cudaStream_t st);
 
 // ---- tcgen05 flash attention (attn_tc.cu) -----------------------------------
 bool attn_tc_supported(int Dh);

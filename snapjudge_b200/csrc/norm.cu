@@ -169,6 +169,104 @@ __global__ void __launch_bounds__(256) add_ln_warp(float* __restrict__ X, const 
   }
 }
 
+// ---- e4m3 (the FP8 variant's GEMM operands) ----
+// Two floats to an e4m3 pair, rounded to nearest even, saturating at +-448;
+// the low byte holds a (cvt puts its first source in the high byte).
+__device__ __forceinline__ uint32_t e4m3x2(float a, float b) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(b), "f"(a));
+  return r;
+}
+// four consecutive values times s -> four e4m3 codes in memory order
+__device__ __forceinline__ uint32_t e4m3x4(float4 v, float s) {
+  const float a = v.x * s, b = v.y * s, c = v.z * s, d = v.w * s;
+  return e4m3x2(a, b) | (e4m3x2(c, d) << 16);
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+// the row scale amax / 448 and its inverse 448 / amax, both correctly rounded
+__device__ __forceinline__ void e4m3_scales(float amax, float& scale, float& inv) {
+  if (amax > 0.f) {
+    scale = __fdiv_rn(amax, 448.f);
+    inv = __fdiv_rn(448.f, amax);
+  } else {
+    scale = 1.f;
+    inv = 0.f;
+  }
+}
+
+// one warp per row, two passes over the row (amax, then the codes); cols % 4 == 0
+template <typename T>
+__global__ void __launch_bounds__(256) quant_rows_kernel(const T* __restrict__ x, int64_t rows,
+                                                         int cols, uint8_t* __restrict__ q,
+                                                         float* __restrict__ scale) {
+  const int lane = threadIdx.x & 31;
+  const int64_t i = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (i >= rows) return;
+  const T* row = x + i * cols;
+  float amax = 0.f;
+  for (int c = 4 * lane; c < cols; c += 128) {
+    const float4 v = load4<T>(row + c);
+    amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+  }
+  amax = warp_max(amax);
+  float sc, inv;
+  e4m3_scales(amax, sc, inv);
+  uint32_t* qrow = reinterpret_cast<uint32_t*>(q + i * cols);
+  for (int c = 4 * lane; c < cols; c += 128) qrow[c >> 2] = e4m3x4(load4<T>(row + c), inv);
+  if (lane == 0) scale[i] = sc;
+}
+
+// LN(X) * w (+ b) of a row held in registers (as add_ln_warp), then quantised
+__global__ void __launch_bounds__(256) ln_e4m3_warp(const float* __restrict__ X,
+                                                    const float* __restrict__ w,
+                                                    const float* __restrict__ b,
+                                                    uint8_t* __restrict__ q,
+                                                    float* __restrict__ scale, int64_t M, int D,
+                                                    float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t i = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (i >= M) return;
+  const int nc4 = D >> 2;
+  float4 v[kMaxChunks];
+#pragma unroll
+  for (int k = 0; k < kMaxChunks; ++k) {
+    const int c = lane + 32 * k;
+    v[k] = c < nc4 ? load4<float>(X + i * D + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  float mean, invs;
+  row_stats(v, lane, nc4, D, eps, mean, invs);
+  float amax = 0.f;
+#pragma unroll
+  for (int k = 0; k < kMaxChunks; ++k) {
+    const int c = lane + 32 * k;
+    if (c >= nc4) break;
+    const float4 g = load4<float>(w + 4 * c);
+    float4 o = make_float4((v[k].x - mean) * invs * g.x, (v[k].y - mean) * invs * g.y,
+                           (v[k].z - mean) * invs * g.z, (v[k].w - mean) * invs * g.w);
+    if (b) {
+      const float4 bb = load4<float>(b + 4 * c);
+      o.x += bb.x; o.y += bb.y; o.z += bb.z; o.w += bb.w;
+    }
+    v[k] = o;
+    amax = fmaxf(amax, fmaxf(fmaxf(fabsf(o.x), fabsf(o.y)), fmaxf(fabsf(o.z), fabsf(o.w))));
+  }
+  amax = warp_max(amax);
+  float sc, inv;
+  e4m3_scales(amax, sc, inv);
+  uint32_t* qrow = reinterpret_cast<uint32_t*>(q + i * D);
+#pragma unroll
+  for (int k = 0; k < kMaxChunks; ++k) {
+    const int c = lane + 32 * k;
+    if (c >= nc4) break;
+    qrow[c] = e4m3x4(v[k], inv);
+  }
+  if (lane == 0) scale[i] = sc;
+}
+
 // ---- generic widths: one block per row, row staged in shared memory ----
 __device__ float block_sum(float v, float* red) {
   v = warp_sum(v);
@@ -276,6 +374,27 @@ cudaError_t add_ln(float* X, const TR* R, const float* w, const float* b, TY* Y,
 cudaError_t cast_bf16(const float* X, bf16* Y, int64_t n, cudaStream_t st) {
   if (n <= 0) return cudaSuccess;
   cast_bf16_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(X, Y, n);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t quant_rows_e4m3(const T* x, int64_t rows, int cols, uint8_t* q, float* scale,
+                            cudaStream_t st) {
+  if (rows <= 0) return cudaSuccess;
+  if (cols <= 0 || cols % 4 != 0) return cudaErrorInvalidValue;
+  quant_rows_kernel<T><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(x, rows, cols, q, scale);
+  return cudaGetLastError();
+}
+template cudaError_t quant_rows_e4m3<float>(const float*, int64_t, int, uint8_t*, float*,
+                                            cudaStream_t);
+template cudaError_t quant_rows_e4m3<bf16>(const bf16*, int64_t, int, uint8_t*, float*,
+                                           cudaStream_t);
+
+cudaError_t ln_e4m3(const float* X, const float* w, const float* b, uint8_t* q, float* scale,
+                    int64_t rows, int D, float eps, cudaStream_t st) {
+  if (rows <= 0) return cudaSuccess;
+  if (D % 128 != 0 || D > 4 * 32 * kMaxChunks) return cudaErrorInvalidValue;
+  ln_e4m3_warp<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(X, w, b, q, scale, rows, D, eps);
   return cudaGetLastError();
 }
 

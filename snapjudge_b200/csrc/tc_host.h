@@ -44,6 +44,23 @@ inline bool make_map_bf16(CUtensorMap* m, const void* base, uint64_t inner, uint
   return r == CUDA_SUCCESS;
 }
 
+// 2D tensor of bytes (fp8 e4m3 codes) [rows, inner], box of box_rows x 128
+// bytes, 128-byte swizzle: the same shared-memory layout as a bf16 box of 64.
+inline bool make_map_u8(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows,
+                        uint64_t row_bytes, uint32_t box_inner, uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (row_bytes & 15)) return false;
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_rows};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
+                  box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 // 2D fp32 row-major tensor, box of box_rows x box_inner (box_inner * 4 == 128), 128-byte swizzle.
 inline bool make_map_f32(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows,
                          uint64_t row_bytes, uint32_t box_inner, uint32_t box_rows) {

@@ -44,7 +44,8 @@ class FastSnapjudge:
         self.cfg = cfg
         self.precision = precision
         self.D = cfg.hidden_size
-        prec = _lib.SJ_PREC_BF16 if precision == "bf16" else _lib.SJ_PREC_FP32
+        prec = {"bf16": _lib.SJ_PREC_BF16, "fp32": _lib.SJ_PREC_FP32,
+                "fp8": _lib.SJ_PREC_FP8}.get(precision, -1)
         if isinstance(cfg, SjConfig):
             sl = None
             c = _lib.FastConfig(cfg.hidden_size, cfg.num_layers, cfg.num_heads,
@@ -59,8 +60,8 @@ class FastSnapjudge:
                                 cfg.norm_eps, cfg.local_attention, sl, cfg.rope_theta_full,
                                 cfg.rope_theta_sliding, prec, device, max_tokens,
                                 _lib.SJ_ARCH_MODERNBERT)
-        if precision not in ("bf16", "fp32"):
-            raise ValueError(f"precision must be 'bf16' or 'fp32', got {precision!r}")
+        if prec < 0:
+            raise ValueError(f"precision must be 'bf16', 'fp32' or 'fp8', got {precision!r}")
         h = C.c_void_p()
         rc = L.sj_fast_create(C.byref(c), C.byref(h))
         if rc != 0:

@@ -90,3 +90,30 @@ def attn(qkv, cu, H, Dh, window=0, kv_lens=None):
     check(_lib.lib().sj_attn(_p(qkv), _p(cu_d), C.c_void_p(cu_h.ctypes.data), _p(kv), _p(O),
                              len(cu_h) - 1, H, Dh, window, _stream()))
     return O
+
+
+def quant_e4m3(x):
+    """fp32 x[rows, cols] -> (e4m3 codes uint8 [rows, cols], fp32 row scales [rows])."""
+    _need(x, torch.float32, "x")
+    rows, cols = x.shape
+    q = torch.empty(rows, cols, dtype=torch.uint8, device=x.device)
+    s = torch.empty(rows, dtype=torch.float32, device=x.device)
+    check(_lib.lib().sj_quant_e4m3(_p(x), rows, cols, _p(q), _p(s), _stream()))
+    return q, s
+
+
+def gemm_e4m3(A, sa, W, sw, bias=None, act=0, geglu=False):
+    """bf16 C[M,N] = act(sa sw (A W^T) + bias) on e4m3 codes A [M,K], W [N,K]
+    (geglu: W = [Wg; Wu] [2N, K], C = gelu(g) * u)."""
+    _need(A, torch.uint8, "A")
+    _need(W, torch.uint8, "W")
+    _need(sa, torch.float32, "sa")
+    _need(sw, torch.float32, "sw")
+    M, K = A.shape
+    N = W.shape[0] // 2 if geglu else W.shape[0]
+    C_ = torch.empty(M, N, dtype=torch.bfloat16, device=A.device)
+    if bias is not None:
+        _need(bias, torch.float32, "bias")
+    check(_lib.lib().sj_gemm_e4m3(_p(A), _p(W), _p(sa), _p(sw), _p(bias), _p(C_), M, N, K,
+                                  int(bias is not None), act, int(geglu), _stream()))
+    return C_

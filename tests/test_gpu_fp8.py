@@ -1,0 +1,151 @@
+"""The FP8 variant (SJ_PREC_FP8): e4m3 quantisation, the e4m3 tcgen05 GEMM, and
+the encoder with its QKV and Wi projections on e4m3 operands.
+
+The reference has no FP8 path, so the kernels are checked against what they
+define, and the encoder against the fp32 CPU forward with a bar of its own:
+* quantisation: bit-exact against torch's float32 -> float8_e4m3fn conversion
+  (round to nearest even) of x * (448 / amax), with scale = amax / 448, both
+  divisions correctly rounded in fp32;
+* GEMM: against a float64 product of the dequantised codes (code value x row
+  scale x channel scale), within bf16 output rounding: |got - want| <=
+  2^-7 |want| + 1e-5 rms(want);
+* encoder (C3 architecture, 12 x 768, ragged batch of 8): final hidden states
+  against the fp32 forward within a relative (Frobenius) error of 0.06 and a
+  row cosine of at least 0.998.  Measured on a B200: relative error 0.031
+  (bf16 mode 0.0024), smallest row cosine 0.9991, max-abs 0.15 (bf16 0.011).
+"""
+import numpy as np
+import pytest
+from scipy.special import erf
+
+torch = pytest.importorskip("torch")
+
+from oracle import oracle  # noqa: E402
+from snapjudge_b200 import ops, synth  # noqa: E402
+from snapjudge_b200.fast import FastSnapjudge, SnapjudgeError  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _blas():
+    oracle.set_blas()
+
+
+def ref_quant(x):
+    """CPU reference of sj_quant_e4m3: (codes uint8, scales fp32)."""
+    x = np.asarray(x, np.float32)
+    amax = np.abs(x).max(axis=1)
+    scale = np.where(amax > 0, amax / np.float32(448), np.float32(1)).astype(np.float32)
+    inv = np.where(amax > 0, np.float32(448) / np.where(amax > 0, amax, 1), 0).astype(np.float32)
+    y = (x * inv[:, None]).astype(np.float32)
+    codes = torch.from_numpy(y).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    return codes, scale
+
+
+def dequant(codes, scale):
+    v = torch.from_numpy(np.ascontiguousarray(codes)).view(torch.float8_e4m3fn).double().numpy()
+    return v * np.asarray(scale, np.float64)[:, None]
+
+
+def quant_dev(x):
+    q, s = ops.quant_e4m3(torch.from_numpy(np.ascontiguousarray(x, np.float32)).to(DEV))
+    return q, s
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 4), (7, 64), (300, 768), (2049, 2048)])
+def test_quant_e4m3_bit_exact(rows, cols):
+    rng = np.random.default_rng(rows + cols)
+    x = rng.standard_normal((rows, cols), dtype=np.float32)
+    x *= np.exp(rng.uniform(-6, 6, size=(rows, 1))).astype(np.float32)  # row magnitudes
+    x[0, : cols // 2] *= 1e-4  # tiny values (e4m3 subnormals) next to the row's maximum
+    if rows > 2:
+        x[1] = 0.0  # an all-zero row: scale 1, codes 0
+    q, s = quant_dev(x)
+    torch.cuda.synchronize()
+    want_q, want_s = ref_quant(x)
+    assert np.array_equal(s.cpu().numpy(), want_s)
+    assert np.array_equal(q.cpu().numpy(), want_q)
+
+
+def gelu(x):
+    return 0.5 * x * (1.0 + erf(x / np.sqrt(2.0)))
+
+
+def _close(got, want):
+    got, want = np.asarray(got, np.float64), np.asarray(want, np.float64)
+    tol = 2.0 ** -7 * np.abs(want) + 1e-5 * np.sqrt(np.mean(want ** 2))
+    bad = np.abs(got - want) > tol
+    assert not bad.any(), f"{bad.sum()} mismatches, max err {np.abs(got - want).max():.3g}"
+
+
+@pytest.mark.parametrize("M,N,K", [(37, 64, 128), (300, 384, 256), (129, 768, 768),
+                                   (2100, 2304, 768), (4096, 768, 768)])
+@pytest.mark.parametrize("act,bias", [(0, False), (1, True)])
+def test_gemm_e4m3(M, N, K, act, bias):
+    rng = np.random.default_rng(M + N + K)
+    A = rng.standard_normal((M, K), dtype=np.float32)
+    W = rng.standard_normal((N, K), dtype=np.float32) * 0.05
+    qa, sa = quant_dev(A)
+    qw, sw = quant_dev(W)
+    b = torch.from_numpy(rng.standard_normal(N, dtype=np.float32) * 0.1).to(DEV) if bias else None
+    got = ops.gemm_e4m3(qa, sa, qw, sw, b, act).float().cpu().numpy()
+    want = dequant(qa.cpu().numpy(), sa.cpu().numpy()) @ dequant(qw.cpu().numpy(),
+                                                                  sw.cpu().numpy()).T
+    if bias:
+        want = want + b.cpu().numpy().astype(np.float64)
+    if act == 1:
+        want = gelu(want)
+    _close(got, want)
+
+
+@pytest.mark.parametrize("M,F,K", [(200, 256, 128), (513, 2048, 768), (3000, 2048, 768),
+                                   (300, 192, 128)])
+def test_gemm_e4m3_geglu(M, F, K):
+    rng = np.random.default_rng(M + F)
+    A = rng.standard_normal((M, K), dtype=np.float32)
+    Wi = rng.standard_normal((2 * F, K), dtype=np.float32) * 0.05
+    qa, sa = quant_dev(A)
+    qw, sw = quant_dev(Wi)
+    got = ops.gemm_e4m3(qa, sa, qw, sw, geglu=True).float().cpu().numpy()
+    h = dequant(qa.cpu().numpy(), sa.cpu().numpy()) @ dequant(qw.cpu().numpy(), sw.cpu().numpy()).T
+    _close(got, gelu(h[:, :F]) * h[:, F:])
+
+
+def test_gemm_e4m3_rejects_bad_shapes():
+    qa = torch.zeros(8, 96, dtype=torch.uint8, device=DEV)
+    s = torch.ones(8, dtype=torch.float32, device=DEV)
+    with pytest.raises(SnapjudgeError, match="K % 128"):
+        ops.gemm_e4m3(qa, s, torch.zeros(64, 96, dtype=torch.uint8, device=DEV),
+                      torch.ones(64, dtype=torch.float32, device=DEV))
+
+
+def _rel(a, b):
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / np.linalg.norm(b))
+
+
+def test_fp8_encoder_against_fp32_forward():
+    """C3 architecture, ragged batch: the FP8 variant's final hidden states
+    against the fp32 CPU forward, beside the bf16 mode's error."""
+    spec = synth.SPECS["c3"]
+    t = synth.make_weights(spec)
+    rng = np.random.default_rng(12)
+    lengths = np.array([300, 251, 177, 128, 96, 64, 17, 1])
+    ids = rng.integers(0, spec.cfg.vocab_size, size=int(lengths.sum())).astype(np.int64)
+    want = oracle.Oracle(spec.cfg, t).encode_packed(ids, lengths)
+    h8 = FastSnapjudge(spec.cfg, t, precision="fp8").encode_packed(ids, lengths)
+    h16 = FastSnapjudge(spec.cfg, t, precision="bf16").encode_packed(ids, lengths)
+    assert np.isfinite(h8).all()
+    e8, e16 = _rel(h8, want), _rel(h16, want)
+    cos = np.sum(h8 * want, axis=1) / (np.linalg.norm(h8, axis=1) * np.linalg.norm(want, axis=1))
+    print(f"relative error: fp8 {e8:.4f}, bf16 {e16:.4f}; min row cosine fp8 {cos.min():.5f}; "
+          f"max abs fp8 {np.abs(h8 - want).max():.4f}, bf16 {np.abs(h16 - want).max():.4f}")
+    assert e8 <= 0.06 and cos.min() >= 0.998
+
+
+def test_fp8_is_decisionmodel_only():
+    cfg, seed = synth.SJ_SPECS["sj_tiny"]
+    with pytest.raises(SnapjudgeError):
+        FastSnapjudge(cfg, synth.make_sj_weights(cfg, seed), precision="fp8")
