@@ -177,6 +177,28 @@ __device__ __forceinline__ void unscale32(uint32_t (&r)[32], float sa, const flo
   }
 }
 
+__device__ __forceinline__ void unscale16(uint32_t (&r)[16], float sa, const float* sw) {
+  const float4* s4 = reinterpret_cast<const float4*>(sw);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float4 w = __ldg(s4 + k);
+    r[4 * k] = __float_as_uint(__uint_as_float(r[4 * k]) * (sa * w.x));
+    r[4 * k + 1] = __float_as_uint(__uint_as_float(r[4 * k + 1]) * (sa * w.y));
+    r[4 * k + 2] = __float_as_uint(__uint_as_float(r[4 * k + 2]) * (sa * w.z));
+    r[4 * k + 3] = __float_as_uint(__uint_as_float(r[4 * k + 3]) * (sa * w.w));
+  }
+}
+// 8 floats -> 8 bf16 (16 bytes)
+__device__ __forceinline__ uint4 pack_bf16x8(const float* v) {
+  uint32_t w[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * e], v[2 * e + 1]);
+    w[e] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
 template <int BN, int EPI, bool PAIR, bool F8>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
@@ -474,13 +496,61 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
         for (int hh = h0; hh < h1; ++hh) {
           const int c = hh * 64;
+          if constexpr (F8) {
+            // the head in two passes of 16 + 16 columns, so that the row's
+            // cos/sin stay in registers beside them; staged like store_chunk
+            const bool rot = col_base + c < ep.rope_cols;
+            uint8_t* rowp = stg + sbuf * (32 * 128) + lane * 128;
+            if (STAGED) {
+              if (lane == 0) bulk_wait_read<1>();
+              __syncwarp();
+            }
+#pragma unroll
+            for (int h2 = 0; h2 < 2; ++h2) {
+              uint32_t a[16], z[16];
+              tmem_ld16(tacc + c + 16 * h2, a);
+              tmem_ld16(tacc + c + 32 + 16 * h2, z);
+              tmem_ld_wait();
+              unscale16(a, sa, ep.sw + col_base + c + 16 * h2);
+              unscale16(z, sa, ep.sw + col_base + c + 32 + 16 * h2);
+              float va[16], vz[16];
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const float x0 = __uint_as_float(a[j]), x1 = __uint_as_float(z[j]);
+                va[j] = rot ? x0 * cs[16 * h2 + j] - x1 * sn[16 * h2 + j] : x0;
+                vz[j] = rot ? x1 * cs[16 * h2 + j] + x0 * sn[16 * h2 + j] : x1;
+              }
+              if (STAGED) {
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                  *reinterpret_cast<uint4*>(rowp + (((2 * h2 + u) ^ (lane & 7)) << 4)) =
+                      pack_bf16x8(va + 8 * u);
+                  *reinterpret_cast<uint4*>(rowp + (((4 + 2 * h2 + u) ^ (lane & 7)) << 4)) =
+                      pack_bf16x8(vz + 8 * u);
+                }
+              } else if (live) {
+                uint4* d0 = reinterpret_cast<uint4*>(ep.C + (int64_t)row * ep.ldc + col_base + c + 16 * h2);
+                uint4* d1 = reinterpret_cast<uint4*>(ep.C + (int64_t)row * ep.ldc + col_base + c + 32 + 16 * h2);
+                d0[0] = pack_bf16x8(va);
+                d0[1] = pack_bf16x8(va + 8);
+                d1[0] = pack_bf16x8(vz);
+                d1[1] = pack_bf16x8(vz + 8);
+              }
+            }
+            if (STAGED) {
+              fence_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+                tma_store_2d(&mapC, stg + sbuf * (32 * 128), col_base + c, m0 + q * 32);
+                bulk_commit();
+              }
+              sbuf ^= 1;
+            }
+            continue;
+          }
           tmem_ld32(tacc + c, r0);
           tmem_ld32(tacc + c + 32, r1);
           tmem_ld_wait();
-          if constexpr (F8) {
-            unscale32(r0, sa, ep.sw + col_base + c);
-            unscale32(r1, sa, ep.sw + col_base + c + 32);
-          }
           float v[64];
           const bool rot = col_base + c < ep.rope_cols;
 #pragma unroll
