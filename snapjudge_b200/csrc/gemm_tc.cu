@@ -413,6 +413,28 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_2d(stg + k * 4096, &mapC, &xb[k], nb * BN + hf * BN / 2 + 32 * k, m0 + q * 32);
         }
       }
+      // RoPE: this row's cos/sin (32 each, 16-byte loads), fetched before the
+      // accumulator is ready so that their latency hides behind the wait
+      float cs[32], sn[32];
+      if constexpr (EPI == TC_ROPE) {
+        constexpr int HEADS = BN / 64;
+        const int r = m0 + q * 32 + lane;
+        const int h0 = hf * ((HEADS + 1) / 2), h1 = min(HEADS, (hf + 1) * ((HEADS + 1) / 2));
+        if (r < M && nb * BN + h0 * 64 < ep.rope_cols && h0 < h1) {
+          const int p = ep.pos[r];
+          const float4* c4 = reinterpret_cast<const float4*>(ep.cos_t + (int64_t)p * 32);
+          const float4* s4 = reinterpret_cast<const float4*>(ep.sin_t + (int64_t)p * 32);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const float4 a = __ldg(c4 + k), z = __ldg(s4 + k);
+            cs[4 * k] = a.x; cs[4 * k + 1] = a.y; cs[4 * k + 2] = a.z; cs[4 * k + 3] = a.w;
+            sn[4 * k] = z.x; sn[4 * k + 1] = z.y; sn[4 * k + 2] = z.z; sn[4 * k + 3] = z.w;
+          }
+        } else {
+#pragma unroll
+          for (int k = 0; k < 32; ++k) { cs[k] = 1.f; sn[k] = 0.f; }
+        }
+      }
       int ok = 1;
       if (lane == 0) ok = mbar_wait(&tfull_bar[b], aphase) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -477,22 +499,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         constexpr int HEADS = BN / 64;
         const int col_base = nb * BN;
         const int h0 = hf * ((HEADS + 1) / 2), h1 = min(HEADS, (hf + 1) * ((HEADS + 1) / 2));
-        // this row's cos/sin (32 each), loaded once per tile with 16-byte loads
-        float cs[32], sn[32];
-        if (live && col_base + h0 * 64 < ep.rope_cols && h0 < h1) {
-          const int p = ep.pos[row];
-          const float4* c4 = reinterpret_cast<const float4*>(ep.cos_t + (int64_t)p * 32);
-          const float4* s4 = reinterpret_cast<const float4*>(ep.sin_t + (int64_t)p * 32);
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const float4 a = __ldg(c4 + k), z = __ldg(s4 + k);
-            cs[4 * k] = a.x; cs[4 * k + 1] = a.y; cs[4 * k + 2] = a.z; cs[4 * k + 3] = a.w;
-            sn[4 * k] = z.x; sn[4 * k + 1] = z.y; sn[4 * k + 2] = z.z; sn[4 * k + 3] = z.w;
-          }
-        } else {
-#pragma unroll
-          for (int k = 0; k < 32; ++k) { cs[k] = 1.f; sn[k] = 0.f; }
-        }
 #pragma unroll 1
         for (int hh = h0; hh < h1; ++hh) {
           const int c = hh * 64;
