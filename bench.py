@@ -369,6 +369,29 @@ def main():
         qkv512 = torch.randn(int(cu512[-1]), 3 * H2 * Dh2, device=dev).to(torch.bfloat16)
         ams512 = time_attn(qkv512, cu512)
         fl512 = 64 * 4.0 * 512 * 512 * Dh2 * H2
+        # C4's attention shape: 32 sequences of 2048 tokens, 16 heads of 64 (compute-bound)
+        H4 = 16
+        cu2048 = synth.cu_seqlens(np.full(32, 2048))
+        qkv2048 = torch.randn(int(cu2048[-1]), 3 * H4 * Dh2, device=dev).to(torch.bfloat16)
+
+        def time_attn_h(x, cu_x, H, reps=10):
+            out = 0.0
+            with torch.cuda.stream(st):
+                for _ in range(3):
+                    ops.attn(x, cu_x, H, Dh2)
+                for _ in range(reps):
+                    flush.zero_()
+                    a0 = torch.cuda.Event(enable_timing=True)
+                    a1 = torch.cuda.Event(enable_timing=True)
+                    a0.record(st)
+                    ops.attn(x, cu_x, H, Dh2)
+                    a1.record(st)
+                    a1.synchronize()
+                    out += a0.elapsed_time(a1) / reps
+            return out
+
+        ams2048 = time_attn_h(qkv2048, cu2048, H4)
+        fl2048 = 32 * 4.0 * 2048 * 2048 * Dh2 * H4
         burst = pk.get("bf16_tflops", FALLBACK["bf16_tflops"])
         line["attention"] = {"config": "c2: 64 seqs x 12 heads x 64, lengths U[32,512], bf16",
                              "ms": ams, "tflops": fl / (ams / 1e3) / 1e12,
@@ -376,6 +399,10 @@ def main():
                              "peak": burst, "peak_kind": f"{pk_kind} burst bf16",
                              "n512": {"ms": ams512, "tflops": fl512 / (ams512 / 1e3) / 1e12,
                                       "frac_of_peak": fl512 / (ams512 / 1e3) / 1e12 / burst},
+                             "n2048_c4": {"config": "32 seqs x 2048 tokens, 16 heads x 64",
+                                          "ms": ams2048,
+                                          "tflops": fl2048 / (ams2048 / 1e3) / 1e12,
+                                          "frac_of_peak": fl2048 / (ams2048 / 1e3) / 1e12 / burst},
                              "l2": "L2 flushed (256 MB write) before every timed launch"}
         if world == 1 and not a.no_fp8:
             line["fp8"] = fp8_section(spec, weights, a, local, st, pass_args, probs_d, T, value)
