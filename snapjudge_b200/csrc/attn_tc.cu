@@ -155,6 +155,13 @@ __device__ __forceinline__ void exp32(const uint32_t (&r)[32], f32x2 scale2, f32
   }
 }
 
+// 32 bytes to global memory in one store (address 32-byte aligned)
+__device__ __forceinline__ void st_global_v8(void* p, const uint32_t (&v)[8]) {
+  asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(v[0]), "r"(v[1]),
+               "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
+}
+
 struct __align__(16) Item {
   int q0, h, s0, n, nk, t_lo, n_kv, pad;  // n_kv: -1 idle grid slot, 0 no visible key
 };
@@ -210,6 +217,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   uint8_t* sKV = smem + Q_BYTES;  // stage s: K at s * 2 * KV, V at + KV
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const bool leader = tid == 0;
+  const bool o32 = (reinterpret_cast<uintptr_t>(O) & 31) == 0;
 
   // this CTA's items: w = blockIdx.x + k * gridDim.x, k < cnt
   const int cnt =
@@ -518,18 +526,25 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     fence_before_sync();
     if (live) {
       const float inv = l > 0.f ? 1.f / l : 0.f;
+      // the row's 64 outputs in four 32-byte stores when O is 32-byte aligned
+      // (rows are then too: their pitch is H * 128 bytes), else eight of 16
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        uint32_t wv[4];
+      for (int q = 0; q < 4; ++q) {
+        uint32_t wv[8];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int d = q * 8 + 2 * e;
+        for (int e = 0; e < 8; ++e) {
+          const int d = q * 16 + 2 * e;
           const float a = __uint_as_float(d < 32 ? oa[d] : ob[d - 32]) * inv;
           const float b2 = __uint_as_float(d + 1 < 32 ? oa[d + 1] : ob[d - 31]) * inv;
           __nv_bfloat162 hb = __floats2bfloat162_rn(a, b2);
           wv[e] = *reinterpret_cast<uint32_t*>(&hb);
         }
-        reinterpret_cast<uint4*>(orow)[q] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+        if (o32) {
+          st_global_v8(orow + 16 * q, wv);
+        } else {
+          reinterpret_cast<uint4*>(orow)[2 * q] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+          reinterpret_cast<uint4*>(orow)[2 * q + 1] = make_uint4(wv[4], wv[5], wv[6], wv[7]);
+        }
       }
     }
   }

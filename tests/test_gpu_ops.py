@@ -135,3 +135,28 @@ def test_attention_c2_shapes():
         s, e = cu[b], cu[b + 1]
         want = oracle.attention_packed(x[s:e, 0], x[s:e, 1], x[s:e, 2], [e - s])
         assert_bf16_close(O[s:e], want, k=4.0)
+
+
+def test_attention_output_alignment():
+    """The tensor-core attention writes each output row with 32-byte stores when
+    O is 32-byte aligned and falls back to 16-byte stores otherwise: an O
+    buffer at a 16-byte offset gives the same bits as an aligned one."""
+    import ctypes as C
+    from snapjudge_b200 import _lib
+    H, Dh = 4, 64
+    lens = np.array([200, 77, 1, 128])
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    T = int(cu[-1])
+    qkv = bf(rnd((T, 3 * H * Dh), 13))
+    want = ops.attn(qkv, cu, H, Dh)
+    big = torch.zeros(T * H * Dh + 8, dtype=torch.bfloat16, device=DEV)
+    O = big[8:]  # 16 bytes past a 256-byte-aligned allocation
+    assert O.data_ptr() % 32 == 16
+    cu_d = torch.from_numpy(cu).to(DEV)
+    rc = _lib.lib().sj_attn(C.c_void_p(qkv.data_ptr()), C.c_void_p(cu_d.data_ptr()),
+                            C.c_void_p(cu.ctypes.data), None, C.c_void_p(O.data_ptr()),
+                            len(lens), H, Dh, 0, C.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert torch.equal(O.view(T, H * Dh), want)
+    assert (big[:8] == 0).all()
