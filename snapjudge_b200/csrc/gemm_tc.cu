@@ -272,7 +272,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = unit; t < num_tiles && !abort_sh; t += units) {
       const int m0 = (t / n_tiles) * TILE_M + (int)rank * BM, nb = t % n_tiles;
       for (int kb = 0; kb < k_blocks; ++kb) {
-        if (!mbar_wait(&empty_bar[stage], phase ^ 1)) {
+        if (!mbar_wait<true>(&empty_bar[stage], phase ^ 1)) {
           record_err(ep.err, 1);
           abort_sh = 1;
           break;
@@ -308,7 +308,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!PAIR || rank == 0) {
       for (int i = 0; i < STAGES && i < issued; ++i) {
         if (--stage < 0) { stage = STAGES - 1; phase ^= 1; }
-        if (!mbar_wait(&full_bar[stage], phase)) record_err(ep.err, 2);
+        if (!mbar_wait<true>(&full_bar[stage], phase)) record_err(ep.err, 2);
       }
     }
   } else if (warp == 1 && lane == 0 && rank == 0) {
@@ -319,7 +319,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = unit; t < num_tiles && !abort_sh; t += units, ++local) {
       const int b = local & 1;
       const uint32_t aphase = (local >> 1) & 1;
-      if (!mbar_wait(&tempty_bar[b], aphase ^ 1)) {
+      if (!mbar_wait<true>(&tempty_bar[b], aphase ^ 1)) {
         record_err(ep.err, 3);
         abort_sh = 1;
         break;
@@ -327,7 +327,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_after_sync();
       const uint32_t d = tmem_base + b * BN;
       for (int kb = 0; kb < k_blocks; ++kb) {
-        if (!mbar_wait(&full_bar[stage], phase)) {
+        if (!mbar_wait<true>(&full_bar[stage], phase)) {
           record_err(ep.err, 4);
           abort_sh = 1;
           break;
@@ -357,7 +357,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (PAIR) mma_commit_pair(&drain_bar, 0x1);
     else mma_commit(&drain_bar);
-    if (!mbar_wait(&drain_bar, 0)) record_err(ep.err, 5);
+    if (!mbar_wait<true>(&drain_bar, 0)) record_err(ep.err, 5);
   } else if (warp >= 2) {
     // ---------------- epilogue ----------------
     const int q = warp & 3;             // TMEM lane quarter this warp may access
@@ -436,7 +436,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       int ok = 1;
-      if (lane == 0) ok = mbar_wait(&tfull_bar[b], aphase) ? 1 : 0;
+      if (lane == 0) ok = mbar_wait<true>(&tfull_bar[b], aphase) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok || abort_sh) {
         if (lane == 0 && !ok) { record_err(ep.err, 6); abort_sh = 1; }
@@ -589,7 +589,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int k = 0; k < NCH; ++k) {
           int okx = 1;
-          if (lane == 0) okx = mbar_wait(&xb[k & 1], (xphase >> (k & 1)) & 1u) ? 1 : 0;
+          if (lane == 0) okx = mbar_wait<true>(&xb[k & 1], (xphase >> (k & 1)) & 1u) ? 1 : 0;
           okx = __shfl_sync(0xffffffffu, okx, 0);
           xphase ^= 1u << (k & 1);
           if (!okx) {

@@ -41,11 +41,30 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
                "r"(bytes)
                : "memory");
 }
+// Test the phase; a thread whose phase is not complete may be suspended for a
+// short, system-dependent time before the test returns false.
 __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// As mbar_try with a suspend-time hint of 1 ms: the thread sleeps in hardware
+// until the phase completes (or the hint runs out) instead of re-issuing the
+// test.  Warps that spin on try_wait without it slow the MMA issue of a
+// warp-specialised GEMM on the same SM (65536 x 4096 x 768 pair GEMM:
+// 317 -> 297 us); the attention kernel's short, latency-bound hand-offs are
+// faster without it.
+__device__ __forceinline__ bool mbar_try_sleep(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 1000000;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
       : "r"(smem_u32(bar)), "r"(parity)
@@ -65,12 +84,15 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 // Wait for the phase with the given parity to complete; false after kWaitNs.
+// kSleep selects mbar_try_sleep for the tests.
+template <bool kSleep = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  if (mbar_try(bar, parity)) return true;
+  auto test = [&]() { return kSleep ? mbar_try_sleep(bar, parity) : mbar_try(bar, parity); };
+  if (test()) return true;
   const uint64_t t0 = globaltimer();
   while (true) {
     for (int i = 0; i < 64; ++i)
-      if (mbar_try(bar, parity)) return true;
+      if (test()) return true;
     if (globaltimer() - t0 > kWaitNs) return false;
   }
 }
