@@ -248,9 +248,14 @@ __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
                    : "memory");
 }
+// Arrive on an mbarrier of a CTA in the cluster (default semantics: release at
+// CTA scope).  Used to hand a TMEM accumulator back to the pair's MMA thread:
+// the epilogue's tcgen05.wait::ld and tcgen05.fence::before_thread_sync
+// already order its TMEM reads before this arrive.  A cluster-scope release
+// here cost ~3300 cycles per tile in the arriving warp (a memory fence) and
+// slowed the pair GEMM by 1-4 %.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
-               : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
