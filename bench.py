@@ -48,10 +48,10 @@ PEAKS = os.path.join(ROOT, "MEASURED_PEAKS.json")
 FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per token of the
 # Wi+GEGLU launch, from the ncu capture summarised in profiles/gemm_geglu_c5.md
-# (56.65 MB + 84.65 MB for a 32768-token launch).  The launch's traffic grows in
+# (56.66 MB + 83.79 MB for a 32768-token launch).  The launch's traffic grows in
 # proportion to its tokens (A rows read once, G rows written once, W 6.3 MB), so
 # the bench scales it to its own launch size.
-GEGLU_DRAM_BYTES_PER_TOKEN = (56.652032e6 + 84.651776e6) / 32768
+GEGLU_DRAM_BYTES_PER_TOKEN = (56.664576e6 + 83.79136e6) / 32768
 
 
 def peaks():
