@@ -21,9 +21,11 @@
 // F8 instances take e4m3 A and W (tcgen05 kind::f8f6f4, 128-element k-blocks:
 // the same 128-byte swizzled rows) with a scale per A row and per W row; the
 // epilogue multiplies the fp32 accumulator by both before its own work.
-// The epilogue of tile i overlaps the MMAs of tile i+1 (double-buffered TMEM).
-// Every mbarrier wait is bounded; a wait that runs out records an error code
-// and the CTA winds down (no trap).
+// The epilogue of tile i overlaps the MMAs of tile i+1 (double-buffered TMEM);
+// each epilogue warp hands its accumulator back with a plain remote arrive.
+// Every mbarrier wait is bounded and sleeps in hardware between tests
+// (mbar_wait<true>: waiters that re-issue try_wait slow the MMA issue); a
+// wait that runs out records an error code and the CTA winds down (no trap).
 #include <algorithm>
 
 #include "common.cuh"
