@@ -3,16 +3,22 @@
 
 Workload: the base-encoder architecture (12 pre-LN layers,
 d_model 768, 12 heads x 64, GEGLU FFN 2048, vocab 32768, RoPE), seeded
-synthetic N(0, 0.02) weights, 32768 requests per GPU packed varlen with
+synthetic N(0, 0.02) weights, ONE set of 32768 requests packed varlen with
 lengths log-normal(median 48, sigma 0.8) clipped to [4, 512], uniform token
 ids, and four linear decision heads on [CLS] (choice-3, choice-8, score-5,
-noul).  One step = the whole batch of this rank through the encoder and the
-heads.  Per-GPU work is fixed (weak scaling); ranks share nothing on the data
-path (no collective); the max over ranks of the device time is reported.
+noul).  Every rank generates the same set (same seed) and takes its share
+with the length-aware partition of snapjudge_b200/shard.py (LPT on a
+cost model of linear + attention work), so the total work is fixed as N grows
+(strong scaling).  One step = this rank's share through the encoder and the
+heads; ranks share nothing on the data path (no collective); the max over
+ranks of the device time is reported and `value` = all 32768 requests' tokens
+/ that time.
 
 * value  — device-resident inputs, CUDA events on the launch stream.
 * e2e    — the public C ABI call sj_fast_decide with pinned host buffers:
-           host->device ids, device->host probabilities inside the timed region.
+           host->device ids, device->host probabilities inside the timed
+           region, then (N > 1) the host-side gather of every rank's
+           decisions into request order on rank 0 (gloo, CPU tensors).
 * roofline — the dominant kernel (Wi projection + GEGLU gate), its launches
            timed live with CUDA events inside the timed steps.
 * cpu_baseline — the reference's own CPU forward (src/model.cpp, compiled
@@ -123,54 +129,101 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ workload
-def workload(rank: int, requests: int):
+def workload(requests: int):
+    """The one C5 request set (identical on every rank)."""
     spec = synth.SPECS["c5"]
-    lengths = synth.make_lengths(spec, batch=requests, seed=spec.seed + 1000 + 7919 * rank)
-    ids = synth.make_ids(spec, lengths, seed=spec.seed + 2000 + 7919 * rank)
+    lengths = synth.make_lengths(spec, batch=requests, seed=spec.seed + 1000)
+    ids = synth.make_ids(spec, lengths, seed=spec.seed + 2000)
     return spec, lengths, ids
 
 
 def passes(lengths: np.ndarray, max_tokens: int):
-    """Split requests into consecutive passes of at most max_tokens tokens."""
-    out, b0, tok = [], 0, 0
-    for b, n in enumerate(lengths):
-        if tok + n > max_tokens and b > b0:
-            out.append((b0, b))
-            b0, tok = b, 0
-        tok += int(n)
-    out.append((b0, len(lengths)))
-    return out
+    """Split requests into consecutive passes of at most max_tokens tokens,
+    as few as fit and of near-equal size (a small last pass would run the
+    kernels on a fraction of the GPU)."""
+    total = int(np.sum(lengths))
+    k = max(1, -(-total // max_tokens))
+    while True:
+        target = -(-total // k)
+        out, b0, tok = [], 0, 0
+        for b, n in enumerate(lengths):
+            if tok + n > target and b > b0:
+                out.append((b0, b))
+                b0, tok = b, 0
+            tok += int(n)
+        out.append((b0, len(lengths)))
+        sizes = [int(np.sum(lengths[x:y])) for x, y in out]
+        if max(sizes) <= max_tokens:
+            return out
+        k += 1
+
+
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
 # ------------------------------------------------------------------ CPU reference
-def reference_sample(spec, weights, seconds: float, min_req: int, max_req: int, seed: int):
-    """Time the reference CPU forward (+ the same heads) request by request.
+_REF_MODELS: dict = {}
 
-    Returns (tokens, seconds, n_requests, kind, cores)."""
+
+def _ref_encoder(spec, weights):
+    """(padded-batch encode function, kind): the reference's own CPU
+    DecisionModel::encode when it was compiled into oracle/_ref, else the C
+    restatement of it."""
     from oracle import oracle
     from snapjudge_b200.checkpoint import save_checkpoint
+    key = spec.name
+    if key not in _REF_MODELS:
+        D = spec.cfg.hidden_size
+        if oracle.ref_available():
+            d = tempfile.mkdtemp(prefix="sjref_")
+            save_checkpoint(d, spec.cfg, weights)
+            model = oracle.RefModel(d)
+            _REF_MODELS[key] = (lambda x, m: model.encode(x, m, D), "reference", model)
+        else:
+            oracle.set_blas()
+            orc = oracle.Oracle(spec.cfg, weights)
+            _REF_MODELS[key] = (lambda x, m: orc.encode_padded(x, m), "port", orc)
+    f, kind, _ = _REF_MODELS[key]
+    return f, kind
+
+
+def reference_sample(spec, weights, seconds: float, min_req: int, max_req: int, seed: int,
+                     batch: int = 1):
+    """Time the reference CPU forward (+ the same heads) on a bounded sample.
+
+    batch == 1: one request per encode call (no padding).  batch > 1: the
+    requests in arrival order, `batch` per call, right-padded to the longest
+    of the call with an attention mask — the padded batch Agent::predict_batch
+    collates (src/agent.cpp:183-212); only valid tokens are counted.
+    Returns (tokens, seconds, n_requests, kind, cores)."""
+    from oracle import oracle
     lengths = synth.make_lengths(spec, batch=max_req, seed=seed)
     ids = synth.make_ids(spec, lengths, seed=seed + 1)
     cu = synth.cu_seqlens(lengths)
-    D = spec.cfg.hidden_size
-    if oracle.ref_available():
-        d = tempfile.mkdtemp(prefix="sjref_")
-        save_checkpoint(d, spec.cfg, weights)
-        model = oracle.RefModel(d)
-        enc = lambda x: model.encode(x[None], np.ones_like(x)[None], D)[0]  # noqa: E731
-        kind = "reference"
-    else:
-        oracle.set_blas()
-        orc = oracle.Oracle(spec.cfg, weights)
-        enc = lambda x: orc.encode_padded(x[None], np.ones_like(x)[None])[0]  # noqa: E731
-        kind = "port"
-    enc(ids[:8])  # warm the BLAS threads
+    enc, kind = _ref_encoder(spec, weights)
+    x = ids[:8]
+    enc(x[None], np.ones_like(x)[None])  # warm the BLAS threads
     tok, n, t0 = 0, 0, time.perf_counter()
     while n < max_req and (n < min_req or time.perf_counter() - t0 < seconds):
-        h = enc(ids[cu[n]:cu[n + 1]])
-        oracle.task_heads(h[:1], weights, spec.heads)
-        tok += int(lengths[n])
-        n += 1
+        b1 = min(max_req, n + batch)
+        L = int(lengths[n:b1].max())
+        pid = np.zeros((b1 - n, L), np.int64)
+        mask = np.zeros((b1 - n, L), np.int64)
+        for r in range(n, b1):
+            pid[r - n, :lengths[r]] = ids[cu[r]:cu[r + 1]]
+            mask[r - n, :lengths[r]] = 1
+        h = enc(pid, mask)
+        oracle.task_heads(h[:, 0, :], weights, spec.heads)
+        tok += int(lengths[n:b1].sum())
+        n = b1
     return tok, time.perf_counter() - t0, n, kind, _NPROC
 
 
@@ -181,7 +234,8 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--requests", type=int, default=32768, help="requests per GPU per step")
+    ap.add_argument("--requests", type=int, default=32768,
+                    help="requests of the whole job (split across the ranks)")
     ap.add_argument("--max-tokens", type=int, default=262144, help="tokens per device pass")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -195,29 +249,43 @@ def main():
     cfgd = {"workload": "c5 serving batch: base encoder 12x768 (12 heads x 64, GEGLU 2048, "
                         "vocab 32768), requests packed varlen, lengths lognormal(48, 0.8) "
                         "clipped to [4, 512], 4 [CLS] heads (choice-3/8, score-5, noul)",
-            "requests_per_gpu": a.requests, "parallelism": f"request-sharded x{world}",
+            "requests": a.requests,
+            "parallelism": f"one request set split across {world} GPU(s) by "
+                           f"shard.partition (LPT, cost n + n^2/4608), host-side gather",
             "l2": "inputs larger than L2 (bf16 weights 0.17 GB + ~4 GB activations per pass)"}
 
     if a.impl == "reference":
         if rank != 0:
             return 0
         weights = synth.make_weights(spec)
-        steps = []
-        for s in range(a.warmup + a.steps):
-            tok, sec, n, kind, cores = reference_sample(spec, weights, 8.0, 4, 64,
-                                                        seed=spec.seed + 50000 + s)
-            if s >= a.warmup:
-                steps.append((tok, sec, n))
-        tok = sum(x[0] for x in steps)
-        sec = sum(x[1] for x in steps)
-        v = tok / sec
+        arms = {}
+        for batch in (1, 16):
+            steps = []
+            for s in range(a.warmup + a.steps):
+                tok, sec, n, kind, cores = reference_sample(spec, weights, 2.5, 4, 256,
+                                                            seed=spec.seed + 50000 + s,
+                                                            batch=batch)
+                if s >= a.warmup:
+                    steps.append((tok, sec, n))
+            tok = sum(x[0] for x in steps)
+            sec = sum(x[1] for x in steps)
+            arms[batch] = {"value": tok / sec, "tokens": tok, "seconds": sec,
+                           "requests": sum(x[2] for x in steps)}
+        best = max(arms, key=lambda b: arms[b]["value"])
+        v = arms[best]["value"]
+        sec = arms[best]["seconds"]
+        how = {1: "one request per encode call",
+               16: "16 requests per encode call, right-padded as Agent::predict_batch collates"}
         line = {"metric": "encoder tokens/sec", "value": v, "unit": "tokens/s", "n_gpus": world,
                 "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1e3 * sec / a.steps,
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
                 "dtype": "f32", "data": "synthetic", "impl": "reference", "config": cfgd,
                 "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": kind,
-                                 "sample": f"{sum(x[2] for x in steps)} c5 requests "
-                                           f"({tok} tokens), one request per encode call"},
+                                 "cpu_model": cpu_model(),
+                                 "sample": f"{arms[best]['requests']} c5 requests "
+                                           f"({arms[best]['tokens']} tokens), {how[best]} "
+                                           f"(the faster of the two call shapes)",
+                                 "by_call_shape": {how[b]: arms[b]["value"] for b in arms}},
                 "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
@@ -226,15 +294,23 @@ def main():
     import torch
     torch.cuda.set_device(local)
     dist = None
+    gloo = None
     if world > 1:
         import datetime
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                 device_id=torch.device("cuda", local))
+        # host-side gather of the decisions (CPU tensors), no NCCL on the data path
+        gloo = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=180))
+    from snapjudge_b200 import shard
     from snapjudge_b200.fast import FastSnapjudge
 
     weights = synth.make_weights(spec)
-    _, lengths, ids = workload(rank, a.requests)
+    _, all_lengths, all_ids = workload(a.requests)
+    T_job = int(all_lengths.sum())
+    groups = shard.partition(all_lengths, world)
+    mine = groups[rank]
+    ids, lengths = shard.rank_batch(all_ids, all_lengths, mine)
     T = int(lengths.sum())
     eng = FastSnapjudge(spec.cfg, weights, precision="bf16", heads=spec.heads, device=local,
                         max_tokens=a.max_tokens)
@@ -282,13 +358,19 @@ def main():
     prof = eng.profile(reset=True)
     eng.set_profiling(False)
     gpu_launches = int(sum(n for _, n in prof.values()))
+    rank_ms = [ms]
+    rank_tok = [T]
     if dist:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    value = T * world * a.steps / (ms / 1e3)
+        t = torch.zeros(2 * world, device=dev, dtype=torch.float64)
+        t[2 * rank] = ms
+        t[2 * rank + 1] = T
+        dist.all_reduce(t)  # every rank's time and tokens (outside the timed region)
+        rank_ms = t[0::2].tolist()
+        rank_tok = [int(x) for x in t[1::2].tolist()]
+        ms = max(rank_ms)
+    value = T_job * a.steps / (ms / 1e3)
 
-    # roofline of the dominant kernel (Wi projection + GEGLU gate)
+    # roofline of the dominant kernel (Wi projection + GEGLU gate), this rank
     pk, pk_kind = peaks()
     D, F, L = spec.cfg.hidden_size, spec.cfg.intermediate_size, spec.cfg.num_hidden_layers
     g_ms, g_n = prof["geglu"]
@@ -302,123 +384,146 @@ def main():
                 "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                 "peak_kind": f"{pk_kind} sustained bf16", "traffic": traffic,
                 "flops_per_launch": flops_per_launch, "launch_ms": dur,
-                "share_of_step": g_ms / ms if ms > 0 else None}
+                "share_of_step": g_ms / rank_ms[rank] if rank_ms[rank] > 0 else None}
     kernels = {k: {"ms_per_step": v[0] / a.steps, "launches_per_step": v[1] // max(1, a.steps)}
                for k, v in prof.items()}
 
-    # end to end through the public C ABI with pinned host buffers
+    # end to end through the public C ABI with pinned host buffers, then the
+    # host-side gather of all ranks' decisions into request order on rank 0
     ids_pin = torch.from_numpy(ids).pin_memory()
     cu_pin = torch.from_numpy(cu_all.astype(np.int32)).pin_memory()
     out_pin = torch.empty(len(lengths), nout, dtype=torch.float32).pin_memory()
     ids_np, cu_np, out_np = ids_pin.numpy(), cu_pin.numpy(), out_pin.numpy()
-    for _ in range(max(1, a.warmup)):
+    gmax = max(len(g) for g in groups)
+    send = torch.zeros(gmax, nout, dtype=torch.float32)
+    recv = [torch.zeros(gmax, nout, dtype=torch.float32) for _ in range(world)]
+    gathered = {}
+
+    def e2e_step():
         eng.decide(ids_np, lengths, out=out_np, cu=cu_np)
+        if gloo is None:
+            gathered["probs"] = out_np
+            return
+        send[:len(mine)] = out_pin
+        dist.gather(send, recv if rank == 0 else None, dst=0, group=gloo)
+        if rank == 0:
+            gathered["probs"] = shard.gather([r[:len(g)].numpy() for r, g in zip(recv, groups)],
+                                             groups, len(all_lengths))
+
+    for _ in range(max(1, a.warmup)):
+        e2e_step()
     barrier()
     t0 = time.perf_counter()
     for _ in range(a.steps):
-        eng.decide(ids_np, lengths, out=out_np, cu=cu_np)
+        e2e_step()
     e2e_s = time.perf_counter() - t0
     if dist:
         t = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
-    e2e = {"value": T * world * a.steps / e2e_s, "unit": "tokens/s",
-           "h2d_bytes_per_step": int(ids.nbytes + cu_np.nbytes),
-           "d2h_bytes_per_step": int(out_np.nbytes), "ms_per_step": 1e3 * e2e_s / a.steps}
+    # bytes copied per step by all ranks together: ids and cu_seqlens in,
+    # probabilities out (each rank copies its own share)
+    e2e = {"value": T_job * a.steps / e2e_s, "unit": "tokens/s",
+           "h2d_bytes_per_step": int(all_ids.nbytes + 4 * (len(all_lengths) + world)),
+           "d2h_bytes_per_step": int(4 * nout * len(all_lengths)),
+           "ms_per_step": 1e3 * e2e_s / a.steps}
+    if world > 1:
+        e2e["gather"] = "host-side gather of all decisions on rank 0 (gloo) inside the timed region"
     # the device-resident and host-API results agree
     assert np.array_equal(out_np, probs_d.cpu().numpy()), "e2e and device results differ"
 
     line = {"metric": "encoder tokens/sec", "value": value, "unit": "tokens/s",
             "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
-            "ms_per_step": ms / a.steps, "higher_is_better": True, "scaling": "weak",
+            "ms_per_step": ms / a.steps, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,0.02) weights)",
-            "config": dict(cfgd, tokens_per_gpu=T, passes=len(P), max_tokens_per_pass=a.max_tokens),
+            "config": dict(cfgd, tokens_total=T_job, tokens_this_rank=T, passes=len(P),
+                           max_tokens_per_pass=a.max_tokens),
             "clocks": clk, "e2e": e2e, "gpu_launches": gpu_launches, "roofline": roofline,
             "kernels": kernels}
+    if world > 1:
+        line["ranks"] = {"tokens": rank_tok, "device_ms_per_step": [x / a.steps for x in rank_ms],
+                         "partition_imbalance": shard.imbalance(all_lengths, groups),
+                         "slowest_over_mean": max(rank_ms) / (sum(rank_ms) / len(rank_ms))}
 
     if rank == 0:
-        # attention-only C2 (second half of the metric): TFLOP/s vs the bf16 peak
-        from snapjudge_b200 import ops
-        lens2, q, k, v = synth.attention_inputs()
-        cu2 = synth.cu_seqlens(lens2)
-        T2, H2, Dh2 = q.shape
-        qkv = torch.from_numpy(np.concatenate([q, k, v], 1).reshape(T2, -1)).to(dev).to(
-            torch.bfloat16)
-        fl = float(sum(4 * int(n) ** 2 * Dh2 * H2 for n in lens2))
-        flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # > L2 (126 MB)
-
-        def time_attn(x, cu_x, reps=20):
-            out = 0.0
-            with torch.cuda.stream(st):
-                for _ in range(5):
-                    ops.attn(x, cu_x, H2, Dh2)
-                for _ in range(reps):
-                    flush.zero_()
-                    a0 = torch.cuda.Event(enable_timing=True)
-                    a1 = torch.cuda.Event(enable_timing=True)
-                    a0.record(st)
-                    ops.attn(x, cu_x, H2, Dh2)
-                    a1.record(st)
-                    a1.synchronize()
-                    out += a0.elapsed_time(a1) / reps
-            return out
-
-        ams = time_attn(qkv, cu2)
-        # fixed-length variant: 64 sequences of exactly 512 tokens
-        cu512 = synth.cu_seqlens(np.full(64, 512))
-        qkv512 = torch.randn(int(cu512[-1]), 3 * H2 * Dh2, device=dev).to(torch.bfloat16)
-        ams512 = time_attn(qkv512, cu512)
-        fl512 = 64 * 4.0 * 512 * 512 * Dh2 * H2
-        # C4's attention shape: 32 sequences of 2048 tokens, 16 heads of 64 (compute-bound)
-        H4 = 16
-        cu2048 = synth.cu_seqlens(np.full(32, 2048))
-        qkv2048 = torch.randn(int(cu2048[-1]), 3 * H4 * Dh2, device=dev).to(torch.bfloat16)
-
-        def time_attn_h(x, cu_x, H, reps=10):
-            out = 0.0
-            with torch.cuda.stream(st):
-                for _ in range(3):
-                    ops.attn(x, cu_x, H, Dh2)
-                for _ in range(reps):
-                    flush.zero_()
-                    a0 = torch.cuda.Event(enable_timing=True)
-                    a1 = torch.cuda.Event(enable_timing=True)
-                    a0.record(st)
-                    ops.attn(x, cu_x, H, Dh2)
-                    a1.record(st)
-                    a1.synchronize()
-                    out += a0.elapsed_time(a1) / reps
-            return out
-
-        ams2048 = time_attn_h(qkv2048, cu2048, H4)
-        fl2048 = 32 * 4.0 * 2048 * 2048 * Dh2 * H4
-        burst = pk.get("bf16_tflops", FALLBACK["bf16_tflops"])
-        line["attention"] = {"config": "c2: 64 seqs x 12 heads x 64, lengths U[32,512], bf16",
-                             "ms": ams, "tflops": fl / (ams / 1e3) / 1e12,
-                             "frac_of_peak": fl / (ams / 1e3) / 1e12 / burst,
-                             "peak": burst, "peak_kind": f"{pk_kind} burst bf16",
-                             "n512": {"ms": ams512, "tflops": fl512 / (ams512 / 1e3) / 1e12,
-                                      "frac_of_peak": fl512 / (ams512 / 1e3) / 1e12 / burst},
-                             "n2048_c4": {"config": "32 seqs x 2048 tokens, 16 heads x 64",
-                                          "ms": ams2048,
-                                          "tflops": fl2048 / (ams2048 / 1e3) / 1e12,
-                                          "frac_of_peak": fl2048 / (ams2048 / 1e3) / 1e12 / burst},
-                             "l2": "L2 flushed (256 MB write) before every timed launch"}
+        line["attention"] = attention_section(st, dev, pk, pk_kind)
         if world == 1 and not a.no_fp8:
             line["fp8"] = fp8_section(spec, weights, a, local, st, pass_args, probs_d, T, value)
         if world == 1 and not a.no_cpu_baseline:
             tok, sec, n, kind, cores = reference_sample(spec, weights, a.cpu_seconds, 8, 4096,
-                                                        seed=spec.seed + 40000)
+                                                        seed=spec.seed + 40000, batch=1)
+            tb, sb, nb, _, _ = reference_sample(spec, weights, a.cpu_seconds / 2, 16, 4096,
+                                                seed=spec.seed + 45000, batch=16)
             line["cpu_baseline"] = {"value": tok / sec, "unit": "tokens/s", "cores": cores,
-                                    "kind": kind,
-                                    "sample": f"{n} c5 requests ({tok} tokens), one request per "
-                                              f"encode call, {sec:.1f} s"}
+                                    "kind": kind, "cpu_model": cpu_model(),
+                                    "sample": f"{n} c5 requests ({tok} tokens), one request "
+                                              f"per encode call, {sec:.1f} s",
+                                    "batched": {"value": tb / sb, "unit": "tokens/s",
+                                                "sample": f"{nb} c5 requests ({tb} tokens), 16 "
+                                                          f"per encode call right-padded as "
+                                                          f"Agent::predict_batch collates, "
+                                                          f"{sb:.1f} s"}}
         print(json.dumps(line), flush=True)
     if dist:
         dist.barrier()
         dist.destroy_process_group()
     eng.close()
     return 0
+
+
+def attention_section(st, dev, pk, pk_kind):
+    """Attention-only figures (the second half of the metric): C2, 64 x 512
+    tokens and C4's 32 x 2048 tokens, TFLOP/s against the burst bf16 peak,
+    L2 flushed before every timed launch."""
+    import torch
+    from snapjudge_b200 import ops
+    lens2, q, k, v = synth.attention_inputs()
+    cu2 = synth.cu_seqlens(lens2)
+    T2, H2, Dh2 = q.shape
+    qkv = torch.from_numpy(np.concatenate([q, k, v], 1).reshape(T2, -1)).to(dev).to(
+        torch.bfloat16)
+    fl = float(sum(4 * int(n) ** 2 * Dh2 * H2 for n in lens2))
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # > L2 (126 MB)
+
+    def time_attn(x, cu_x, H, reps):
+        out = 0.0
+        with torch.cuda.stream(st):
+            for _ in range(3):
+                ops.attn(x, cu_x, H, Dh2)
+            for _ in range(reps):
+                flush.zero_()
+                a0 = torch.cuda.Event(enable_timing=True)
+                a1 = torch.cuda.Event(enable_timing=True)
+                a0.record(st)
+                ops.attn(x, cu_x, H, Dh2)
+                a1.record(st)
+                a1.synchronize()
+                out += a0.elapsed_time(a1) / reps
+        return out
+
+    ams = time_attn(qkv, cu2, H2, 20)
+    # fixed-length variant: 64 sequences of exactly 512 tokens
+    cu512 = synth.cu_seqlens(np.full(64, 512))
+    qkv512 = torch.randn(int(cu512[-1]), 3 * H2 * Dh2, device=dev).to(torch.bfloat16)
+    ams512 = time_attn(qkv512, cu512, H2, 20)
+    fl512 = 64 * 4.0 * 512 * 512 * Dh2 * H2
+    # C4's attention shape: 32 sequences of 2048 tokens, 16 heads of 64 (compute-bound)
+    H4 = 16
+    cu2048 = synth.cu_seqlens(np.full(32, 2048))
+    qkv2048 = torch.randn(int(cu2048[-1]), 3 * H4 * Dh2, device=dev).to(torch.bfloat16)
+    ams2048 = time_attn(qkv2048, cu2048, H4, 10)
+    fl2048 = 32 * 4.0 * 2048 * 2048 * Dh2 * H4
+    burst = pk.get("bf16_tflops", FALLBACK["bf16_tflops"])
+
+    def fig(f, t):
+        return {"ms": t, "tflops": f / (t / 1e3) / 1e12, "frac_of_peak": f / (t / 1e3) / 1e12 / burst}
+
+    return dict(config="c2: 64 seqs x 12 heads x 64, lengths U[32,512], bf16", **fig(fl, ams),
+                peak=burst, peak_kind=f"{pk_kind} burst bf16",
+                n512=dict(config="64 seqs x 512 tokens, 12 heads x 64", **fig(fl512, ams512)),
+                n2048_c4=dict(config="32 seqs x 2048 tokens, 16 heads x 64",
+                              **fig(fl2048, ams2048)),
+                l2="L2 flushed (256 MB write) before every timed launch")
 
 
 def fp8_section(spec, weights, a, local, st, pass_args, probs_d, T, value_bf16):

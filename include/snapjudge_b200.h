@@ -105,6 +105,28 @@ int sj_attn_noalloc(const sj_bf16* qkv, const int32_t* cu_seqlens, const int32_t
                     const int32_t* kv_lens, sj_bf16* O, int B, int H, int Dh, int window,
                     void* stream);
 
+/* Status of the kernel entry points above on the current device.  They are
+ * asynchronous and return once their kernels are queued, so a failure inside
+ * a kernel cannot be their return value: a bounded device-side wait that ran
+ * out (the kernel stops issuing, waits for its own copies, frees its
+ * resources and returns early, leaving its output incomplete) is recorded in
+ * a status word of the library, one per device, shared by every call of
+ * sj_gemm, sj_gemm_geglu, sj_attn, sj_attn_noalloc and sj_gemm_e4m3.  This
+ * call waits for `stream`, returns SJ_ERR_TIMEOUT (message in sj_last_error)
+ * if any of those calls recorded one since the last check, and clears the
+ * word.  Call it where the reference would check cudaGetLastError after a
+ * synchronisation (src/capi.cpp:89-93 reports failures the same way: a status
+ * and a message).  The engine (sj_fast_*) keeps its own flags and reports in
+ * sj_fast_sync and its synchronous calls. */
+int sj_check_device_errors(void* stream);
+
+/* Failure-detection test hook (no counterpart in the reference): while
+ * enabled (enable != 0), tcgen05 attention launches in this process issue no
+ * TMA load, so their first bounded wait (about 2 s) runs out with nothing in
+ * flight; the kernel records SJ_ERR_TIMEOUT's code and returns.  For tests of
+ * the timeout path only; disable it afterwards. */
+void sj_test_attn_wait_timeout(int enable);
+
 /* The FP8 variant's two kernels (no counterpart in the reference, which has
  * no FP8 path; SJ_PREC_FP8 runs them inside the engine).
  *

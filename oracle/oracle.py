@@ -28,9 +28,28 @@ _I64 = C.POINTER(C.c_int64)
 _U8 = C.POINTER(C.c_uint8)
 
 
+def reference_tree() -> str | None:
+    """The snapjudge reference checkout the _ref checkers compile from:
+    $SNAPJUDGE_REFERENCE, else a directory named "reference" beside this
+    repository; None when neither holds src/model.cpp."""
+    cands = [os.environ.get("SNAPJUDGE_REFERENCE"),
+             os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")]
+    for c in cands:
+        if c and os.path.exists(os.path.join(c, "src", "model.cpp")):
+            return c
+    return None
+
+
 def build() -> None:
     """Build the checkers (make; the _ref part only where the reference tree exists)."""
-    subprocess.run(["make", "-s", "-C", HERE, "all"], check=True)
+    args = ["make", "-s", "-C", HERE, "all"]
+    ref = reference_tree()
+    if ref:
+        args.append(f"REF={ref}")
+    blas = find_openblas()
+    if blas:
+        args.append(f"OPENBLAS={blas}")
+    subprocess.run(args, check=True)
 
 
 def _fp(a):
@@ -112,11 +131,18 @@ def set_blas(path: str | None = None) -> bool:
 
 
 def find_openblas() -> str | None:
+    """The OpenBLAS the reference is timed with: $SNAPJUDGE_OPENBLAS, else the
+    copy bundled with opencv-python-headless in this interpreter's
+    site-packages (OpenBLAS 0.3.15, which exports cblas_sgemm)."""
     import glob
-    pats = ["/opt/prime-rl/.venv/lib/python3.12/site-packages/opencv_python_headless.libs/"
-            "libopenblasp-r0-*.so"]
-    for p in pats:
-        g = sorted(glob.glob(p))
+    import site
+    env = os.environ.get("SNAPJUDGE_OPENBLAS")
+    if env and os.path.exists(env):
+        return env
+    dirs = list(site.getsitepackages()) + [site.getusersitepackages()]
+    for d in dirs:
+        g = sorted(glob.glob(os.path.join(d, "opencv_python_headless.libs",
+                                          "libopenblasp-r0-*.so")))
         if g:
             return g[0]
     return None

@@ -26,7 +26,8 @@ SJ_ARCH_SJMODEL = 1
 
 # every symbol declared in include/snapjudge_b200.h
 EXPORTS = ["sj_b200_version", "sj_last_error", "sj_gemm", "sj_gemm_geglu", "sj_add_ln", "sj_rope",
-           "sj_attn", "sj_attn_noalloc", "sj_quant_e4m3", "sj_gemm_e4m3", "sj_fast_create", "sj_fast_set_tensor", "sj_fast_set_heads",
+           "sj_attn", "sj_attn_noalloc", "sj_check_device_errors", "sj_test_attn_wait_timeout",
+           "sj_quant_e4m3", "sj_gemm_e4m3", "sj_fast_create", "sj_fast_set_tensor", "sj_fast_set_heads",
            "sj_fast_commit", "sj_fast_encode", "sj_fast_embed", "sj_fast_decide", "sj_fast_forward", "sj_fast_n_act",
            "sj_fast_encode_device",
            "sj_fast_sync", "sj_fast_launch_count", "sj_fast_set_profiling", "sj_fast_profile",
@@ -73,6 +74,9 @@ def lib() -> C.CDLL:
         L.sj_rope.argtypes = [_P, _P, _P, _P, _P, _I, _I, _I, _P]
         L.sj_attn.argtypes = [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P]
         L.sj_attn_noalloc.argtypes = [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P]
+        L.sj_check_device_errors.argtypes = [_P]
+        L.sj_test_attn_wait_timeout.argtypes = [_I]
+        L.sj_test_attn_wait_timeout.restype = None
         L.sj_quant_e4m3.argtypes = [_P, C.c_int64, _I, _P, _P, _P]
         L.sj_gemm_e4m3.argtypes = [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P]
         L.sj_fast_create.argtypes = [C.POINTER(FastConfig), C.POINTER(_P)]

@@ -20,7 +20,11 @@
 //    before any stream capture;
 //  * every call writes the whole schedule it uses (nothing carries over), but
 //    calls share the one array: calls whose launches overlap on the GPU (two
-//    streams, two host threads) race on it — serialise them.
+//    streams, two host threads) race on it — serialise them;
+//  * failures inside the kernels (a bounded wait that ran out, device
+//    cu_seqlens that disagree with the host mirror) are reported by
+//    sj_check_device_errors, which reads file-scope status words: that check
+//    allocates nothing either.
 #include <mutex>
 #include <string>
 
@@ -36,20 +40,40 @@ constexpr int kBuckets = 256;  // sequences bucketed by their tile count (capped
 
 // The schedule scratch: (segment, first query row) per tile.
 static __device__ __align__(256) int2 g_sched_scratch[kSchedMax];
+// Set by build_schedule when the device cu_seqlens give another tile count
+// than the host mirror did (read and cleared by sj_check_device_errors).
+static __device__ int g_sched_err;
 
 // Longest-first query-tile schedule of B segments, built by one block:
 // tiles of segments with more tiles come first (bucketed counting sort).
+// n_tiles (<= kSchedMax) is the count the host found in its mirror of cu; the
+// kernel writes exactly entries [0, n_tiles).  If the device array disagrees,
+// every entry becomes an idle tile (first row past any segment, which the
+// attention kernel skips), g_sched_err is set and nothing past n_tiles is
+// written.
 __global__ void __launch_bounds__(1024) build_schedule(const int32_t* __restrict__ cu, int B,
-                                                       int qt, int2* __restrict__ sched) {
+                                                       int qt, int n_tiles,
+                                                       int2* __restrict__ sched) {
   __shared__ int count[kBuckets];
   __shared__ int cursor[kBuckets];
+  __shared__ int total;
   for (int i = threadIdx.x; i < kBuckets; i += blockDim.x) count[i] = 0;
+  if (threadIdx.x == 0) total = 0;
   __syncthreads();
   for (int b = threadIdx.x; b < B; b += blockDim.x) {
-    const int nt = (cu[b + 1] - cu[b] + qt - 1) / qt;
-    if (nt > 0) atomicAdd(&count[min(nt, kBuckets - 1)], nt);
+    const int n = cu[b + 1] - cu[b];
+    const int nt = n > 0 ? (n + qt - 1) / qt : 0;
+    if (nt > 0) {
+      atomicAdd(&count[min(nt, kBuckets - 1)], nt);
+      atomicAdd(&total, nt);
+    }
   }
   __syncthreads();
+  if (total != n_tiles) {  // device cu_seqlens differ from the host mirror
+    for (int t = threadIdx.x; t < n_tiles; t += blockDim.x) sched[t] = make_int2(0, 0x3fffffff);
+    if (threadIdx.x == 0) g_sched_err = 1;
+    return;
+  }
   if (threadIdx.x == 0) {  // bucket start offsets, most tiles first
     int off = 0;
     for (int k = kBuckets - 1; k >= 1; --k) {
@@ -60,10 +84,10 @@ __global__ void __launch_bounds__(1024) build_schedule(const int32_t* __restrict
   __syncthreads();
   for (int b = threadIdx.x; b < B; b += blockDim.x) {
     const int n = cu[b + 1] - cu[b];
-    const int nt = (n + qt - 1) / qt;
+    const int nt = n > 0 ? (n + qt - 1) / qt : 0;
     if (nt == 0) continue;
     const int at = atomicAdd(&cursor[min(nt, kBuckets - 1)], nt);
-    for (int t = 0; t < nt; ++t) sched[at + t] = make_int2(b, t * qt);
+    for (int t = 0; t < nt && at + t < n_tiles; ++t) sched[at + t] = make_int2(b, t * qt);
   }
 }
 
@@ -76,6 +100,18 @@ int fail(int code, const std::string& m) {
 }
 
 }  // namespace
+
+cudaError_t attn_noalloc_take_status(int* code) {
+  int v = 0;
+  cudaError_t rc = cudaMemcpyFromSymbol(&v, g_sched_err, sizeof(int));
+  if (rc == cudaSuccess && v != 0) {
+    const int zero = 0;
+    rc = cudaMemcpyToSymbol(g_sched_err, &zero, sizeof(int));
+  }
+  *code = v;
+  return rc;
+}
+
 }  // namespace sjb
 
 extern "C" {
@@ -106,8 +142,12 @@ int sj_attn_noalloc(const sj_bf16* qkv, const int32_t* cu_seqlens, const int32_t
   if (!qkv || !O || !cu_seqlens) return fail(SJ_ERR_INVALID, "null attention operand");
   int dev = 0;
   cudaError_t rc = cudaGetDevice(&dev);
-  if (rc != cudaSuccess || dev < 0 || dev >= 64)
+  if (rc != cudaSuccess)
     return fail(SJ_ERR_CUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(rc));
+  if (dev < 0 || dev >= 64)
+    return fail(SJ_ERR_UNSUPPORTED, "sj_attn_noalloc: device ordinal " + std::to_string(dev) +
+                                        " >= 64 (the library keeps the array's address for "
+                                        "ordinals 0-63)");
   int2* sched = nullptr;
   {
     std::lock_guard<std::mutex> lk(g_mu);
@@ -121,7 +161,7 @@ int sj_attn_noalloc(const sj_bf16* qkv, const int32_t* cu_seqlens, const int32_t
     sched = g_sched_ptr[dev];
   }
   auto st = static_cast<cudaStream_t>(stream);
-  build_schedule<<<1, 1024, 0, st>>>(cu_seqlens, B, qt, sched);
+  build_schedule<<<1, 1024, 0, st>>>(cu_seqlens, B, qt, (int)tiles, sched);
   if ((rc = cudaGetLastError()) != cudaSuccess)
     return fail(SJ_ERR_CUDA, std::string("build_schedule: ") + cudaGetErrorString(rc));
   const bf16* q = reinterpret_cast<const bf16*>(qkv);

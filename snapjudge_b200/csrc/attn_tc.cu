@@ -35,6 +35,7 @@
 // mbarrier wait is bounded; a failed wait is carried to the next block-wide
 // barrier (__syncthreads_or), where all threads leave together (no trap).
 #include <algorithm>
+#include <atomic>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -206,7 +207,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     attn_tc_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapKV,
                    const int32_t* __restrict__ cu, const int32_t* __restrict__ kv_lens,
                    bf16* __restrict__ O, int H, int window, const int2* __restrict__ tiles,
-                   int n_items, int nqt, int* err) {
+                   int n_items, int nqt, int* err, int inject) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t q_full, kv_full[KV_STAGES], s_full, pv_done, drain;
   __shared__ Item items[2][CHUNK];  // this CTA's work items, chunk c in items[c & 1]
@@ -372,7 +373,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         for (int q = 0; q < 8; ++q) reinterpret_cast<uint4*>(orow)[q] = make_uint4(0, 0, 0, 0);
       continue;
     }
-    if (loader && !fail) {
+    // (inject: the failure-detection test's launch issues no load, so the
+    // first wait below runs out with nothing in flight)
+    if (loader && !fail && !inject) {
       if (q_item != k) issue_q(k);
       if (lk < k) {  // items lk..k-1 had no tiles (their buffer may be reused)
         lk = k;
@@ -572,16 +575,28 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 
 bool attn_tc_supported(int Dh) { return Dh == DH; }
 
+namespace {
+std::atomic<int> g_inject_timeout{0};
+}
+
+void attn_tc_inject_wait_timeout(bool enable) { g_inject_timeout.store(enable ? 1 : 0); }
+
+cudaError_t attn_tc_take_status(int* code) {
+  int v = 0;
+  cudaError_t rc = cudaMemcpyFromSymbol(&v, g_attn_tc_err, sizeof(int));
+  if (rc == cudaSuccess && v != 0) {
+    const int zero = 0;
+    rc = cudaMemcpyToSymbol(g_attn_tc_err, &zero, sizeof(int));
+  }
+  *code = v;
+  return rc;
+}
+
 cudaError_t attn_tc(const bf16* qkv, const int32_t* cu, const int32_t* kv_lens, bf16* O, int T,
                     int H, int window, const int2* tiles, int n_tiles, int B, int max_seqlen,
                     int* err, cudaStream_t st) {
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t rc = cudaFuncSetAttribute(attn_tc_kernel,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    if (rc != cudaSuccess) return rc;
-    attr_set = true;
-  }
+  static std::atomic<uint64_t> attr_done{0};  // per device ordinal
+  if (cudaError_t rc = ensure_smem_attr(attn_tc_kernel, SMEM_BYTES, attr_done)) return rc;
   if (T <= 0) return cudaSuccess;
   CUtensorMap mq, mkv;
   const uint64_t cols = 3ull * H * DH;
@@ -594,7 +609,8 @@ cudaError_t attn_tc(const bf16* qkv, const int32_t* cu, const int32_t* kv_lens, 
   if (items > 0x7fffffff) return cudaErrorInvalidValue;
   const int grid = (int)std::min<long long>(items, (long long)kCtasPerSm * sm_count());
   attn_tc_kernel<<<grid, kThreads, SMEM_BYTES, st>>>(mq, mkv, cu, kv_lens, O, H, window, tiles,
-                                                      (int)items, nqt, err);
+                                                      (int)items, nqt, err,
+                                                      g_inject_timeout.load());
   return cudaGetLastError();
 }
 

@@ -132,6 +132,29 @@ int sj_attn(const sj_bf16* qkv, const int32_t* cu_seqlens, const int32_t* cu_seq
                   "attn_simt");
 }
 
+int sj_check_device_errors(void* stream) {
+  auto st = static_cast<cudaStream_t>(stream);
+  cudaError_t rc = cudaStreamSynchronize(st);
+  if (rc != cudaSuccess) return launched(rc, "cudaStreamSynchronize");
+  int a = 0, g = 0, sc = 0;
+  if ((rc = sjb::attn_tc_take_status(&a)) != cudaSuccess) return launched(rc, "attention status");
+  if ((rc = sjb::gemm_tc_take_status(&g)) != cudaSuccess) return launched(rc, "GEMM status");
+  if ((rc = sjb::attn_noalloc_take_status(&sc)) != cudaSuccess)
+    return launched(rc, "schedule status");
+  if (sc)
+    return fail(SJ_ERR_INVALID, "sj_attn_noalloc: the device cu_seqlens disagree with "
+                                "cu_seqlens_host; the schedule was left idle and O not written");
+  if (a || g)
+    return fail(SJ_ERR_TIMEOUT, std::string("a bounded device wait ran out in the ") +
+                                    (a ? "attention" : "GEMM") + " kernel (code " +
+                                    std::to_string(a ? a : g) +
+                                    "); the outputs of the calls since the last check are "
+                                    "incomplete");
+  return SJ_OK;
+}
+
+void sj_test_attn_wait_timeout(int enable) { sjb::attn_tc_inject_wait_timeout(enable != 0); }
+
 int sj_quant_e4m3(const float* x, int64_t rows, int cols, uint8_t* q, float* scale,
                   void* stream) {
   if (rows < 0 || cols <= 0 || cols % 4 != 0)

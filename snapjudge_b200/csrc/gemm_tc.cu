@@ -27,6 +27,7 @@
 // (mbar_wait<true>: waiters that re-issue try_wait slow the MMA issue); a
 // wait that runs out records an error code and the CTA winds down (no trap).
 #include <algorithm>
+#include <atomic>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -734,13 +735,9 @@ cudaError_t launch(const void* A, const void* W, int M, int N_out, int K, int w_
   constexpr int STAGES = stages_for<BN, EPI, PAIR>();
   constexpr int BROWS = PAIR ? BN / 2 : BN;
   constexpr int SMEM = STAGES * (BM * BK * 2 + BROWS * BK * 2) + out_bytes<BN, EPI>() + 1024;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t rc = cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI, PAIR, F8>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
-    if (rc != cudaSuccess) return rc;
-    attr_set = true;
-  }
+  static std::atomic<uint64_t> attr_done{0};  // per device ordinal
+  if (cudaError_t rc = ensure_smem_attr(gemm_tc_kernel<BN, EPI, PAIR, F8>, SMEM, attr_done))
+    return rc;
   CUtensorMap ma, mb, mc;
   const int b_box = PAIR ? BROWS : (EPI == TC_GEGLU ? BN / 2 : BN);
   if (F8) {
@@ -837,6 +834,17 @@ cudaError_t gemm_tc(const bf16* A, const bf16* W, const float* bias, bf16* C, fl
     case TC_ROPE: return dispatch_bn<TC_ROPE>(A, W, M, N, K, N, ep, st);
   }
   return cudaErrorInvalidValue;
+}
+
+cudaError_t gemm_tc_take_status(int* code) {
+  int v = 0;
+  cudaError_t rc = cudaMemcpyFromSymbol(&v, g_gemm_tc_err, sizeof(int));
+  if (rc == cudaSuccess && v != 0) {
+    const int zero = 0;
+    rc = cudaMemcpyToSymbol(g_gemm_tc_err, &zero, sizeof(int));
+  }
+  *code = v;
+  return rc;
 }
 
 bool gemm_tc_f8_supported(int M, int N, int K, int epi) {

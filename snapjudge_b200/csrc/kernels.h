@@ -120,6 +120,8 @@ cudaError_t gemm_tc(const bf16* A, const bf16* W, const float* bias, bf16* C, fl
 // codes with a scale per A row (sa [M]) and per W row (sw [N_w], 16-byte
 // aligned); acc = sa[m] sw[n] sum_k A[m, k] W[n, k] in fp32, then the epilogue
 // as gemm_tc.  Epilogues TC_STORE, TC_GEGLU, TC_ROPE; K % 128 == 0.
+// As attn_tc_take_status, for the GEMM launches given no error flag.
+cudaError_t gemm_tc_take_status(int* code);
 bool gemm_tc_f8_supported(int M, int N, int K, int epi);
 cudaError_t gemm_tc_f8(const uint8_t* A, const uint8_t* W, const float* sa, const float* sw,
                        const float* bias, bf16* C, int M, int N, int K, int epi, int act,
@@ -138,6 +140,17 @@ cudaError_t ln_e4m3(const float* X, const float* w, const float* b, uint8_t* q, 
 
 // ---- tcgen05 flash attention (attn_tc.cu) -----------------------------------
 bool attn_tc_supported(int Dh);
+// Launches given no error flag (err == null) record a wait that ran out in a
+// status word of the library on their device.  *code = that word (0: none),
+// which is then cleared; synchronous, on the current device, allocates nothing.
+cudaError_t attn_tc_take_status(int* code);
+// Failure-detection test hook: while enabled, attention launches of this
+// process issue no TMA load, so their first bounded wait runs out (nothing is
+// in flight) and they record a timeout and return.
+void attn_tc_inject_wait_timeout(bool enable);
+// sj_attn_noalloc's schedule check: *code != 0 when a schedule build found
+// device cu_seqlens that disagree with the host mirror (then cleared).
+cudaError_t attn_noalloc_take_status(int* code);
 // tiles: list of (b, q0) query tiles of 128 rows (or null: B x ceil(max_seqlen/128)).
 cudaError_t attn_tc(const bf16* qkv, const int32_t* cu, const int32_t* kv_lens, bf16* O, int T,
                     int H, int window, const int2* tiles, int n_tiles, int B, int max_seqlen,

@@ -5,6 +5,7 @@
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <mutex>
 
 namespace sjb {
@@ -82,6 +83,22 @@ inline int sm_count() {
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
   return n > 0 ? n : 1;
+}
+
+// Raise a kernel's dynamic shared-memory limit to `bytes` on the current
+// device.  The attribute belongs to the device, so it is set once per device
+// ordinal (bit d of `done`); ordinals >= 64 set it on every call.  Safe from
+// several host threads: two threads that race both set the same value.
+template <typename Kernel>
+inline cudaError_t ensure_smem_attr(Kernel kernel, int bytes, std::atomic<uint64_t>& done) {
+  int dev = 0;
+  cudaError_t rc = cudaGetDevice(&dev);
+  if (rc != cudaSuccess) return rc;
+  const uint64_t bit = (dev >= 0 && dev < 64) ? (1ull << dev) : 0ull;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+  rc = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (rc == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_acq_rel);
+  return rc;
 }
 
 }  // namespace tc

@@ -125,7 +125,9 @@ def sjmodel_goldens() -> None:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=oracle.reference_tree(), required=oracle.reference_tree() is None,
+                    help="snapjudge reference checkout (default: $SNAPJUDGE_REFERENCE, else a "
+                         "'reference' directory beside this repository)")
     a = ap.parse_args()
     oracle.build()
     convert_tensor_ops(a.reference)

@@ -153,9 +153,13 @@ def test_c5_subset_vs_oracle():
     _subset_check(synth.SPECS["c5"], 24, 78)
 
 
-def test_c4_one_sequence_vs_oracle():
+def test_c4_full_length_vs_oracle():
+    """C4 at its full size per sequence: 24 layers x 1024, 16 heads, two
+    sequences of 2048 tokens (the config's fixed length) against the C
+    restatement, hidden states / logits / probabilities at the bf16 bars."""
     spec = synth.SPECS["c4"]
-    _subset_check(spec, 1, 79, max_len=1024)
+    eng, t, lengths, ids, hp = _subset_check(spec, 2, 79)
+    assert (lengths == 2048).all()
 
 
 def test_c3_full_batch_properties():
