@@ -1,0 +1,134 @@
+// agent_check.cpp — the reference runtime on the GPU fast path, on the
+// reference's own tiny checkpoint fixture.  TEST INFRASTRUCTURE ONLY (built by
+// oracle/Makefile into oracle/_ref/ from the reference's sources, with
+// src/agent.cpp carrying the two-line dispatch of INTEGRATION.md section 2,
+// and linked with snapjudge_b200/integration/fast.cpp).
+//
+// usage: agent_check <tiny checkpoint dir> <model_tiny.json>
+// 1. Agent(ckpt, "cpu").system_one equals the golden (the reference's own
+//    tests/test_model.cpp:29-45 check);
+// 2. Agent(ckpt, "cuda") runs FastSnapjudge (accelerated() is true) and its
+//    system_one matches the golden: the same keys, labels and token counts,
+//    numbers within $AGENT_CHECK_TOL (default 0: equal);
+// 3. the C API with {"device":"cuda"} (tests/capi/test_capi.c's call) answers
+//    with an "answers" object whose numbers match the same call on "cpu"
+//    within the tolerance.
+// Prints one JSON line; exit 0 when all hold.
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <fstream>
+#include <string>
+
+#include "nlohmann/json.hpp"
+#include "snapjudge/agent.hpp"
+#include "snapjudge/capi.h"
+
+using nlohmann::ordered_json;
+
+namespace {
+double g_tol = 0.0, g_max_diff = 0.0;
+std::string g_first_mismatch;
+
+void note(const std::string& where) {
+  if (g_first_mismatch.empty()) g_first_mismatch = where;
+}
+// structural equality; numbers within g_tol (largest difference recorded)
+void compare(const ordered_json& a, const ordered_json& b, const std::string& path) {
+  if (a.is_number() && b.is_number()) {
+    const double d = std::fabs(a.get<double>() - b.get<double>());
+    if (d > g_max_diff) g_max_diff = d;
+    if (d > g_tol) note(path + ": " + a.dump() + " vs " + b.dump());
+    return;
+  }
+  if (a.type() != b.type()) return note(path + ": type");
+  if (a.is_object()) {
+    if (a.size() != b.size()) return note(path + ": keys");
+    for (auto it = a.begin(); it != a.end(); ++it) {
+      if (!b.contains(it.key())) return note(path + "." + it.key() + ": missing");
+      compare(it.value(), b[it.key()], path + "." + it.key());
+    }
+    return;
+  }
+  if (a.is_array()) {
+    if (a.size() != b.size()) return note(path + ": length");
+    for (size_t i = 0; i < a.size(); ++i) compare(a[i], b[i], path + "[" + std::to_string(i) + "]");
+    return;
+  }
+  if (a != b) note(path + ": " + a.dump() + " vs " + b.dump());
+}
+}  // namespace
+
+int main(int argc, char** argv) {
+  if (argc < 3) return 2;
+  if (const char* t = std::getenv("AGENT_CHECK_TOL")) g_tol = std::atof(t);
+  const std::string ckpt = argv[1];
+  ordered_json gold;
+  std::ifstream(argv[2]) >> gold;
+  const ordered_json state = "the invoice was charged twice please fix";
+  const ordered_json qs = ordered_json{
+      {"urgent", {{"type", "noul"}, {"instructions", "Is this time-sensitive?"}}},
+      {"route", {{"type", "choice"}, {"instructions", "who handles this?"},
+                 {"criteria", ordered_json{{"billing", "money"}, {"tech", "broken"},
+                                           {"other", "rest"}}}}}};
+  ordered_json out;
+  // 1. reference CPU forward against its golden
+  snapjudge::Agent cpu(ckpt, "cpu");
+  out["cpu_equals_golden"] = cpu.system_one(state, qs) == gold["system_one"];
+  // 2. the same Agent on the GPU fast path
+  snapjudge::Agent gpu(ckpt, "cuda");
+  out["accelerated"] = gpu.accelerated();
+  ordered_json res = gpu.system_one(state, qs);
+  // a choice whose golden probabilities are tied within the tolerance may go
+  // either way (bf16 mode: the tiny checkpoint's three options sit within
+  // 1e-4 of each other); such a label is accepted and counted
+  int ties = 0;
+  for (auto& [qid, a] : res["answers"].items()) {
+    const auto& ga = gold["system_one"]["answers"][qid];
+    if (!a.contains("choice") || a["choice"] == ga["choice"]) continue;
+    const double pg = ga["probabilities"][ga["choice"].get<std::string>()].get<double>();
+    const double pr = ga["probabilities"][a["choice"].get<std::string>()].get<double>();
+    if (std::fabs(pg - pr) <= g_tol) {
+      a["choice"] = ga["choice"];
+      ++ties;
+    }
+  }
+  out["ties_accepted"] = ties;
+  compare(res, gold["system_one"], "system_one");
+  const double d_agent = g_max_diff;
+  const bool agent_ok = g_first_mismatch.empty();
+  out["agent_max_diff"] = d_agent;
+  out["agent_mismatch"] = g_first_mismatch;
+  // 3. the C API, cuda against cpu
+  const char* st = "{\"text\":\"I was charged twice, please refund\"}";
+  const char* q = "{\"q\":{\"type\":\"noul\",\"instructions\":\"Does the customer want money back?\"}}";
+  ordered_json capi[2];
+  bool capi_ok = true;
+  const char* opts[2] = {"{\"device\":\"cpu\"}", "{\"device\":\"cuda\"}"};
+  for (int i = 0; i < 2; ++i) {
+    sj_engine* e = sj_engine_new(opts[i]);
+    char* r = nullptr;
+    if (e && sj_load(e, "main", ckpt.c_str()) == 0) r = sj_predict(e, st, q, "");
+    if (!r) {
+      capi_ok = false;
+      out["capi_error"] = e && sj_error_message(e) ? sj_error_message(e) : "sj_predict failed";
+    } else {
+      capi[i] = ordered_json::parse(r);
+      sj_string_free(r);
+    }
+    if (e) sj_engine_free(e);
+  }
+  g_max_diff = 0.0;
+  g_first_mismatch.clear();
+  if (capi_ok) {
+    capi_ok = capi[1].contains("answers") && capi[1]["answers"].contains("q");
+    compare(capi[1], capi[0], "capi");
+    capi_ok = capi_ok && g_first_mismatch.empty();
+  }
+  out["capi_ok"] = capi_ok;
+  out["capi_max_diff"] = g_max_diff;
+  out["capi_mismatch"] = g_first_mismatch;
+  std::printf("%s\n", out.dump().c_str());
+  const bool ok = out["cpu_equals_golden"].get<bool>() && gpu.accelerated() && agent_ok && capi_ok;
+  return ok ? 0 : 1;
+}

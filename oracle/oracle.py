@@ -204,6 +204,46 @@ def attention(q, k, v, lens=None, window=0):
     return out
 
 
+def attention_packed_np(q, k, v, lengths, window=0, kv_lens=None, dtype=np.float64):
+    """attention_packed restated with matrix products (NumPy BLAS), for
+    segments too long for the scalar C loop: per (segment, head) the same
+    steps as src/tensor.cpp:156-228 — scores q.k / sqrt(Dh) over keys
+    [max(0, i - w), min(kv_len, i + w + 1)) (w = 0: [0, kv_len)), max
+    subtracted, exponentials summed, o = sum p v / sum p; no visible key
+    gives 0.  q/k/v [T, H, Dh]; returns float32 [T, H, Dh].  Pinned against
+    the C restatement in tests/test_oracle.py.  dtype float32 halves the time
+    of the largest cases (its error, ~1e-6 relative, is far below the bf16
+    bars it checks)."""
+    q = np.asarray(q, dtype)
+    k = np.asarray(k, dtype)
+    v = np.asarray(v, dtype)
+    T, H, Dh = q.shape
+    out = np.zeros((T, H, Dh), np.float32)
+    cu = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int64)
+    scale = 1.0 / np.sqrt(np.float32(Dh))
+    for b in range(len(lengths)):
+        s0, e = int(cu[b]), int(cu[b + 1])
+        n = e - s0
+        if n == 0:
+            continue
+        nk = n if kv_lens is None else min(int(kv_lens[b]), n)
+        if nk == 0:
+            continue
+        i = np.arange(n)[:, None]
+        j = np.arange(nk)[None, :]
+        vis = np.ones((n, nk), bool) if window <= 0 else (np.abs(i - j) <= window)
+        for h in range(H):
+            s = (q[s0:e, h] @ k[s0:s0 + nk, h].T) * scale
+            s = np.where(vis, s, -np.inf)
+            m = s.max(1, keepdims=True)
+            m = np.where(np.isfinite(m), m, 0.0)
+            p = np.where(vis, np.exp(s - m), 0.0)
+            lsum = p.sum(1, keepdims=True)
+            o = (p @ v[s0:s0 + nk, h]) / np.where(lsum > 0, lsum, 1.0)
+            out[s0:e, h] = o.astype(np.float32)
+    return out
+
+
 def attention_packed(q, k, v, lengths, window=0, kv_lens=None):
     """Packed varlen attention: q/k/v [T, H, Dh]; one segment per sequence."""
     out = np.empty_like(_f32(q))

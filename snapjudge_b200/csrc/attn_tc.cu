@@ -168,9 +168,12 @@ struct __align__(16) Item {
 };
 
 // Work item w: list form (tiles != null): tile w / H, head w % H; grid form:
-// w = ((b * nqt) + qtile) * H + h.  Idle grid-form items get n_kv = -1.
-__device__ __forceinline__ Item decode(int w, const int2* tiles, int H, int nqt,
-                                       const int32_t* cu, const int32_t* kv_lens, int window) {
+// w = ((nqt - 1 - qtile) * B + b) * H + h, the highest query tiles first: only
+// long segments have them, so without a schedule the longest work still goes
+// first (C2's mixed lengths: 91 -> ~75 us).  Idle grid-form items get n_kv = -1.
+__device__ __forceinline__ Item decode(int w, const int2* tiles, int H, int nqt, int B,
+                                       const int32_t* cu, const int32_t* kv_lens, int window,
+                                       int long_min) {
   Item it;
   it.h = w % H;
   const int rest = w / H;
@@ -180,13 +183,13 @@ __device__ __forceinline__ Item decode(int w, const int2* tiles, int H, int nqt,
     b = t.x;
     it.q0 = t.y;
   } else {
-    b = rest / nqt;
-    it.q0 = (rest % nqt) * QT;
+    b = rest % B;
+    it.q0 = (nqt - 1 - rest / B) * QT;
   }
   it.s0 = cu[b];
   it.n = cu[b + 1] - it.s0;
   it.pad = 0;
-  if (it.q0 >= it.n) {
+  if (it.q0 >= it.n || (!tiles && it.n >= long_min)) {
     it.nk = it.t_lo = 0;
     it.n_kv = -1;
     return it;
@@ -207,7 +210,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     attn_tc_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapKV,
                    const int32_t* __restrict__ cu, const int32_t* __restrict__ kv_lens,
                    bf16* __restrict__ O, int H, int window, const int2* __restrict__ tiles,
-                   int n_items, int nqt, int* err, int inject) {
+                   int n_items, int nqt, int B, int* err, int inject, int long_min) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t q_full, kv_full[KV_STAGES], s_full, pv_done, drain;
   __shared__ Item items[2][CHUNK];  // this CTA's work items, chunk c in items[c & 1]
@@ -226,8 +229,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   auto decode_chunk = [&](int c) {
     const int k = c * CHUNK + tid;
     if (tid < CHUNK && k < cnt)
-      items[c & 1][tid] = decode((int)blockIdx.x + k * (int)gridDim.x, tiles, H, nqt, cu, kv_lens,
-                                 window);
+      items[c & 1][tid] = decode((int)blockIdx.x + k * (int)gridDim.x, tiles, H, nqt, B, cu,
+                                 kv_lens, window, long_min);
   };
 
   if (leader) {
@@ -594,7 +597,7 @@ cudaError_t attn_tc_take_status(int* code) {
 
 cudaError_t attn_tc(const bf16* qkv, const int32_t* cu, const int32_t* kv_lens, bf16* O, int T,
                     int H, int window, const int2* tiles, int n_tiles, int B, int max_seqlen,
-                    int* err, cudaStream_t st) {
+                    int* err, cudaStream_t st, int long_min) {
   static std::atomic<uint64_t> attr_done{0};  // per device ordinal
   if (cudaError_t rc = ensure_smem_attr(attn_tc_kernel, SMEM_BYTES, attr_done)) return rc;
   if (T <= 0) return cudaSuccess;
@@ -609,8 +612,8 @@ cudaError_t attn_tc(const bf16* qkv, const int32_t* cu, const int32_t* kv_lens, 
   if (items > 0x7fffffff) return cudaErrorInvalidValue;
   const int grid = (int)std::min<long long>(items, (long long)kCtasPerSm * sm_count());
   attn_tc_kernel<<<grid, kThreads, SMEM_BYTES, st>>>(mq, mkv, cu, kv_lens, O, H, window, tiles,
-                                                      (int)items, nqt, err,
-                                                      g_inject_timeout.load());
+                                                      (int)items, nqt, B, err,
+                                                      g_inject_timeout.load(), long_min);
   return cudaGetLastError();
 }
 

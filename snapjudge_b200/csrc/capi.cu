@@ -25,18 +25,20 @@ int launched(cudaError_t rc, const char* what) {
   g_err = std::string("snapjudge CUDA: ") + what + ": " + cudaGetErrorString(rc);
   return SJ_ERR_CUDA;
 }
-int check_cu(const int32_t* cu_host, int B, int* T, int* max_len) {
+int check_cu(const int32_t* cu_host, int B, int* T, int* max_len, int* min_len = nullptr) {
   if (!cu_host) return fail(SJ_ERR_INVALID, "cu_seqlens_host is null");
   if (B < 0) return fail(SJ_ERR_INVALID, "negative batch");
   if (B > 0 && cu_host[0] != 0) return fail(SJ_ERR_INVALID, "cu_seqlens[0] must be 0");
-  int ml = 0;
+  int ml = 0, mn = 0x7fffffff;
   for (int b = 0; b < B; ++b) {
     int n = cu_host[b + 1] - cu_host[b];
     if (n < 0) return fail(SJ_ERR_INVALID, "cu_seqlens must be non-decreasing");
     ml = n > ml ? n : ml;
+    mn = n < mn ? n : mn;
   }
   *T = B > 0 ? cu_host[B] : 0;
   *max_len = ml;
+  if (min_len) *min_len = mn;
   return SJ_OK;
 }
 }  // namespace
@@ -113,18 +115,29 @@ int sj_rope(sj_bf16* qkv, const float* cos_t, const float* sin_t, const int32_t*
 
 int sj_attn(const sj_bf16* qkv, const int32_t* cu_seqlens, const int32_t* cu_seqlens_host,
             const int32_t* kv_lens, sj_bf16* O, int B, int H, int Dh, int window, void* stream) {
-  int T = 0, ml = 0, s;
-  if ((s = check_cu(cu_seqlens_host, B, &T, &ml))) return s;
+  int T = 0, ml = 0, mn = 0, s;
+  if ((s = check_cu(cu_seqlens_host, B, &T, &ml, &mn))) return s;
   if (H <= 0 || window < 0) return fail(SJ_ERR_INVALID, "bad attention shape");
   if (T && (!qkv || !O || !cu_seqlens)) return fail(SJ_ERR_INVALID, "null attention operand");
   if (T == 0) return SJ_OK;
   auto st = static_cast<cudaStream_t>(stream);
   const bf16* q = reinterpret_cast<const bf16*>(qkv);
   bf16* o = reinterpret_cast<bf16*>(O);
-  if (sjb::attn_tc_supported(Dh))
+  if (sjb::attn_tc_supported(Dh)) {
+    // full attention: segments of kAttnLongMin tokens or more on the long-segment kernel
+    const bool split = window == 0 && ml >= sjb::kAttnLongMin &&
+                       sjb::attn_long_pays(cu_seqlens_host, B);
+    if (split) {
+      const int rc = launched(sjb::attn_long(q, cu_seqlens, kv_lens, o, T, H, nullptr, 0, B, ml,
+                                             nullptr, st),
+                              "attn_long");
+      if (rc != SJ_OK) return rc;
+      if (mn >= sjb::kAttnLongMin) return SJ_OK;  // no short segment left
+    }
     return launched(sjb::attn_tc(q, cu_seqlens, kv_lens, o, T, H, window, nullptr, 0, B, ml,
-                                 nullptr, st),
+                                 nullptr, st, split ? sjb::kAttnLongMin : 0x7fffffff),
                     "attn_tc");
+  }
   if (Dh != 8 && Dh != 16 && Dh != 32 && Dh != 64 && Dh != 128)
     return fail(SJ_ERR_UNSUPPORTED, "head_dim must be 8, 16, 32, 64 or 128");
   return launched(sjb::attn_simt<bf16>(q, cu_seqlens, kv_lens, o, H, Dh, window, nullptr, 0, B, ml,
@@ -136,8 +149,11 @@ int sj_check_device_errors(void* stream) {
   auto st = static_cast<cudaStream_t>(stream);
   cudaError_t rc = cudaStreamSynchronize(st);
   if (rc != cudaSuccess) return launched(rc, "cudaStreamSynchronize");
-  int a = 0, g = 0, sc = 0;
+  int a = 0, g = 0, sc = 0, al = 0;
   if ((rc = sjb::attn_tc_take_status(&a)) != cudaSuccess) return launched(rc, "attention status");
+  if ((rc = sjb::attn_long_take_status(&al)) != cudaSuccess)
+    return launched(rc, "attention status");
+  if (!a) a = al;
   if ((rc = sjb::gemm_tc_take_status(&g)) != cudaSuccess) return launched(rc, "GEMM status");
   if ((rc = sjb::attn_noalloc_take_status(&sc)) != cudaSuccess)
     return launched(rc, "schedule status");

@@ -463,7 +463,9 @@ int sj_fast::commit() {
   }
   // workspace
   const size_t T = (size_t)max_tokens, es = bf16_mode ? 2 : 4;
-  max_tiles = max_tokens / 64 + max_tokens + 1;
+  // 128-row (or 64-row) query tiles of every segment, then the 256-row items
+  // of the long-segment attention
+  max_tiles = max_tokens / 64 + max_tokens + 1 + max_tokens / 256 + max_tokens / sjb::kAttnLongMin + 1;
   if ((rc = dalloc(&X, T * D)) || (rc = dalloc((char**)&Y, T * D * es)) ||
       (rc = dalloc((char**)&QKV, T * 3 * D * es)) || (rc = dalloc((char**)&O, T * D * es)) ||
       (rc = dalloc((char**)&G, T * (hlayers.empty() ? F : std::max(F, head_ffn)) * es)) ||
@@ -623,16 +625,34 @@ int sj_fast::forward(const int64_t* d_ids, const int32_t* d_cu, const int32_t* h
   std::stable_sort(order.begin(), order.end(), [&](int a, int b) {
     return hcu[a + 1] - hcu[a] > hcu[b + 1] - hcu[b];
   });
-  int nt = 0;
+  // h_tiles = [query tiles of every segment, longest first: those of the
+  // segments of kAttnLongMin tokens or more (n_long_tiles) come first]
+  //           [256-row items of those long segments (n_pairs)]
+  // Full-attention layers at head_dim 64 run the long items on attn_long and
+  // the remaining tiles on attn_tc; windowed layers run every tile on attn_tc.
+  int nt = 0, n_long_tiles = 0, n_pairs = 0;
+  const bool split = tc_attn && sjb::attn_long_pays(hcu, B);
   for (int b : order) {
     const int n = hcu[b + 1] - hcu[b];
     for (int q0 = 0; q0 < n; q0 += qt) {
       if (nt >= max_tiles) return fail(SJ_ERR_INVALID, "too many query tiles");
       h_tiles[nt++] = make_int2(b, q0);
     }
+    if (split && n >= sjb::kAttnLongMin) n_long_tiles = nt;
   }
-  if (nt > 0) {
-    rc = cudaMemcpyAsync(tiles, h_tiles, nt * sizeof(int2), cudaMemcpyHostToDevice, st);
+  if (n_long_tiles > 0) {
+    for (int b : order) {
+      const int n = hcu[b + 1] - hcu[b];
+      if (n < sjb::kAttnLongMin) break;
+      for (int q0 = 0; q0 < n; q0 += 256) {
+        if (nt + n_pairs >= max_tiles) return fail(SJ_ERR_INVALID, "too many query tiles");
+        h_tiles[nt + n_pairs++] = make_int2(b, q0);
+      }
+    }
+  }
+  if (nt + n_pairs > 0) {
+    rc = cudaMemcpyAsync(tiles, h_tiles, (nt + n_pairs) * sizeof(int2), cudaMemcpyHostToDevice,
+                         st);
     if (rc != cudaSuccess) return cuda_fail(rc, "cudaMemcpyAsync (tiles)");
   }
   if ((rc = cudaEventRecord(staged_ev, st))) return cuda_fail(rc, "cudaEventRecord");
@@ -690,9 +710,18 @@ int sj_fast::forward(const int64_t* d_ids, const int32_t* d_cu, const int32_t* h
       return s;
     }
     if (tc_attn) {
-      if constexpr (kBf16)
-        SJ_LAUNCH(SJ_K_ATTN, sjb::attn_tc(Qt, d_cu, d_kvl, Ot, ntok, H, ly.window, tiles, nt, B, 0, dflags + 2,
-                               st));
+      if constexpr (kBf16) {
+        if (ly.window == 0 && n_pairs > 0) {
+          SJ_LAUNCH(SJ_K_ATTN, sjb::attn_long(Qt, d_cu, d_kvl, Ot, ntok, H, tiles + nt, n_pairs, B,
+                                              0, dflags + 2, st));
+          if (nt > n_long_tiles)
+            SJ_LAUNCH(SJ_K_ATTN, sjb::attn_tc(Qt, d_cu, d_kvl, Ot, ntok, H, 0, tiles + n_long_tiles,
+                                              nt - n_long_tiles, B, 0, dflags + 2, st));
+        } else {
+          SJ_LAUNCH(SJ_K_ATTN, sjb::attn_tc(Qt, d_cu, d_kvl, Ot, ntok, H, ly.window, tiles, nt, B, 0,
+                                            dflags + 2, st));
+        }
+      }
     } else {
       SJ_LAUNCH(SJ_K_ATTN, sjb::attn_simt<T>(Qt, d_cu, d_kvl, Ot, H, Dh, ly.window, tiles, nt, B, 0, st));
     }
@@ -1008,7 +1037,12 @@ int sj_fast::dm_call(const int64_t* ids_h, const int32_t* cu_h, const int32_t* k
 extern "C" {
 
 int sj_fast_create(const sj_fast_config* cfg, sj_fast** out) {
-  if (!cfg || !out) return SJ_ERR_INVALID;
+  // failures leave their message in sj_last_error() (there is no engine yet)
+  auto bad = [](int code, const std::string& m) {
+    sjb::set_last_error("sj_fast_create: " + m);
+    return code;
+  };
+  if (!cfg || !out) return bad(SJ_ERR_INVALID, "null argument");
   *out = nullptr;
   std::unique_ptr<sj_fast> e(new sj_fast());
   e->cfg = *cfg;
@@ -1017,19 +1051,22 @@ int sj_fast_create(const sj_fast_config* cfg, sj_fast** out) {
       c.intermediate_size <= 0 || c.vocab_size <= 0 || c.max_position_embeddings <= 0 ||
       c.hidden_size % c.num_attention_heads != 0 ||
       (c.hidden_size / c.num_attention_heads) % 2 != 0)
-    return SJ_ERR_INVALID;
+    return bad(SJ_ERR_INVALID, "bad model shape (sizes must be positive, hidden_size a multiple "
+                               "of num_attention_heads, head_dim even)");
   if (c.precision != SJ_PREC_BF16 && c.precision != SJ_PREC_FP32 && c.precision != SJ_PREC_FP8)
-    return SJ_ERR_UNSUPPORTED;
+    return bad(SJ_ERR_UNSUPPORTED, "unknown precision");
   // the FP8 variant: the DecisionModel encoder, e4m3 GEMMs need K = D % 128 == 0,
   // the quantising LN D <= 1024, the attention head_dim 64 and N % 64 == 0
   if (c.precision == SJ_PREC_FP8 &&
       (c.arch != SJ_ARCH_MODERNBERT || c.hidden_size % 128 != 0 || c.hidden_size > 1024 ||
        c.hidden_size / c.num_attention_heads != 64 || c.intermediate_size % 64 != 0))
-    return SJ_ERR_UNSUPPORTED;
-  if (c.arch != SJ_ARCH_MODERNBERT && c.arch != SJ_ARCH_SJMODEL) return SJ_ERR_UNSUPPORTED;
+    return bad(SJ_ERR_UNSUPPORTED, "the FP8 variant needs the DecisionModel encoder with "
+                                   "hidden_size % 128 == 0, <= 1024, head_dim 64");
+  if (c.arch != SJ_ARCH_MODERNBERT && c.arch != SJ_ARCH_SJMODEL)
+    return bad(SJ_ERR_UNSUPPORTED, "unknown arch");
   // SjModel's learned positions are added in the warp-per-row embedding kernel
   if (c.arch == SJ_ARCH_SJMODEL && (c.hidden_size > 1024 || c.hidden_size % 4 != 0))
-    return SJ_ERR_UNSUPPORTED;
+    return bad(SJ_ERR_UNSUPPORTED, "SjModel needs hidden_size <= 1024 and % 4 == 0");
   e->D = c.hidden_size;
   e->H = c.num_attention_heads;
   e->Dh = e->D / e->H;
@@ -1045,10 +1082,13 @@ int sj_fast_create(const sj_fast_config* cfg, sj_fast** out) {
   if (c.layer_sliding && c.arch == SJ_ARCH_MODERNBERT)
     for (int i = 0; i < e->NL; ++i) e->sliding[i] = c.layer_sliding[i];
   e->cfg.layer_sliding = nullptr;  // not retained
-  if (e->bf16_mode && (e->D % 8 != 0 || e->F % 8 != 0)) return SJ_ERR_UNSUPPORTED;
+  if (e->bf16_mode && (e->D % 8 != 0 || e->F % 8 != 0))
+    return bad(SJ_ERR_UNSUPPORTED, "bf16 mode needs hidden_size and intermediate_size % 8 == 0");
   cudaError_t rc = cudaSetDevice(c.device);
   if (rc == cudaSuccess) rc = cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking);
-  if (rc != cudaSuccess) return SJ_ERR_CUDA;
+  if (rc != cudaSuccess)
+    return bad(SJ_ERR_CUDA, std::string("device ") + std::to_string(c.device) + ": " +
+                                cudaGetErrorString(rc));
   *out = e.release();
   return SJ_OK;
 }

@@ -152,8 +152,39 @@ void attn_tc_inject_wait_timeout(bool enable);
 // device cu_seqlens that disagree with the host mirror (then cleared).
 cudaError_t attn_noalloc_take_status(int* code);
 // tiles: list of (b, q0) query tiles of 128 rows (or null: B x ceil(max_seqlen/128)).
+// In the grid form, segments of long_min tokens or more are skipped (they
+// went to attn_long).
 cudaError_t attn_tc(const bf16* qkv, const int32_t* cu, const int32_t* kv_lens, bf16* O, int T,
                     int H, int window, const int2* tiles, int n_tiles, int B, int max_seqlen,
-                    int* err, cudaStream_t st);
+                    int* err, cudaStream_t st, int long_min = 0x7fffffff);
+
+// ---- tcgen05 flash attention for long segments (attn_long.cu) ----------------
+// Full-attention layers (no window) at head_dim 64 send segments of at least
+// kAttnLongMin tokens to attn_long (one CTA per SM, items of 256 queries,
+// 128-key tiles) and the rest to attn_tc.  Measured per segment length (12
+// heads, 65536 tokens, L2 flushed): attn_tc is faster up to 384 tokens, the
+// two are even at 512, attn_long is 8-16 % faster from 768 to 2048.
+constexpr int kAttnLongMin = 512;
+// The split pays when the long segments carry at least half of the attention
+// work (sum of n^2 over segments): otherwise the long kernel's launch, run
+// before attn_tc on the same stream, costs more than it saves (C2's mixed
+// lengths with one 512-token segment: 89 against 74 us).
+inline bool attn_long_pays(const int32_t* cu_host, int B) {
+  double all = 0.0, lng = 0.0;
+  for (int b = 0; b < B; ++b) {
+    const double n = (double)(cu_host[b + 1] - cu_host[b]);
+    all += n * n;
+    if (n >= kAttnLongMin) lng += n * n;
+  }
+  return lng > 0.0 && 2.0 * lng >= all;
+}
+// pairs: list of (b, q0) items of 256 query rows (q0 % 256 == 0), or null:
+// the grid form over B x ceil(max_seqlen / 256) items per head, segments
+// shorter than kAttnLongMin idle.
+cudaError_t attn_long(const bf16* qkv, const int32_t* cu, const int32_t* kv_lens, bf16* O, int T,
+                      int H, const int2* pairs, int n_pairs, int B, int max_seqlen, int* err,
+                      cudaStream_t st);
+// As attn_tc_take_status, for attn_long launches given no error flag.
+cudaError_t attn_long_take_status(int* code);
 
 }  // namespace sjb

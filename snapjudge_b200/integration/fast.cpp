@@ -14,7 +14,11 @@
 // the padding; then every padded row is computed, keys masked by the row's
 // attention-mask length, as the CPU forward does.
 // Failures throw std::runtime_error("snapjudge CUDA: ..."), as cuda/fast.cpp:54-58.
+// Precision: bf16 (the reference fast path's contract, cuda/fast.cpp:1-6) unless
+// SNAPJUDGE_FAST_PRECISION=fp32 selects the fp32 parity mode (1e-4 relative to
+// the CPU forward), e.g. to reproduce CPU outputs that sit on a tie.
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <stdexcept>
@@ -68,7 +72,8 @@ FastSnapjudge::FastSnapjudge(DecisionModel* model, int max_len, bool /*use_graph
   fc.layer_sliding = sliding.data();
   fc.rope_theta_full = c.rope_theta_full;
   fc.rope_theta_sliding = c.rope_theta_sliding;
-  fc.precision = SJ_PREC_BF16;
+  const char* prec = std::getenv("SNAPJUDGE_FAST_PRECISION");
+  fc.precision = (prec && std::string(prec) == "fp32") ? SJ_PREC_FP32 : SJ_PREC_BF16;
   fc.device = 0;
   fc.max_tokens = 0;
   int rc = sj_fast_create(&fc, &im.e);

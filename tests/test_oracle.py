@@ -140,3 +140,19 @@ def test_embed_mean_known_answer():
     h2 = h.copy()
     h2[0, 2] = np.nan
     assert np.array_equal(oracle.embed_mean(h2, mask), got)
+
+
+@pytest.mark.parametrize("H,Dh,lens,window,kv_lens", [
+    (2, 8, [6, 4], 0, None), (2, 8, [6, 4], 2, None), (3, 16, [40, 1, 0, 17], 0, [30, 1, 0, 3]),
+    (2, 64, [300, 129], 0, None), (2, 64, [200, 50], 7, None), (1, 16, [5, 9], 0, [0, 9])])
+def test_numpy_attention_matches_c_restatement(H, Dh, lens, window, kv_lens):
+    """The matrix-product restatement (used for long segments in the GPU
+    parity tests) agrees with the scalar C restatement of
+    src/tensor.cpp:156-228, including kv_lens (padded-batch semantics), windows,
+    empty segments and segments with no visible key."""
+    rng = np.random.default_rng(21)
+    T = int(np.sum(lens))
+    q, k, v = (rng.standard_normal((T, H, Dh), dtype=np.float32) for _ in range(3))
+    want = oracle.attention_packed(q, k, v, lens, window, kv_lens)
+    close(oracle.attention_packed_np(q, k, v, lens, window, kv_lens), want, 2e-6)
+    close(oracle.attention_packed_np(q, k, v, lens, window, kv_lens, dtype=np.float32), want, 2e-5)
