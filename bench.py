@@ -240,7 +240,11 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-fp8", action="store_true", help="skip the FP8-variant section")
+    ap.add_argument("--ncu-case", action="store_true",
+                    help="run only the small case the profiles/ summaries are captured on")
     a = ap.parse_args()
+    if a.ncu_case:
+        return ncu_case()
 
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
@@ -468,6 +472,35 @@ def main():
         dist.barrier()
         dist.destroy_process_group()
     eng.close()
+    return 0
+
+
+def ncu_case():
+    """The small case of the ncu captures (profiles/): two C5-like encoder passes
+    of ~32k tokens through sj_fast_decide (every encoder kernel, launched as in
+    the bench), then two launches of sj_attn on C4's attention shape at 16 x 2048
+    tokens (16 heads; attn_long).  A few GB on the device at most; inputs larger
+    than L2 except where noted in the summaries."""
+    import torch
+    from snapjudge_b200 import ops
+    from snapjudge_b200.fast import FastSnapjudge
+    torch.cuda.set_device(0)
+    spec = synth.SPECS["c5"]
+    weights = synth.make_weights(spec)
+    lengths = synth.make_lengths(spec, batch=32768, seed=5)
+    lengths = lengths[: int(np.searchsorted(np.cumsum(lengths), 32768))]
+    ids = synth.make_ids(spec, lengths, seed=6)
+    eng = FastSnapjudge(spec.cfg, weights, precision="bf16", heads=spec.heads, max_tokens=65536)
+    for _ in range(2):
+        probs = eng.decide(ids, lengths)
+    cu = synth.cu_seqlens(np.full(16, 2048))
+    qkv = torch.randn(int(cu[-1]), 3 * 16 * 64, device="cuda").to(torch.bfloat16)
+    for _ in range(2):
+        o = ops.attn(qkv, cu, 16, 64)
+    torch.cuda.synchronize()
+    eng.close()
+    print(f"ncu case: {int(lengths.sum())} tokens, probs sum {float(probs.sum()):.3f}, "
+          f"attention |O| mean {float(o.float().abs().mean()):.5f}")
     return 0
 
 

@@ -181,10 +181,12 @@ struct LItem {
 };
 
 // Item w.  List form (pairs != null): pairs[w / H] = (b, q0), head w % H.
-// Grid form: w = ((npp - 1 - p) * B + b) * H + h, q0 = 256 p (npp items per
-// segment at most), the highest p first: only the longest segments have them,
-// so their work starts first; segments shorter than long_min belong to attn_tc
-// and are idle here.
+// Grid form: w = (b * npp + (npp - 1 - p)) * H + h, q0 = 256 p (npp items per
+// segment at most): a segment's items are adjacent, so the CTAs working on it
+// at the same time share its K/V tiles through L2 (with the items of one
+// segment and head spread over time, each re-read K/V from DRAM: 948 MB for
+// 201 MB of Q/K/V on C4's shape); segments shorter than long_min belong to
+// attn_tc and are idle here.
 __device__ __forceinline__ LItem decode(int w, const int2* pairs, int H, int B, int npp,
                                         const int32_t* cu, const int32_t* kv_lens, int long_min) {
   LItem it;
@@ -196,8 +198,8 @@ __device__ __forceinline__ LItem decode(int w, const int2* pairs, int H, int B, 
     b = p.x;
     it.q0 = p.y;
   } else {
-    b = rest % B;
-    it.q0 = (npp - 1 - rest / B) * 2 * QT;
+    b = rest / npp;
+    it.q0 = (npp - 1 - rest % npp) * 2 * QT;
   }
   it.s0 = cu[b];
   it.n = cu[b + 1] - it.s0;

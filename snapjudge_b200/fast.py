@@ -96,7 +96,10 @@ class FastSnapjudge:
 
     def close(self) -> None:
         if getattr(self, "_h", None):
-            _lib.lib().sj_fast_destroy(self._h)
+            try:
+                _lib.lib().sj_fast_destroy(self._h)
+            except TypeError:  # interpreter shutdown: the bindings are gone already
+                pass
             self._h = None
 
     def __del__(self):
