@@ -240,11 +240,14 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-fp8", action="store_true", help="skip the FP8-variant section")
+    ap.add_argument("--no-c4", action="store_true", help="skip the C4 encoder section")
     ap.add_argument("--ncu-case", action="store_true",
                     help="run only the small case the profiles/ summaries are captured on")
+    ap.add_argument("--ncu-precision", default="bf16",
+                    help="engine precision of the --ncu-case passes (bf16, fp8, fp8_tensor)")
     a = ap.parse_args()
     if a.ncu_case:
-        return ncu_case()
+        return ncu_case(a.ncu_precision)
 
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
@@ -453,6 +456,8 @@ def main():
         line["attention"] = attention_section(st, dev, pk, pk_kind)
         if world == 1 and not a.no_fp8:
             line["fp8"] = fp8_section(spec, weights, a, local, st, pass_args, probs_d, T, value)
+        if world == 1 and not a.no_c4:
+            line["c4"] = c4_section(a, local, st, pk, pk_kind)
         if world == 1 and not a.no_cpu_baseline:
             tok, sec, n, kind, cores = reference_sample(spec, weights, a.cpu_seconds, 8, 4096,
                                                         seed=spec.seed + 40000, batch=1)
@@ -475,12 +480,68 @@ def main():
     return 0
 
 
-def ncu_case():
+def c4_section(a, local, st, pk, pk_kind):
+    """BASELINE config 4 (the attention-dominated encoder): 24 pre-LN layers,
+    d_model 1024, 16 heads x 64, GEGLU 2816, vocab 50368, 32 sequences of
+    2048 tokens (no padding), seeded N(0, 0.02) weights, the noul head.  One
+    step = the batch through the encoder and the head (one pass), device-
+    resident inputs, CUDA events; the roofline is the forward's FLOPs
+    (layers x [T 2 (4 D^2 + 3 D F) + 4 D sum n^2]) against the
+    measured sustained bf16 peak."""
+    import torch
+    from snapjudge_b200.fast import FastSnapjudge
+    spec = synth.SPECS["c4"]
+    weights = synth.make_weights(spec)
+    lengths = synth.make_lengths(spec)
+    ids = synth.make_ids(spec, lengths)
+    c = spec.cfg
+    D, F, L, H = c.hidden_size, c.intermediate_size, c.num_hidden_layers, c.num_attention_heads
+    T = int(lengths.sum())
+    eng = FastSnapjudge(c, weights, precision="bf16", heads=spec.heads, device=local,
+                        max_tokens=T)
+    dev = torch.device("cuda", local)
+    cu_h = synth.cu_seqlens(lengths).astype(np.int32)
+    ids_d = torch.from_numpy(ids).to(dev)
+    cu_d = torch.from_numpy(cu_h).to(dev)
+    probs = torch.empty(len(lengths), eng.n_out, dtype=torch.float32, device=dev)
+    steps = max(3, a.steps // 2)
+    for _ in range(a.warmup):
+        eng.encode_device(ids_d, cu_d, cu_h, probs=probs, stream=st)
+    eng.sync(st)
+    eng.profile(reset=True)
+    eng.set_profiling(True)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(steps):
+        eng.encode_device(ids_d, cu_d, cu_h, probs=probs, stream=st)
+    e1.record(st)
+    eng.sync(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    prof = eng.profile(reset=True)
+    eng.set_profiling(False)
+    eng.close()
+    sq = float(np.sum(lengths.astype(np.float64) ** 2))
+    flops = L * (T * 2.0 * (4 * D * D + 3 * D * F) + 4.0 * D * sq)
+    tf = flops / (ms / 1e3) / 1e12
+    peak = pk.get("bf16_tflops_sustained", FALLBACK["bf16_tflops_sustained"])
+    return {"config": "c4: 24 layers x 1024 (16 heads x 64, GEGLU 2816, vocab 50368), "
+                      "32 x 2048 tokens, noul head, bf16",
+            "tokens_per_s": T / (ms / 1e3), "ms_per_step": ms, "steps": steps,
+            "flops_per_step": flops, "tflops": tf, "frac_of_roofline": tf / peak,
+            "peak": peak, "peak_kind": f"{pk_kind} sustained bf16",
+            "kernels_ms_per_step": {k: v[0] / steps for k, v in prof.items()}}
+
+
+def ncu_case(precision: str = "bf16"):
     """The small case of the ncu captures (profiles/): two C5-like encoder passes
     of ~32k tokens through sj_fast_decide (every encoder kernel, launched as in
-    the bench), then two launches of sj_attn on C4's attention shape at 16 x 2048
-    tokens (16 heads; attn_long).  A few GB on the device at most; inputs larger
-    than L2 except where noted in the summaries."""
+    the bench; `precision` selects the engine mode, e.g. fp8_tensor, whose
+    first call adds its bf16 calibration pass), then two launches of sj_attn on
+    C4's attention shape at 16 x 2048 tokens (16 heads; attn_long).  A few GB
+    on the device at most; inputs larger than L2 except where noted in the
+    summaries."""
     import torch
     from snapjudge_b200 import ops
     from snapjudge_b200.fast import FastSnapjudge
@@ -490,7 +551,8 @@ def ncu_case():
     lengths = synth.make_lengths(spec, batch=32768, seed=5)
     lengths = lengths[: int(np.searchsorted(np.cumsum(lengths), 32768))]
     ids = synth.make_ids(spec, lengths, seed=6)
-    eng = FastSnapjudge(spec.cfg, weights, precision="bf16", heads=spec.heads, max_tokens=65536)
+    eng = FastSnapjudge(spec.cfg, weights, precision=precision, heads=spec.heads,
+                        max_tokens=65536)
     for _ in range(2):
         probs = eng.decide(ids, lengths)
     cu = synth.cu_seqlens(np.full(16, 2048))
@@ -580,59 +642,92 @@ def attention_section(st, dev, pk, pk_kind):
 
 
 def fp8_section(spec, weights, a, local, st, pass_args, probs_d, T, value_bf16):
-    """The FP8 variant (SJ_PREC_FP8: e4m3 operands for the QKV and Wi projections)
-    on the same passes, timed like the main line; reported separately, beside the
-    bf16 headline, with its difference from the bf16 outputs."""
+    """The two FP8 variants on the same passes, timed like the main line and
+    reported separately, beside the bf16 headline:
+    * fp8 (SJ_PREC_FP8): e4m3 operands for the QKV and Wi projections,
+      per-token activation and per-channel weight scales;
+    * fp8_tensor (SJ_PREC_FP8_TENSOR): QKV, Wi and Wo2 on e4m3, one scale per
+      weight tensor and static activation scales, calibrated on the engine's
+      first pass (the first warm-up pass here).
+    Accuracy: decision probabilities of config 5's four heads on 256 requests
+    of its length distribution, against the engine's fp32 mode (which the
+    tests hold to 1e-4 relative of the CPU forward), beside the bf16 mode's."""
     import torch
     from snapjudge_b200.fast import FastSnapjudge
-    eng8 = FastSnapjudge(spec.cfg, weights, precision="fp8", heads=spec.heads, device=local,
-                         max_tokens=a.max_tokens)
-    probs8 = torch.empty_like(probs_d)
-    off = 0
-    args8 = []
-    for x_ids, x_cu, x_cuh, x_p in pass_args:
-        args8.append((x_ids, x_cu, x_cuh, probs8[off:off + x_p.shape[0]]))
-        off += x_p.shape[0]
-
-    def step8():
-        for x_ids, x_cu, x_cuh, x_p in args8:
-            eng8.encode_device(x_ids, x_cu, x_cuh, probs=x_p, stream=st)
-
-    for _ in range(a.warmup):
-        step8()
-    eng8.sync(st)
-    eng8.profile(reset=True)
-    eng8.set_profiling(True)
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(st)
-    for _ in range(a.steps):
-        step8()
-    e1.record(st)
-    eng8.sync(st)
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1)
-    prof = eng8.profile(reset=True)
-    eng8.set_profiling(False)
     D, F, L = spec.cfg.hidden_size, spec.cfg.intermediate_size, spec.cfg.num_hidden_layers
-    flops = {"qkv": 2.0 * T * 3 * D * D * L, "geglu": 2.0 * T * 2 * F * D * L}
-    kern = {}
-    for k in ("qkv", "geglu"):
-        kms = prof[k][0] / a.steps
-        tf = flops[k] / (kms / 1e3) / 1e12
-        kern[k] = {"ms_per_step": kms, "tflops": tf, "frac_of_nominal_fp8": tf / 4500.0}
-    v8 = T * a.steps / (ms / 1e3)
-    out = {"value": v8, "unit": "tokens/s", "ms_per_step": ms / a.steps,
-           "speedup_vs_bf16": v8 / value_bf16,
-           "precision": "e4m3 operands for the QKV and Wi (GEGLU) projections, per-token "
-                        "activation and per-channel weight scales, fp32 accumulation; bf16 "
-                        "elsewhere (SJ_PREC_FP8); reported separately from the bf16 headline",
-           "kernels": kern,
-           "probs_max_abs_diff_vs_bf16": float((probs8 - probs_d).abs().max().item()),
-           "peak_note": "nominal dense e4m3 4.5 PFLOP/s (no measured FP8 peak on this pool)"}
-    eng8.close()
-    return out
+    flops = {"qkv": 2.0 * T * 3 * D * D * L, "geglu": 2.0 * T * 2 * F * D * L,
+             "wo2": 2.0 * T * D * F * L}
+    acc_len = synth.make_lengths(spec, batch=256, seed=spec.seed + 52000)
+    acc_ids = synth.make_ids(spec, acc_len, seed=spec.seed + 53000)
 
+    def probs_of(prec, eng=None):
+        own = eng is None
+        if own:
+            eng = FastSnapjudge(spec.cfg, weights, precision=prec, heads=spec.heads,
+                                device=local, max_tokens=a.max_tokens)
+        p = eng.decide(acc_ids, acc_len).copy()
+        if own:
+            eng.close()
+        return p
+
+    p32 = probs_of("fp32")
+    out = {"accuracy_sample": f"{len(acc_len)} c5 requests ({int(acc_len.sum())} tokens), "
+                              f"4 heads ({p32.shape[1]} probabilities each), max-abs against "
+                              f"the fp32 mode",
+           "bf16_probs_max_abs_vs_fp32": float(np.abs(probs_of("bf16") - p32).max()),
+           "peak_note": "nominal dense e4m3 4.5 PFLOP/s (no measured FP8 peak on this pool)"}
+    for prec in ("fp8", "fp8_tensor"):
+        eng8 = FastSnapjudge(spec.cfg, weights, precision=prec, heads=spec.heads, device=local,
+                             max_tokens=a.max_tokens)
+        probs8 = torch.empty_like(probs_d)
+        off = 0
+        args8 = []
+        for x_ids, x_cu, x_cuh, x_p in pass_args:
+            args8.append((x_ids, x_cu, x_cuh, probs8[off:off + x_p.shape[0]]))
+            off += x_p.shape[0]
+
+        def step8():
+            for x_ids, x_cu, x_cuh, x_p in args8:
+                eng8.encode_device(x_ids, x_cu, x_cuh, probs=x_p, stream=st)
+
+        for _ in range(a.warmup):
+            step8()
+        eng8.sync(st)
+        eng8.profile(reset=True)
+        eng8.set_profiling(True)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(a.steps):
+            step8()
+        e1.record(st)
+        eng8.sync(st)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        prof = eng8.profile(reset=True)
+        eng8.set_profiling(False)
+        kern = {}
+        for k in ("qkv", "geglu", "wo2"):
+            kms = prof[k][0] / a.steps
+            tf = flops[k] / (kms / 1e3) / 1e12
+            kern[k] = {"ms_per_step": kms, "tflops": tf,
+                       "operands": "e4m3" if (k != "wo2" or prec == "fp8_tensor") else "bf16"}
+        v8 = T * a.steps / (ms / 1e3)
+        out[prec] = {
+            "value": v8, "unit": "tokens/s", "ms_per_step": ms / a.steps,
+            "speedup_vs_bf16": v8 / value_bf16,
+            "precision": ("e4m3 operands for the QKV and Wi (GEGLU) projections, per-token "
+                          "activation and per-channel weight scales, fp32 accumulation; bf16 "
+                          "elsewhere (SJ_PREC_FP8)") if prec == "fp8" else
+                         ("e4m3 operands for the QKV, Wi and Wo2 projections, one scale per "
+                          "weight tensor, static per-tensor activation scales calibrated on "
+                          "the first pass (amax x 2 / 448), fp32 accumulation; bf16 elsewhere "
+                          "(SJ_PREC_FP8_TENSOR)"),
+            "kernels": kern,
+            "probs_max_abs_vs_bf16_on_bench_set": float((probs8 - probs_d).abs().max().item()),
+            "probs_max_abs_vs_fp32": float(np.abs(probs_of(prec, eng8) - p32).max())}
+        eng8.close()
+    return out
 
 if __name__ == "__main__":
     sys.exit(main())

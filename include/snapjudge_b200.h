@@ -43,6 +43,11 @@ extern "C" {
                           operands: per-token activation scales, per-channel weight scales,
                           fp32 accumulation (DecisionModel encoder only; reported separately,
                           not held to the bf16 tolerances) */
+#define SJ_PREC_FP8_TENSOR 3 /* SJ_PREC_FP8 with one scale per tensor: per-tensor weight scales,
+                                static activation scales calibrated on the engine's first
+                                forward (a bf16 pass recording each operand's amax, 2x
+                                headroom), and the Wo2 projection on e4m3 too (the GEGLU
+                                GEMM writes e4m3 codes); intermediate_size % 128 == 0 */
 
 #define SJ_HEAD_SOFTMAX 0
 #define SJ_HEAD_SIGMOID 1
@@ -163,7 +168,7 @@ typedef struct sj_fast_config {
   double rope_theta_full;
   double rope_theta_sliding;
   /* engine options */
-  int precision;                /* SJ_PREC_BF16, SJ_PREC_FP32 or SJ_PREC_FP8 */
+  int precision;                /* SJ_PREC_BF16, SJ_PREC_FP32, SJ_PREC_FP8 or SJ_PREC_FP8_TENSOR */
   int device;                   /* CUDA device ordinal */
   int max_tokens;               /* tokens per device pass (workspace size); 0 = default */
   int arch;                     /* SJ_ARCH_MODERNBERT (0) or SJ_ARCH_SJMODEL (1) */

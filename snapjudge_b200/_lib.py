@@ -21,6 +21,7 @@ SJ_ERR_STATE = -5
 SJ_PREC_BF16 = 0
 SJ_PREC_FP32 = 1
 SJ_PREC_FP8 = 2
+SJ_PREC_FP8_TENSOR = 3
 SJ_ARCH_MODERNBERT = 0
 SJ_ARCH_SJMODEL = 1
 

@@ -64,9 +64,11 @@ struct LayerDev {
   // wqkv with bias bqkv [3D], Wo bias, wi = ffn.w1 [F, D] + b1, wo2 = ffn.w2 + b2
   float *attn_norm_b = nullptr, *mlp_norm_b = nullptr;
   float *bqkv = nullptr, *bo = nullptr, *b1 = nullptr, *b2 = nullptr;
-  // SJ_PREC_FP8: e4m3 copies of wqkv and wi with a scale per row
-  uint8_t *wqkv8 = nullptr, *wi8 = nullptr;
-  float *sqkv = nullptr, *si = nullptr;
+  // SJ_PREC_FP8: e4m3 copies of wqkv and wi with a scale per row;
+  // SJ_PREC_FP8_TENSOR: wqkv, wi and wo2 with one scale per tensor (the scale
+  // arrays then hold that one value in every row)
+  uint8_t *wqkv8 = nullptr, *wi8 = nullptr, *wo2_8 = nullptr;
+  float *sqkv = nullptr, *si = nullptr, *so2 = nullptr;
 };
 
 // One pre-norm TransformerEncoderLayer of the decision head (model.cpp:134-152):
@@ -97,6 +99,12 @@ struct sj_fast {
   int max_tokens = 0;
   bool bf16_mode = true;
   bool fp8 = false;  // SJ_PREC_FP8: QKV and Wi projections on e4m3 operands
+  // SJ_PREC_FP8_TENSOR: QKV, Wi and Wo2 on e4m3 operands, one scale per tensor;
+  // the activation scales are calibrated on the engine's first pass
+  bool fp8_tensor = false;
+  bool calibrated = false, calibrating = false;
+  float* act_scale = nullptr;     // [3 * NL]: QKV input, Wi input, Wo2 input of each layer
+  unsigned* act_amax = nullptr;   // [3 * NL] amax seen by the calibration pass (float bits)
   bool committed = false;
   cudaStream_t stream = nullptr;
   std::string err;
@@ -152,6 +160,8 @@ struct sj_fast {
   float* z = nullptr;     // LoRA [max_tokens, r]
   uint8_t* Y8 = nullptr;  // SJ_PREC_FP8: LN output as e4m3 [max_tokens, D]
   float* sa8 = nullptr;   //   and its row scales [max_tokens]
+  uint8_t* G8 = nullptr;  // SJ_PREC_FP8_TENSOR: GEGLU output as e4m3 [max_tokens, F]
+  float* sg8 = nullptr;   //   and its row scales [max_tokens]
   int* dflags = nullptr;  // device error flags: [0] bad id, [1] gemm wait, [2] attn wait
   // pinned host staging
   int2* h_tiles = nullptr;
@@ -285,6 +295,25 @@ struct sj_fast {
     return rc == cudaSuccess ? SJ_OK : cuda_fail(rc, "e4m3 weight upload");
   }
 
+  // e4m3 codes of a [rows, cols] weight with one scale for the whole tensor
+  // (its amax / 448, taken on the host); the scale array holds it per row
+  int upload_e4m3_tensor(const HostTensor* t, uint8_t** q, float** scale) {
+    const int64_t rows = t->shape[0];
+    float amax = 0.f;
+    for (float v : t->data) amax = std::max(amax, std::fabs(v));
+    float* tmp = nullptr;
+    cudaError_t rc = cudaMalloc(&tmp, t->data.size() * sizeof(float));
+    if (rc != cudaSuccess) return cuda_fail(rc, "cudaMalloc");
+    if ((rc = cudaMemcpy(tmp, t->data.data(), t->data.size() * sizeof(float),
+                         cudaMemcpyHostToDevice)) == cudaSuccess &&
+        (rc = dalloc(q, t->data.size())) == cudaSuccess && (rc = dalloc(scale, rows)) == cudaSuccess &&
+        (rc = sjb::quant_tensor_e4m3(tmp, (int64_t)t->data.size(), (int)rows, amax, *q, *scale,
+                                     nullptr)) == cudaSuccess)
+      rc = cudaDeviceSynchronize();
+    cudaFree(tmp);
+    return rc == cudaSuccess ? SJ_OK : cuda_fail(rc, "e4m3 weight upload");
+  }
+
   int commit();
   int load_sjmodel();
   template <typename T>
@@ -347,16 +376,21 @@ int sj_fast::commit() {
     }
     if ((s = require(p + "attn.Wqkv.weight", {3 * (int64_t)D, D}, &t))) return s;
     if ((s = upload_w(t, &ly.wqkv))) return s;
-    if (fp8 && (s = upload_e4m3(t, &ly.wqkv8, &ly.sqkv))) return s;
+    if (fp8 && (s = fp8_tensor ? upload_e4m3_tensor(t, &ly.wqkv8, &ly.sqkv)
+                               : upload_e4m3(t, &ly.wqkv8, &ly.sqkv)))
+      return s;
     if ((s = require(p + "attn.Wo.weight", {D, D}, &t))) return s;
     if ((s = upload_w(t, &ly.wo))) return s;
     if ((s = require(p + "mlp_norm.weight", {D}, &t))) return s;
     if ((s = upload_f32(t, &ly.mlp_norm))) return s;
     if ((s = require(p + "mlp.Wi.weight", {2 * (int64_t)F, D}, &t))) return s;
     if ((s = upload_w(t, &ly.wi))) return s;
-    if (fp8 && (s = upload_e4m3(t, &ly.wi8, &ly.si))) return s;
+    if (fp8 && (s = fp8_tensor ? upload_e4m3_tensor(t, &ly.wi8, &ly.si)
+                               : upload_e4m3(t, &ly.wi8, &ly.si)))
+      return s;
     if ((s = require(p + "mlp.Wo.weight", {D, F}, &t))) return s;
     if ((s = upload_w(t, &ly.wo2))) return s;
+    if (fp8_tensor && (s = upload_e4m3_tensor(t, &ly.wo2_8, &ly.so2))) return s;
   }
   // optional encoder-output LoRA (src/model.cpp:192-203)
   const HostTensor* la = get("lora_A.weight");
@@ -473,7 +507,10 @@ int sj_fast::commit() {
       (rc = dalloc(&cu, T + 1)) || (rc = dalloc(&kvl, T)) || (rc = dalloc(&tiles, max_tiles)) ||
       (rc = dalloc(&Hc, T * D)) || (rc = dalloc(&probs, T * (size_t)std::max(1, spec.n_total))) ||
       (rc = dalloc(&hid, T * D)) || (rc = dalloc(&z, T * (size_t)std::max(1, lora_r))) ||
-      (rc = dalloc(&dflags, 8)) || (fp8 && ((rc = dalloc(&Y8, T * D)) || (rc = dalloc(&sa8, T)))))
+      (rc = dalloc(&dflags, 8)) || (fp8 && ((rc = dalloc(&Y8, T * D)) || (rc = dalloc(&sa8, T)))) ||
+      (fp8_tensor && ((rc = dalloc(&G8, T * F)) || (rc = dalloc(&sg8, T)) ||
+                      (rc = dalloc(&act_scale, 3 * (size_t)NL)) ||
+                      (rc = dalloc(&act_amax, 3 * (size_t)NL)))))
     return cuda_fail(rc, "cudaMalloc (workspace)");
   if ((rc = cudaMemset(dflags, 0, 8 * sizeof(int)))) return cuda_fail(rc, "cudaMemset");
   if ((rc = cudaMallocHost(&h_tiles, max_tiles * sizeof(int2))) ||
@@ -676,13 +713,24 @@ int sj_fast::forward(const int64_t* d_ids, const int32_t* d_cu, const int32_t* h
   };
 
   // SJ_PREC_FP8: the attn_norm and mlp_norm outputs are e4m3 rows with their
-  // scales (Y8, sa8), the QKV and Wi GEMMs run on the e4m3 weights
-  const bool f8 = kBf16 && fp8 && !sjm;
+  // scales (Y8, sa8), the QKV and Wi GEMMs run on the e4m3 weights.
+  // SJ_PREC_FP8_TENSOR: the same with one static scale per activation tensor
+  // (act_scale), and the GEGLU GEMM writes e4m3 codes (G8) for an e4m3 Wo2.
+  // Its calibration pass runs the bf16 path and records each of those
+  // tensors' amax (act_amax).
+  const bool f8 = kBf16 && fp8 && !sjm && !calibrating;
+  const bool f8t = f8 && fp8_tensor;
   int s;
   for (int li = 0; li < NL; ++li) {
     const LayerDev& ly = layers[li];
     const T* Yin = Yt;
-    if (f8) {
+    if (f8t) {
+      if (ly.attn_norm)
+        SJ_LAUNCH(SJ_K_LN, sjb::ln_e4m3_static(X, ly.attn_norm, ly.attn_norm_b, Y8, sa8,
+                                               act_scale + 3 * li, ntok, D, eps, st));
+      else
+        SJ_LAUNCH(SJ_K_LN, sjb::quant_rows_static(X, ntok, D, Y8, sa8, act_scale + 3 * li, st));
+    } else if (f8) {
       if (ly.attn_norm)
         SJ_LAUNCH(SJ_K_LN, sjb::ln_e4m3(X, ly.attn_norm, ly.attn_norm_b, Y8, sa8, ntok, D, eps, st));
       else
@@ -694,6 +742,14 @@ int sj_fast::forward(const int64_t* d_ids, const int32_t* d_cu, const int32_t* h
       if constexpr (kBf16) SJ_LAUNCH(SJ_K_LN, sjb::cast_bf16(X, Yt, (int64_t)ntok * D, st));
       else Yin = reinterpret_cast<const T*>(X);
     }
+    if (calibrating) {  // the QKV input (layer 0's identity norm: X itself)
+      if constexpr (kBf16) {
+        if (ly.attn_norm || li > 0)
+          SJ_LAUNCH(SJ_K_LN, sjb::amax_abs<bf16>(Yt, (int64_t)ntok * D, act_amax + 3 * li, st));
+        else
+          SJ_LAUNCH(SJ_K_LN, sjb::amax_abs<float>(X, (int64_t)ntok * D, act_amax + 3 * li, st));
+      }
+    }
     const float* ct = ly.sliding ? cos_s : cos_f;
     const float* stb = ly.sliding ? sin_s : sin_f;
     if (sjm) {  // SjModel: biased q/k/v, no RoPE
@@ -703,8 +759,10 @@ int sj_fast::forward(const int64_t* d_ids, const int32_t* d_cu, const int32_t* h
     } else if (f8) {
       if constexpr (kBf16) {
         sjb::TcRope rp{ct, stb, pos, H};
+        sjb::TcQ8 uq;
+        uq.uniform = f8t;
         SJ_LAUNCH(SJ_K_QKV, sjb::gemm_tc_f8(Y8, ly.wqkv8, sa8, ly.sqkv, nullptr, Qt, ntok, 3 * D, D,
-                                            sjb::TC_ROPE, 0, rp, dflags + 1, st));
+                                            sjb::TC_ROPE, 0, rp, dflags + 1, st, nullptr, uq));
       }
     } else if ((s = gemm(SJ_K_QKV, Yin, ly.wqkv, Qt, nullptr, 3 * D, D, sjb::TC_ROPE, ct, stb))) {
       return s;
@@ -727,15 +785,33 @@ int sj_fast::forward(const int64_t* d_ids, const int32_t* d_cu, const int32_t* h
     }
     if ((s = gemm(SJ_K_WO, Ot, ly.wo, nullptr, X, D, D, sjb::TC_RESID, nullptr, nullptr, ly.bo)))
       return s;
-    if (f8)
+    if (f8t)
+      SJ_LAUNCH(SJ_K_LN, sjb::ln_e4m3_static(X, ly.mlp_norm, ly.mlp_norm_b, Y8, sa8,
+                                             act_scale + 3 * li + 1, ntok, D, eps, st));
+    else if (f8)
       SJ_LAUNCH(SJ_K_LN, sjb::ln_e4m3(X, ly.mlp_norm, ly.mlp_norm_b, Y8, sa8, ntok, D, eps, st));
     else
       SJ_LAUNCH(SJ_K_LN, (sjb::add_ln<T, T>(X, nullptr, ly.mlp_norm, ly.mlp_norm_b, Yt, ntok, D, eps,
                                             nullptr, st)));
+    if (calibrating) {
+      if constexpr (kBf16)
+        SJ_LAUNCH(SJ_K_LN, sjb::amax_abs<bf16>(Yt, (int64_t)ntok * D, act_amax + 3 * li + 1, st));
+    }
     if (sjm) {  // SjModel: G = gelu(Y W1^T + b1), X += G W2^T + b2
       if ((s = gemm(SJ_K_GEGLU, Yt, ly.wi, Gt, nullptr, F, D, sjb::TC_STORE, nullptr, nullptr, ly.b1,
                     sjb::ACT_GELU)))
         return s;
+    } else if (f8t) {
+      if constexpr (kBf16) {
+        sjb::TcQ8 q8;
+        q8.C = G8;
+        q8.scale = act_scale + 3 * li + 2;
+        q8.rowscale = sg8;
+        q8.uniform = true;
+        SJ_LAUNCH(SJ_K_GEGLU, sjb::gemm_tc_f8(Y8, ly.wi8, sa8, ly.si, nullptr, nullptr, ntok, F, D,
+                                              sjb::TC_GEGLU, 0, sjb::TcRope{}, dflags + 1, st,
+                                              nullptr, q8));
+      }
     } else if (f8) {
       if constexpr (kBf16)
         SJ_LAUNCH(SJ_K_GEGLU, sjb::gemm_tc_f8(Y8, ly.wi8, sa8, ly.si, nullptr, Gt, ntok, F, D,
@@ -743,8 +819,21 @@ int sj_fast::forward(const int64_t* d_ids, const int32_t* d_cu, const int32_t* h
     } else if ((s = gemm(SJ_K_GEGLU, Yt, ly.wi, Gt, nullptr, F, D, sjb::TC_GEGLU, nullptr, nullptr))) {
       return s;
     }
-    if ((s = gemm(SJ_K_WO2, Gt, ly.wo2, nullptr, X, D, F, sjb::TC_RESID, nullptr, nullptr, ly.b2)))
+    if (calibrating) {
+      if constexpr (kBf16)
+        SJ_LAUNCH(SJ_K_GEGLU, sjb::amax_abs<bf16>(Gt, (int64_t)ntok * F, act_amax + 3 * li + 2, st));
+    }
+    if (f8t) {
+      if constexpr (kBf16) {
+        sjb::TcQ8 uq;
+        uq.uniform = true;
+        SJ_LAUNCH(SJ_K_WO2, sjb::gemm_tc_f8(G8, ly.wo2_8, sg8, ly.so2, ly.b2, nullptr, ntok, D, F,
+                                            sjb::TC_RESID, 0, sjb::TcRope{}, dflags + 1, st, X, uq));
+      }
+    } else if ((s = gemm(SJ_K_WO2, Gt, ly.wo2, nullptr, X, D, F, sjb::TC_RESID, nullptr, nullptr,
+                         ly.b2))) {
       return s;
+    }
   }
   // final norm (+ LoRA): all rows -> d_hidden, [CLS] rows -> heads
   if (d_hidden) {
@@ -861,6 +950,22 @@ int sj_fast::run(const int64_t* d_ids, const int32_t* d_cu, const int32_t* hcu,
   launches = 0;
   cudaError_t rc = cudaSetDevice(cfg.device);
   if (rc != cudaSuccess) return cuda_fail(rc, "cudaSetDevice");
+  if (fp8_tensor && !calibrated) {
+    // calibration: this first pass runs in bf16 and records the amax of every
+    // tensor that becomes an e4m3 operand; the scales are amax * 2 / 448 (a
+    // binade of headroom for later batches, whose larger values saturate at
+    // 448), fixed from then on; the pass then runs again in FP8
+    rc = cudaMemsetAsync(act_amax, 0, 3 * (size_t)NL * sizeof(unsigned), st);
+    if (rc != cudaSuccess) return cuda_fail(rc, "cudaMemsetAsync");
+    calibrating = true;
+    const int cs = forward<bf16>(d_ids, d_cu, hcu, d_kvl, B, T, d_hidden, d_probs, dm, st);
+    calibrating = false;
+    if (cs) return cs;
+    rc = sjb::scales_from_amax(act_amax, act_scale, 3 * NL, 2.f, st);
+    if (rc != cudaSuccess) return cuda_fail(rc, "scales_from_amax");
+    calibrated = true;
+    launches = 0;
+  }
   return bf16_mode ? forward<bf16>(d_ids, d_cu, hcu, d_kvl, B, T, d_hidden, d_probs, dm, st)
                    : forward<float>(d_ids, d_cu, hcu, d_kvl, B, T, d_hidden, d_probs, dm, st);
 }
@@ -1053,13 +1158,15 @@ int sj_fast_create(const sj_fast_config* cfg, sj_fast** out) {
       (c.hidden_size / c.num_attention_heads) % 2 != 0)
     return bad(SJ_ERR_INVALID, "bad model shape (sizes must be positive, hidden_size a multiple "
                                "of num_attention_heads, head_dim even)");
-  if (c.precision != SJ_PREC_BF16 && c.precision != SJ_PREC_FP32 && c.precision != SJ_PREC_FP8)
+  if (c.precision != SJ_PREC_BF16 && c.precision != SJ_PREC_FP32 && c.precision != SJ_PREC_FP8 &&
+      c.precision != SJ_PREC_FP8_TENSOR)
     return bad(SJ_ERR_UNSUPPORTED, "unknown precision");
   // the FP8 variant: the DecisionModel encoder, e4m3 GEMMs need K = D % 128 == 0,
   // the quantising LN D <= 1024, the attention head_dim 64 and N % 64 == 0
-  if (c.precision == SJ_PREC_FP8 &&
+  if ((c.precision == SJ_PREC_FP8 || c.precision == SJ_PREC_FP8_TENSOR) &&
       (c.arch != SJ_ARCH_MODERNBERT || c.hidden_size % 128 != 0 || c.hidden_size > 1024 ||
-       c.hidden_size / c.num_attention_heads != 64 || c.intermediate_size % 64 != 0))
+       c.hidden_size / c.num_attention_heads != 64 ||
+       c.intermediate_size % (c.precision == SJ_PREC_FP8_TENSOR ? 128 : 64) != 0))
     return bad(SJ_ERR_UNSUPPORTED, "the FP8 variant needs the DecisionModel encoder with "
                                    "hidden_size % 128 == 0, <= 1024, head_dim 64");
   if (c.arch != SJ_ARCH_MODERNBERT && c.arch != SJ_ARCH_SJMODEL)
@@ -1073,8 +1180,10 @@ int sj_fast_create(const sj_fast_config* cfg, sj_fast** out) {
   e->F = c.intermediate_size;
   e->V = c.vocab_size;
   e->NL = c.num_hidden_layers;
-  e->bf16_mode = c.precision == SJ_PREC_BF16 || c.precision == SJ_PREC_FP8;
-  e->fp8 = c.precision == SJ_PREC_FP8;
+  e->bf16_mode = c.precision == SJ_PREC_BF16 || c.precision == SJ_PREC_FP8 ||
+                 c.precision == SJ_PREC_FP8_TENSOR;
+  e->fp8 = c.precision == SJ_PREC_FP8 || c.precision == SJ_PREC_FP8_TENSOR;
+  e->fp8_tensor = c.precision == SJ_PREC_FP8_TENSOR;
   e->max_tokens = c.max_tokens > 0 ? c.max_tokens : (e->bf16_mode ? 262144 : 65536);
   e->max_tokens = std::max(e->max_tokens, 128);
   e->arch = c.arch;

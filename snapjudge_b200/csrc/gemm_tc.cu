@@ -58,6 +58,12 @@ struct EpiArgs {
   int rope_cols;         // columns [0, rope_cols) are rotated q/k heads
   const float* sa;       // F8: [M] scale of each A row
   const float* sw;       // F8: [w_rows] scale of each W row
+  // GEGLU with e4m3 output (SJ_PREC_FP8_TENSOR): codes of v / *c8_scale into
+  // C8 [M, ldc] (bytes) instead of bf16 C, c8_rowscale[row] = *c8_scale
+  uint8_t* C8;
+  const float* c8_scale;
+  float* c8_rowscale;
+  int uniform;           // F8: sa and sw hold one value each (per-tensor scales)
   int* err;
 };
 
@@ -152,6 +158,21 @@ __device__ __forceinline__ float2 geglu_pair(float ga, float gb, float ua, float
   return unpk2(mul2(gelu, pk2(ua, ub)));
 }
 
+// 32 values to e4m3 codes (x * inv, RN, saturating at +-448) in memory order,
+// written as two 16-byte stores
+__device__ __forceinline__ void store_e4m3x32(uint8_t* dst, const float* v, float inv) {
+  uint32_t w[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    uint16_t lo, hi;
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(lo) : "f"(v[4 * j + 1] * inv), "f"(v[4 * j] * inv));
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(hi) : "f"(v[4 * j + 3] * inv), "f"(v[4 * j + 2] * inv));
+    w[j] = (uint32_t)lo | ((uint32_t)hi << 16);
+  }
+  uint4* d = reinterpret_cast<uint4*>(dst);
+  d[0] = make_uint4(w[0], w[1], w[2], w[3]);
+  d[1] = make_uint4(w[4], w[5], w[6], w[7]);
+}
 __device__ __forceinline__ void store_bf16x32(bf16* dst, const float* v) {
   uint4* d = reinterpret_cast<uint4*>(dst);
 #pragma unroll
@@ -168,7 +189,12 @@ __device__ __forceinline__ void store_bf16x32(bf16* dst, const float* v) {
 
 // r[j] *= sa * sw[j] for 32 accumulator columns (sw 16-byte aligned): the
 // e4m3 operands' row and channel scales
-__device__ __forceinline__ void unscale32(uint32_t (&r)[32], float sa, const float* sw) {
+__device__ __forceinline__ void unscale32(uint32_t (&r)[32], float sa, const float* sw, float su) {
+  if (su != 0.f) {  // per-tensor scales: one product for every element
+#pragma unroll
+    for (int k = 0; k < 32; ++k) r[k] = __float_as_uint(__uint_as_float(r[k]) * su);
+    return;
+  }
   const float4* s4 = reinterpret_cast<const float4*>(sw);
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
@@ -180,17 +206,20 @@ __device__ __forceinline__ void unscale32(uint32_t (&r)[32], float sa, const flo
   }
 }
 
-__device__ __forceinline__ void unscale16(uint32_t (&r)[16], float sa, const float* sw) {
-  const float4* s4 = reinterpret_cast<const float4*>(sw);
+// unscale16 with the channel scales already in registers
+__device__ __forceinline__ void unscale16w(uint32_t (&r)[16], float sa, const float4 (&w)[4],
+                                           float su) {
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    const float4 w = __ldg(s4 + k);
-    r[4 * k] = __float_as_uint(__uint_as_float(r[4 * k]) * (sa * w.x));
-    r[4 * k + 1] = __float_as_uint(__uint_as_float(r[4 * k + 1]) * (sa * w.y));
-    r[4 * k + 2] = __float_as_uint(__uint_as_float(r[4 * k + 2]) * (sa * w.z));
-    r[4 * k + 3] = __float_as_uint(__uint_as_float(r[4 * k + 3]) * (sa * w.w));
+    const float m0 = su != 0.f ? su : sa * w[k].x, m1 = su != 0.f ? su : sa * w[k].y;
+    const float m2 = su != 0.f ? su : sa * w[k].z, m3 = su != 0.f ? su : sa * w[k].w;
+    r[4 * k] = __float_as_uint(__uint_as_float(r[4 * k]) * m0);
+    r[4 * k + 1] = __float_as_uint(__uint_as_float(r[4 * k + 1]) * m1);
+    r[4 * k + 2] = __float_as_uint(__uint_as_float(r[4 * k + 2]) * m2);
+    r[4 * k + 3] = __float_as_uint(__uint_as_float(r[4 * k + 3]) * m3);
   }
 }
+
 // 8 floats -> 8 bf16 (16 bytes)
 __device__ __forceinline__ uint4 pack_bf16x8(const float* v) {
   uint32_t w[4];
@@ -371,6 +400,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     int sbuf = 0;
     uint32_t xphase = 0u;  // bit b: parity of this warp's residual-load barrier b
     uint64_t* xb = xload_bar[warp - 2];
+    // per-tensor scales (ep.uniform): the product of the row and channel
+    // scales is one value, read once; the e4m3 GEGLU output's static scale too
+    const float su = F8 && ep.uniform ? ep.sa[0] * ep.sw[0] : 0.f;
+    const float s8 = ep.C8 ? *ep.c8_scale : 0.f, inv8 = s8 > 0.f ? 1.f / s8 : 0.f;
     // hand accumulator buffer b back to the MMA warp (rank 0's barrier in a pair)
     auto release = [&](int b) {
       fence_before_sync();
@@ -438,6 +471,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int k = 0; k < 32; ++k) { cs[k] = 1.f; sn[k] = 0.f; }
         }
       }
+      // the row scale (written before this kernel started) is read before
+      // the accumulator wait too
+      const int row = m0 + q * 32 + lane;
+      const bool live = row < M;
+      const float sa = F8 && live && su == 0.f ? ep.sa[row] : 0.f;
       int ok = 1;
       if (lane == 0) ok = mbar_wait<true>(&tfull_bar[b], aphase) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -446,9 +484,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       fence_after_sync();
-      const int row = m0 + q * 32 + lane;
-      const bool live = row < M;
-      const float sa = F8 && live ? ep.sa[row] : 0.f;
       const uint32_t tacc = tmem_base + ((uint32_t)(q * 32) << 16) + b * BN;
       uint32_t r0[32], r1[32];
       if (EPI == TC_GEGLU && STAGED) {
@@ -463,8 +498,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_ld32(tacc + HALF + c + 32 * k2, r1);
             tmem_ld_wait();
             if constexpr (F8) {
-              unscale32(r0, sa, ep.sw + col_base + c + 32 * k2);
-              unscale32(r1, sa, ep.sw + up_row0 + col_base + c + 32 * k2);
+              unscale32(r0, sa, ep.sw + col_base + c + 32 * k2, su);
+              unscale32(r1, sa, ep.sw + up_row0 + col_base + c + 32 * k2, su);
             }
 #pragma unroll
             for (int j = 0; j < 32; j += 2) {
@@ -474,7 +509,16 @@ __global__ void __launch_bounds__(kThreads, 1)
               v[32 * k2 + j + 1] = o.y;
             }
           }
-          store_chunk(v, col_base + c, m0 + q * 32);
+          if (ep.C8) {  // e4m3 codes at the tensor's static scale, direct stores
+            if (live) {
+              uint8_t* dst = ep.C8 + (int64_t)row * ep.ldc + col_base + c;
+              store_e4m3x32(dst, v, inv8);
+              store_e4m3x32(dst + 32, v + 32, inv8);
+              if (nb == 0 && c == 0) ep.c8_rowscale[row] = s8;
+            }
+          } else {
+            store_chunk(v, col_base + c, m0 + q * 32);
+          }
         }
       } else if (EPI == TC_GEGLU) {
         constexpr int HALF = BN / 2;    // output columns of the tile
@@ -485,8 +529,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld32(tacc + HALF + c, r1);
           tmem_ld_wait();
           if constexpr (F8) {
-            unscale32(r0, sa, ep.sw + col_base + c);
-            unscale32(r1, sa, ep.sw + up_row0 + col_base + c);
+            unscale32(r0, sa, ep.sw + col_base + c, su);
+            unscale32(r1, sa, ep.sw + up_row0 + col_base + c, su);
           }
           float v[32];
 #pragma unroll
@@ -496,7 +540,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             v[j] = o.x;
             v[j + 1] = o.y;
           }
-          if (live) store_bf16x32(ep.C + (int64_t)row * ep.ldc + col_base + c, v);
+          if (live && ep.C8) {
+            store_e4m3x32(ep.C8 + (int64_t)row * ep.ldc + col_base + c, v, inv8);
+            if (nb == 0 && c == 0) ep.c8_rowscale[row] = s8;
+          } else if (live) {
+            store_bf16x32(ep.C + (int64_t)row * ep.ldc + col_base + c, v);
+          }
         }
       } else if (EPI == TC_ROPE) {
         constexpr int HEADS = BN / 64;
@@ -517,11 +566,22 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int h2 = 0; h2 < 2; ++h2) {
               uint32_t a[16], z[16];
+              // the channel scales are requested before the TMEM loads, so
+              // that the two latencies overlap
+              float4 wa[4], wz[4];
+              if (su == 0.f) {
+                const float4* pa = reinterpret_cast<const float4*>(ep.sw + col_base + c + 16 * h2);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                  wa[k] = __ldg(pa + k);
+                  wz[k] = __ldg(pa + 8 + k);
+                }
+              }
               tmem_ld16(tacc + c + 16 * h2, a);
               tmem_ld16(tacc + c + 32 + 16 * h2, z);
               tmem_ld_wait();
-              unscale16(a, sa, ep.sw + col_base + c + 16 * h2);
-              unscale16(z, sa, ep.sw + col_base + c + 32 + 16 * h2);
+              unscale16w(a, sa, wa, su);
+              unscale16w(z, sa, wz, su);
               float va[16], vz[16];
 #pragma unroll
               for (int j = 0; j < 16; ++j) {
@@ -599,6 +659,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0) { record_err(ep.err, 7); abort_sh = 1; }
             break;
           }
+          if constexpr (F8) unscale32(acc[k], sa, ep.sw + xcol + 32 * k, su);  // e4m3 operands
           uint8_t* rowp = stg + (k & 1) * 4096 + lane * 128;
           const float4* bias4 =
               ep.bias ? reinterpret_cast<const float4*>(ep.bias + xcol + 32 * k) : nullptr;
@@ -654,6 +715,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tmem_ld32(tacc + c0 + 32 * k, r0);
           tmem_ld_wait();
+          if constexpr (F8) unscale32(r0, sa, ep.sw + nb * BN + c0 + 32 * k, su);
           if (live) {
             const float* bk = ep.bias ? ep.bias + nb * BN + c0 + 32 * k : nullptr;
 #pragma unroll
@@ -685,7 +747,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int k2 = 0; k2 < 2; ++k2) {
             tmem_ld32(tacc + c + 32 * k2, r0);
             tmem_ld_wait();
-            if constexpr (F8) unscale32(r0, sa, ep.sw + col_base + c + 32 * k2);
+            if constexpr (F8) unscale32(r0, sa, ep.sw + col_base + c + 32 * k2, su);
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
               float a = __uint_as_float(r0[j]);
@@ -702,7 +764,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld32(tacc + c, r0);
           tmem_ld_wait();
           if (!live) continue;
-          if constexpr (F8) unscale32(r0, sa, ep.sw + col_base + c);
+          if constexpr (F8) unscale32(r0, sa, ep.sw + col_base + c, su);
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
@@ -849,12 +911,12 @@ cudaError_t gemm_tc_take_status(int* code) {
 
 bool gemm_tc_f8_supported(int M, int N, int K, int epi) {
   if (M <= 0 || K < 2 * BK || K % (2 * BK) != 0 || N % 64 != 0) return false;
-  return epi == TC_STORE || epi == TC_GEGLU || epi == TC_ROPE;
+  return epi == TC_STORE || epi == TC_GEGLU || epi == TC_ROPE || epi == TC_RESID;
 }
 
 cudaError_t gemm_tc_f8(const uint8_t* A, const uint8_t* W, const float* sa, const float* sw,
                        const float* bias, bf16* C, int M, int N, int K, int epi, int act,
-                       TcRope rope, int* err, cudaStream_t st) {
+                       TcRope rope, int* err, cudaStream_t st, float* resid, TcQ8 q8) {
   if (!gemm_tc_f8_supported(M, N, K, epi) || !sa || !sw) return cudaErrorInvalidValue;
   if (reinterpret_cast<uintptr_t>(sw) & 15) return cudaErrorInvalidValue;
   EpiArgs ep{};
@@ -868,9 +930,18 @@ cudaError_t gemm_tc_f8(const uint8_t* A, const uint8_t* W, const float* sa, cons
   ep.rope_cols = 2 * rope.H * 64;
   ep.sa = sa;
   ep.sw = sw;
+  ep.resid = resid;
+  ep.ldr = N;
+  ep.C8 = q8.C;
+  ep.c8_scale = q8.scale;
+  ep.c8_rowscale = q8.rowscale;
+  ep.uniform = q8.uniform ? 1 : 0;
   ep.err = err;
+  if (epi == TC_RESID && !resid) return cudaErrorInvalidValue;
+  if (q8.C && (epi != TC_GEGLU || !q8.scale || !q8.rowscale)) return cudaErrorInvalidValue;
   switch (epi) {
     case TC_STORE: return dispatch_bn<TC_STORE, true>(A, W, M, N, K, N, ep, st);
+    case TC_RESID: return dispatch_bn<TC_RESID, true>(A, W, M, N, K, N, ep, st);
     case TC_GEGLU: return dispatch_bn<TC_GEGLU, true>(A, W, M, N, K, 2 * N, ep, st);
     case TC_ROPE: return dispatch_bn<TC_ROPE, true>(A, W, M, N, K, N, ep, st);
   }

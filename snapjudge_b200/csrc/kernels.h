@@ -119,13 +119,26 @@ cudaError_t gemm_tc(const bf16* A, const bf16* W, const float* bias, bf16* C, fl
 // The FP8 variant (tcgen05 kind::f8f6f4): A [M, K] and W [N_w, K] are e4m3
 // codes with a scale per A row (sa [M]) and per W row (sw [N_w], 16-byte
 // aligned); acc = sa[m] sw[n] sum_k A[m, k] W[n, k] in fp32, then the epilogue
-// as gemm_tc.  Epilogues TC_STORE, TC_GEGLU, TC_ROPE; K % 128 == 0.
+// as gemm_tc.  Epilogues TC_STORE, TC_GEGLU, TC_ROPE, TC_RESID; K % 128 == 0.
 // As attn_tc_take_status, for the GEMM launches given no error flag.
 cudaError_t gemm_tc_take_status(int* code);
 bool gemm_tc_f8_supported(int M, int N, int K, int epi);
+// SJ_PREC_FP8_TENSOR options.  C set: GEGLU output as e4m3 codes at one static
+// scale, C gets e4m3(gelu(g) u / *scale) [M, N] bytes, rowscale[m] = *scale,
+// bf16 C unused.  uniform: sa and sw hold one value each (per-tensor scales),
+// so the epilogue multiplies by sa[0] * sw[0] without per-row or per-column
+// scale loads.
+struct TcQ8 {
+  uint8_t* C = nullptr;
+  const float* scale = nullptr;
+  float* rowscale = nullptr;
+  bool uniform = false;
+};
+// TC_RESID adds to the fp32 resid [M, N] (W the [N, K] output projection).
 cudaError_t gemm_tc_f8(const uint8_t* A, const uint8_t* W, const float* sa, const float* sw,
                        const float* bias, bf16* C, int M, int N, int K, int epi, int act,
-                       TcRope rope, int* err, cudaStream_t st);
+                       TcRope rope, int* err, cudaStream_t st, float* resid = nullptr,
+                       TcQ8 q8 = TcQ8{});
 
 // ---- e4m3 quantisation (quant.cu) --------------------------------------------
 // Per row: scale = amax / 448 (1 for an all-zero row), q = e4m3(x * (448 / amax))
@@ -137,6 +150,21 @@ cudaError_t quant_rows_e4m3(const T* x, int64_t rows, int cols, uint8_t* q, floa
 // D <= 1024): the FP8 variant's attn_norm / mlp_norm.
 cudaError_t ln_e4m3(const float* X, const float* w, const float* b, uint8_t* q, float* scale,
                     int64_t rows, int D, float eps, cudaStream_t st);
+// SJ_PREC_FP8_TENSOR: one static scale per activation tensor, read from device
+// memory (*s_t): LN(X) * w (+ b) (or, quant_rows_static, X itself) quantised as
+// x / s_t, and sa[row] = s_t for the GEMM epilogue.
+cudaError_t ln_e4m3_static(const float* X, const float* w, const float* b, uint8_t* q, float* sa,
+                           const float* s_t, int64_t rows, int D, float eps, cudaStream_t st);
+cudaError_t quant_rows_static(const float* x, int64_t rows, int cols, uint8_t* q, float* sa,
+                              const float* s_t, cudaStream_t st);
+// *amax = max(*amax, max |x|) (float bits in an unsigned; calibration)
+template <typename T>
+cudaError_t amax_abs(const T* x, int64_t n, unsigned* amax, cudaStream_t st);
+// s[i] = amax[i] * margin / 448, 1 where amax[i] == 0
+cudaError_t scales_from_amax(const unsigned* amax, float* s, int n, float margin, cudaStream_t st);
+// a weight with one scale per tensor: q = e4m3(x * 448 / amax), sw[0..rows) = amax / 448
+cudaError_t quant_tensor_e4m3(const float* x, int64_t n, int rows, float amax, uint8_t* q,
+                              float* sw, cudaStream_t st);
 
 // ---- tcgen05 flash attention (attn_tc.cu) -----------------------------------
 bool attn_tc_supported(int Dh);

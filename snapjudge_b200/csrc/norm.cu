@@ -8,6 +8,8 @@
 //
 // One warp per row, 16-byte loads: each lane owns D/128 float4 chunks
 // (D <= 1024 in registers).  Rows of other widths use a block-per-row kernel.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -267,6 +269,95 @@ __global__ void __launch_bounds__(256) ln_e4m3_warp(const float* __restrict__ X,
   if (lane == 0) scale[i] = sc;
 }
 
+// ---- e4m3 with one static scale per tensor (SJ_PREC_FP8_TENSOR) ----
+// The scale s is read from device memory (calibrated by the engine); every row
+// is quantised as x / s (RN, saturating) and its entry of the row-scale array
+// the GEMM epilogue reads is set to s.
+__device__ __forceinline__ float static_inv(float s) { return s > 0.f ? __fdiv_rn(1.f, s) : 0.f; }
+
+// LN(X) * w (+ b) as ln_e4m3_warp, quantised with the tensor's scale
+__global__ void __launch_bounds__(256) ln_e4m3_static_warp(const float* __restrict__ X,
+                                                           const float* __restrict__ w,
+                                                           const float* __restrict__ b,
+                                                           uint8_t* __restrict__ q,
+                                                           float* __restrict__ sa,
+                                                           const float* __restrict__ s_t,
+                                                           int64_t M, int D, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t i = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (i >= M) return;
+  const int nc4 = D >> 2;
+  float4 v[kMaxChunks];
+#pragma unroll
+  for (int k = 0; k < kMaxChunks; ++k) {
+    const int c = lane + 32 * k;
+    v[k] = c < nc4 ? load4<float>(X + i * D + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  float mean, invs;
+  row_stats(v, lane, nc4, D, eps, mean, invs);
+  const float st = *s_t, inv = static_inv(st);
+  uint32_t* qrow = reinterpret_cast<uint32_t*>(q + i * D);
+#pragma unroll
+  for (int k = 0; k < kMaxChunks; ++k) {
+    const int c = lane + 32 * k;
+    if (c >= nc4) break;
+    const float4 g = load4<float>(w + 4 * c);
+    float4 o = make_float4((v[k].x - mean) * invs * g.x, (v[k].y - mean) * invs * g.y,
+                           (v[k].z - mean) * invs * g.z, (v[k].w - mean) * invs * g.w);
+    if (b) {
+      const float4 bb = load4<float>(b + 4 * c);
+      o.x += bb.x; o.y += bb.y; o.z += bb.z; o.w += bb.w;
+    }
+    qrow[c] = e4m3x4(o, inv);
+  }
+  if (lane == 0) sa[i] = st;
+}
+
+// rows of x quantised with the tensor's scale (the identity norm of layer 0)
+__global__ void __launch_bounds__(256) quant_rows_static_kernel(const float* __restrict__ x,
+                                                                int64_t rows, int cols,
+                                                                uint8_t* __restrict__ q,
+                                                                float* __restrict__ sa,
+                                                                const float* __restrict__ s_t) {
+  const int lane = threadIdx.x & 31;
+  const int64_t i = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (i >= rows) return;
+  const float st = *s_t, inv = static_inv(st);
+  uint32_t* qrow = reinterpret_cast<uint32_t*>(q + i * cols);
+  for (int c = 4 * lane; c < cols; c += 128) qrow[c >> 2] = e4m3x4(load4<float>(x + i * cols + c), inv);
+  if (lane == 0) sa[i] = st;
+}
+
+// amax |x| over n values into *amax (float bits compared as unsigned, values >= 0)
+template <typename T>
+__global__ void __launch_bounds__(256) amax_kernel(const T* __restrict__ x, int64_t n,
+                                                   unsigned* __restrict__ amax) {
+  float m = 0.f;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    m = fmaxf(m, fabsf(static_cast<float>(x[i])));
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0 && m > 0.f) atomicMax(amax, __float_as_uint(m));
+}
+
+// s[i] = amax[i] * margin / 448 (1 where nothing was seen)
+__global__ void scales_from_amax_kernel(const unsigned* __restrict__ amax, float* __restrict__ s,
+                                        int n, float margin) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float a = __uint_as_float(amax[i]);
+  s[i] = a > 0.f ? __fdiv_rn(a * margin, 448.f) : 1.f;
+}
+
+// x quantised with one scale (weights, per tensor): q = e4m3(x * inv), and
+// the row-scale array filled with s
+__global__ void quant_tensor_kernel(const float* __restrict__ x, int64_t n4, float inv, float s,
+                                    uint8_t* __restrict__ q, float* __restrict__ sw, int rows) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n4) reinterpret_cast<uint32_t*>(q)[i] = e4m3x4(reinterpret_cast<const float4*>(x)[i], inv);
+  if (i < rows) sw[i] = s;
+}
+
 // ---- generic widths: one block per row, row staged in shared memory ----
 __device__ float block_sum(float v, float* red) {
   v = warp_sum(v);
@@ -395,6 +486,50 @@ cudaError_t ln_e4m3(const float* X, const float* w, const float* b, uint8_t* q, 
   if (rows <= 0) return cudaSuccess;
   if (D % 128 != 0 || D > 4 * 32 * kMaxChunks) return cudaErrorInvalidValue;
   ln_e4m3_warp<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(X, w, b, q, scale, rows, D, eps);
+  return cudaGetLastError();
+}
+
+cudaError_t ln_e4m3_static(const float* X, const float* w, const float* b, uint8_t* q, float* sa,
+                           const float* s_t, int64_t rows, int D, float eps, cudaStream_t st) {
+  if (rows <= 0) return cudaSuccess;
+  if (D % 128 != 0 || D > 4 * 32 * kMaxChunks) return cudaErrorInvalidValue;
+  ln_e4m3_static_warp<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(X, w, b, q, sa, s_t, rows, D,
+                                                                  eps);
+  return cudaGetLastError();
+}
+
+cudaError_t quant_rows_static(const float* x, int64_t rows, int cols, uint8_t* q, float* sa,
+                              const float* s_t, cudaStream_t st) {
+  if (rows <= 0) return cudaSuccess;
+  if (cols <= 0 || cols % 4 != 0) return cudaErrorInvalidValue;
+  quant_rows_static_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(x, rows, cols, q, sa, s_t);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t amax_abs(const T* x, int64_t n, unsigned* amax, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  const int64_t blocks = std::min<int64_t>((n + 255) / 256, 148 * 8);
+  amax_kernel<T><<<(unsigned)blocks, 256, 0, st>>>(x, n, amax);
+  return cudaGetLastError();
+}
+template cudaError_t amax_abs<float>(const float*, int64_t, unsigned*, cudaStream_t);
+template cudaError_t amax_abs<bf16>(const bf16*, int64_t, unsigned*, cudaStream_t);
+
+cudaError_t scales_from_amax(const unsigned* amax, float* s, int n, float margin,
+                             cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  scales_from_amax_kernel<<<(n + 255) / 256, 256, 0, st>>>(amax, s, n, margin);
+  return cudaGetLastError();
+}
+
+cudaError_t quant_tensor_e4m3(const float* x, int64_t n, int rows, float amax, uint8_t* q,
+                              float* sw, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  if (n % 4 != 0) return cudaErrorInvalidValue;
+  const float s = amax > 0.f ? amax / 448.f : 1.f, inv = amax > 0.f ? 448.f / amax : 0.f;
+  const int64_t n4 = n / 4, work = std::max<int64_t>(n4, rows);
+  quant_tensor_kernel<<<(unsigned)((work + 255) / 256), 256, 0, st>>>(x, n4, inv, s, q, sw, rows);
   return cudaGetLastError();
 }
 

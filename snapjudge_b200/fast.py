@@ -45,7 +45,8 @@ class FastSnapjudge:
         self.precision = precision
         self.D = cfg.hidden_size
         prec = {"bf16": _lib.SJ_PREC_BF16, "fp32": _lib.SJ_PREC_FP32,
-                "fp8": _lib.SJ_PREC_FP8}.get(precision, -1)
+                "fp8": _lib.SJ_PREC_FP8,
+                "fp8_tensor": _lib.SJ_PREC_FP8_TENSOR}.get(precision, -1)
         if isinstance(cfg, SjConfig):
             sl = None
             c = _lib.FastConfig(cfg.hidden_size, cfg.num_layers, cfg.num_heads,
@@ -61,7 +62,8 @@ class FastSnapjudge:
                                 cfg.rope_theta_sliding, prec, device, max_tokens,
                                 _lib.SJ_ARCH_MODERNBERT)
         if prec < 0:
-            raise ValueError(f"precision must be 'bf16', 'fp32' or 'fp8', got {precision!r}")
+            raise ValueError("precision must be 'bf16', 'fp32', 'fp8' or 'fp8_tensor', "
+                             f"got {precision!r}")
         h = C.c_void_p()
         rc = L.sj_fast_create(C.byref(c), C.byref(h))
         if rc != 0:

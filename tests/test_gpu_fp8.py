@@ -1,5 +1,7 @@
-"""The FP8 variant (SJ_PREC_FP8): e4m3 quantisation, the e4m3 tcgen05 GEMM, and
-the encoder with its QKV and Wi projections on e4m3 operands.
+"""The FP8 variants: e4m3 quantisation, the e4m3 tcgen05 GEMM, and the encoder
+with its QKV and Wi projections on e4m3 operands (SJ_PREC_FP8: per-token and
+per-channel scales) or its QKV, Wi and Wo2 projections (SJ_PREC_FP8_TENSOR:
+one scale per tensor, activation scales calibrated on the first pass).
 
 The reference has no FP8 path, so the kernels are checked against what they
 define, and the encoder against the fp32 CPU forward with a bar of its own:
@@ -220,3 +222,108 @@ def test_fp8_c4_architecture_and_passes():
     got, ids = _fp8_vs_oracle(spec.cfg, t, lengths, 94, rel_bar=0.12, cos_bar=0.994)
     again = FastSnapjudge(spec.cfg, t, precision="fp8", max_tokens=320).encode_packed(ids, lengths)
     assert np.array_equal(got, again)
+
+
+# ---- SJ_PREC_FP8_TENSOR: per-tensor scales, calibrated activation scales ----
+
+def _vs(got, want):
+    cos = np.sum(got * want, axis=1) / (np.linalg.norm(got, axis=1) * np.linalg.norm(want, axis=1))
+    return _rel(got, want), float(cos.min())
+
+
+def test_fp8_tensor_encoder_against_fp32_forward():
+    """The per-tensor variant (QKV, Wi and Wo2 on e4m3, one scale per weight
+    tensor, static activation scales from a calibration pass over this same
+    batch), C3 architecture, ragged batch of 8, against the fp32 forward with
+    the per-token variant's bars.  Measured on a B200: relative error 0.0375
+    (per-token 0.0309), smallest row cosine 0.9991."""
+    spec = synth.SPECS["c3"]
+    t = synth.make_weights(spec)
+    rng = np.random.default_rng(12)
+    lengths = np.array([300, 251, 177, 128, 96, 64, 17, 1])
+    ids = rng.integers(0, spec.cfg.vocab_size, size=int(lengths.sum())).astype(np.int64)
+    want = oracle.Oracle(spec.cfg, t).encode_packed(ids, lengths)
+    ht = FastSnapjudge(spec.cfg, t, precision="fp8_tensor").encode_packed(ids, lengths)
+    h8 = FastSnapjudge(spec.cfg, t, precision="fp8").encode_packed(ids, lengths)
+    assert np.isfinite(ht).all()
+    et, ct = _vs(ht, want)
+    e8, c8 = _vs(h8, want)
+    print(f"relative error: fp8_tensor {et:.4f} (min row cosine {ct:.5f}), "
+          f"fp8 {e8:.4f} ({c8:.5f})")
+    assert et <= 0.06 and ct >= 0.998
+
+
+def test_fp8_tensor_scales_fixed_after_first_pass():
+    """Calibration runs once, on the engine's first pass: the same batch again
+    gives identical states, and a later batch of other lengths and ids, run at
+    the first batch's scales, stays within the bars against the fp32 forward."""
+    spec = synth.SPECS["c3"]
+    t = synth.make_weights(spec)
+    rng = np.random.default_rng(21)
+    la = np.array([200, 150, 33, 9])
+    lb = np.array([511, 64, 2, 300, 120])
+    ia = rng.integers(0, spec.cfg.vocab_size, size=int(la.sum())).astype(np.int64)
+    ib = rng.integers(0, spec.cfg.vocab_size, size=int(lb.sum())).astype(np.int64)
+    eng = FastSnapjudge(spec.cfg, t, precision="fp8_tensor")
+    a1 = eng.encode_packed(ia, la)
+    hb = eng.encode_packed(ib, lb)
+    a2 = eng.encode_packed(ia, la)
+    assert np.array_equal(a1, a2)
+    e, c = _vs(hb, oracle.Oracle(spec.cfg, t).encode_packed(ib, lb))
+    print(f"second batch at the first batch's scales: relative error {e:.4f}, min cosine {c:.5f}")
+    assert e <= 0.06 and c >= 0.998
+
+
+def test_fp8_tensor_c4_architecture():
+    """C4 architecture (24 x 1024, F = 2816, a multiple of 128) in the
+    per-tensor variant, with the per-token variant's C4 bars.  Measured on a
+    B200: relative error 0.084 (per-token 0.069), smallest row cosine 0.9953."""
+    spec = synth.SPECS["c4"]
+    t = synth.make_weights(spec)
+    lengths = np.array([300, 77, 129])
+    ids = np.random.default_rng(94).integers(0, spec.cfg.vocab_size, size=int(lengths.sum()))
+    ids = ids.astype(np.int64)
+    want = oracle.Oracle(spec.cfg, t).encode_packed(ids, lengths)
+    got = FastSnapjudge(spec.cfg, t, precision="fp8_tensor").encode_packed(ids, lengths)
+    e, c = _vs(got, want)
+    print(f"fp8_tensor c4: relative error {e:.4f}, min row cosine {c:.5f}")
+    assert np.isfinite(got).all() and e <= 0.12 and c >= 0.994
+
+
+def test_fp8_tensor_needs_intermediate_multiple_of_128():
+    import dataclasses
+    spec = synth.SPECS["c3"]
+    cfg = dataclasses.replace(spec.cfg, intermediate_size=2048 - 64)
+    t = synth.make_weights(dataclasses.replace(spec, cfg=cfg))
+    with pytest.raises(SnapjudgeError):
+        FastSnapjudge(cfg, t, precision="fp8_tensor")
+    FastSnapjudge(cfg, t, precision="fp8").close()  # the per-token variant takes F % 64
+
+
+def test_fp8_variants_on_c5_heads():
+    """Config 5's four decision heads (choice3, choice8, score5, noul) on 64
+    requests of its length distribution: decision probabilities of the bf16
+    mode and both FP8 variants against the fp32 CPU forward and fp64 heads.
+    Bars: bf16 5e-3 (the bf16 probability bar), both FP8 variants 5e-2; the
+    [CLS] states within 0.06 relative.  Measured on a B200: probabilities
+    bf16 1.9e-3, fp8 2.4e-2, fp8_tensor 3.1e-2; [CLS] relative error 0.0025,
+    0.032, 0.039."""
+    spec = synth.SPECS["c5"]
+    t = synth.make_weights(spec)
+    lengths = synth.make_lengths(spec, batch=64, seed=515)
+    ids = synth.make_ids(spec, lengths, seed=516)
+    want_h = oracle.Oracle(spec.cfg, t).encode_packed(ids, lengths)
+    cls = synth.cu_seqlens(lengths)[:-1]
+    want = np.concatenate(oracle.task_heads(want_h[cls], t, spec.heads), axis=1)
+    res = {}
+    for prec in ("bf16", "fp8", "fp8_tensor"):
+        eng = FastSnapjudge(spec.cfg, t, precision=prec, heads=spec.heads)
+        p = eng.decide(ids, lengths)
+        h = eng.encode_packed(ids, lengths)[cls]
+        res[prec] = (float(np.abs(p - want).max()), _rel(h, want_h[cls]))
+        eng.close()
+    print("c5 heads, probability max-abs / [CLS] relative error: " +
+          ", ".join(f"{k} {v[0]:.2e} / {v[1]:.4f}" for k, v in res.items()))
+    assert res["bf16"][0] <= 5e-3
+    for k in ("fp8", "fp8_tensor"):
+        assert res[k][0] <= 5e-2 and res[k][1] <= 0.06, (k, res[k])
