@@ -724,6 +724,7 @@ def fp8_section(spec, weights, a, local, st, pass_args, probs_d, T, value_bf16):
                           "the first pass (amax x 2 / 448), fp32 accumulation; bf16 elsewhere "
                           "(SJ_PREC_FP8_TENSOR)"),
             "kernels": kern,
+            "kernels_ms_per_step": {k: v[0] / a.steps for k, v in prof.items()},
             "probs_max_abs_vs_bf16_on_bench_set": float((probs8 - probs_d).abs().max().item()),
             "probs_max_abs_vs_fp32": float(np.abs(probs_of(prec, eng8) - p32).max())}
         eng8.close()

@@ -161,6 +161,7 @@ struct sj_fast {
   uint8_t* Y8 = nullptr;  // SJ_PREC_FP8: LN output as e4m3 [max_tokens, D]
   float* sa8 = nullptr;   //   and its row scales [max_tokens]
   uint8_t* G8 = nullptr;  // SJ_PREC_FP8_TENSOR: GEGLU output as e4m3 [max_tokens, F]
+  bf16* Xh = nullptr;     //   its residual stream, bf16 [max_tokens, D]
   float* sg8 = nullptr;   //   and its row scales [max_tokens]
   int* dflags = nullptr;  // device error flags: [0] bad id, [1] gemm wait, [2] attn wait
   // pinned host staging
@@ -509,6 +510,7 @@ int sj_fast::commit() {
       (rc = dalloc(&hid, T * D)) || (rc = dalloc(&z, T * (size_t)std::max(1, lora_r))) ||
       (rc = dalloc(&dflags, 8)) || (fp8 && ((rc = dalloc(&Y8, T * D)) || (rc = dalloc(&sa8, T)))) ||
       (fp8_tensor && ((rc = dalloc(&G8, T * F)) || (rc = dalloc(&sg8, T)) ||
+                      (rc = dalloc(&Xh, T * D)) ||
                       (rc = dalloc(&act_scale, 3 * (size_t)NL)) ||
                       (rc = dalloc(&act_amax, 3 * (size_t)NL)))))
     return cuda_fail(rc, "cudaMalloc (workspace)");
@@ -700,11 +702,22 @@ int sj_fast::forward(const int64_t* d_ids, const int32_t* d_cu, const int32_t* h
   T* Gt = static_cast<T*>(G);
   const float eps = cfg.norm_eps;
   SJ_LAUNCH(SJ_K_FINAL, sjb::positions(d_cu, B, ntok, pos, nullptr, st));
-  const bool y0 = !layers.empty() && !layers[0].attn_norm;
-  SJ_LAUNCH(SJ_K_EMBED, sjb::embed_ln<T>(d_ids, ntok, emb, V, D, emb_norm, eps, X, y0 ? Yt : nullptr,
-                                         dflags, st, pos_emb, pos, cfg.max_position_embeddings,
-                                         emb_norm_b));
   const bool sjm = arch == SJ_ARCH_SJMODEL;
+  // SJ_PREC_FP8: the attn_norm and mlp_norm outputs are e4m3 rows with their
+  // scales (Y8, sa8), the QKV and Wi GEMMs run on the e4m3 weights.
+  // SJ_PREC_FP8_TENSOR: the same with one static scale per activation tensor
+  // (act_scale); the GEGLU GEMM writes e4m3 codes (G8) for an e4m3 Wo2, and
+  // the residual stream is bf16 (Xh: written by the embedding, updated by the
+  // Wo and Wo2 epilogues, widened to fp32 X for the final norm).  Its
+  // calibration pass runs the bf16 path and records each e4m3 operand's amax
+  // (act_amax).
+  const bool f8 = kBf16 && fp8 && !sjm && !calibrating;
+  const bool f8t = f8 && fp8_tensor;
+  const bool y0 = !layers.empty() && !layers[0].attn_norm;
+  T* y_emb = f8t ? reinterpret_cast<T*>(Xh) : (y0 ? Yt : nullptr);
+  SJ_LAUNCH(SJ_K_EMBED, sjb::embed_ln<T>(d_ids, ntok, emb, V, D, emb_norm, eps, X, y_emb, dflags,
+                                         st, pos_emb, pos, cfg.max_position_embeddings,
+                                         emb_norm_b));
 
   auto gemm = [&](int cls, const T* A, const void* W, T* C, float* resid, int N, int K, int epi,
                   const float* ct, const float* stb, const float* bias = nullptr,
@@ -712,24 +725,17 @@ int sj_fast::forward(const int64_t* d_ids, const int32_t* d_cu, const int32_t* h
     return gemm_any<T>(cls, A, W, bias, act, C, resid, ntok, N, K, epi, ct, stb, st);
   };
 
-  // SJ_PREC_FP8: the attn_norm and mlp_norm outputs are e4m3 rows with their
-  // scales (Y8, sa8), the QKV and Wi GEMMs run on the e4m3 weights.
-  // SJ_PREC_FP8_TENSOR: the same with one static scale per activation tensor
-  // (act_scale), and the GEGLU GEMM writes e4m3 codes (G8) for an e4m3 Wo2.
-  // Its calibration pass runs the bf16 path and records each of those
-  // tensors' amax (act_amax).
-  const bool f8 = kBf16 && fp8 && !sjm && !calibrating;
-  const bool f8t = f8 && fp8_tensor;
   int s;
   for (int li = 0; li < NL; ++li) {
     const LayerDev& ly = layers[li];
     const T* Yin = Yt;
     if (f8t) {
       if (ly.attn_norm)
-        SJ_LAUNCH(SJ_K_LN, sjb::ln_e4m3_static(X, ly.attn_norm, ly.attn_norm_b, Y8, sa8,
-                                               act_scale + 3 * li, ntok, D, eps, st));
+        SJ_LAUNCH(SJ_K_LN, sjb::ln_e4m3_static<bf16>(Xh, ly.attn_norm, ly.attn_norm_b, Y8, sa8,
+                                                     act_scale + 3 * li, ntok, D, eps, st));
       else
-        SJ_LAUNCH(SJ_K_LN, sjb::quant_rows_static(X, ntok, D, Y8, sa8, act_scale + 3 * li, st));
+        SJ_LAUNCH(SJ_K_LN,
+                  sjb::quant_rows_static<bf16>(Xh, ntok, D, Y8, sa8, act_scale + 3 * li, st));
     } else if (f8) {
       if (ly.attn_norm)
         SJ_LAUNCH(SJ_K_LN, sjb::ln_e4m3(X, ly.attn_norm, ly.attn_norm_b, Y8, sa8, ntok, D, eps, st));
@@ -783,11 +789,18 @@ int sj_fast::forward(const int64_t* d_ids, const int32_t* d_cu, const int32_t* h
     } else {
       SJ_LAUNCH(SJ_K_ATTN, sjb::attn_simt<T>(Qt, d_cu, d_kvl, Ot, H, Dh, ly.window, tiles, nt, B, 0, st));
     }
-    if ((s = gemm(SJ_K_WO, Ot, ly.wo, nullptr, X, D, D, sjb::TC_RESID, nullptr, nullptr, ly.bo)))
+    if (f8t) {
+      if constexpr (kBf16)
+        SJ_LAUNCH(SJ_K_WO, sjb::gemm_tc(Ot, static_cast<const bf16*>(ly.wo), ly.bo, Xh, nullptr, ntok, D,
+                                        D, sjb::TC_RESID16, 0,
+                                        sjb::TcRope{}, dflags + 1, st));
+    } else if ((s = gemm(SJ_K_WO, Ot, ly.wo, nullptr, X, D, D, sjb::TC_RESID, nullptr, nullptr,
+                         ly.bo))) {
       return s;
+    }
     if (f8t)
-      SJ_LAUNCH(SJ_K_LN, sjb::ln_e4m3_static(X, ly.mlp_norm, ly.mlp_norm_b, Y8, sa8,
-                                             act_scale + 3 * li + 1, ntok, D, eps, st));
+      SJ_LAUNCH(SJ_K_LN, sjb::ln_e4m3_static<bf16>(Xh, ly.mlp_norm, ly.mlp_norm_b, Y8, sa8,
+                                                   act_scale + 3 * li + 1, ntok, D, eps, st));
     else if (f8)
       SJ_LAUNCH(SJ_K_LN, sjb::ln_e4m3(X, ly.mlp_norm, ly.mlp_norm_b, Y8, sa8, ntok, D, eps, st));
     else
@@ -827,8 +840,9 @@ int sj_fast::forward(const int64_t* d_ids, const int32_t* d_cu, const int32_t* h
       if constexpr (kBf16) {
         sjb::TcQ8 uq;
         uq.uniform = true;
-        SJ_LAUNCH(SJ_K_WO2, sjb::gemm_tc_f8(G8, ly.wo2_8, sg8, ly.so2, ly.b2, nullptr, ntok, D, F,
-                                            sjb::TC_RESID, 0, sjb::TcRope{}, dflags + 1, st, X, uq));
+        SJ_LAUNCH(SJ_K_WO2, sjb::gemm_tc_f8(G8, ly.wo2_8, sg8, ly.so2, ly.b2, Xh, ntok, D, F,
+                                            sjb::TC_RESID16, 0, sjb::TcRope{}, dflags + 1, st,
+                                            nullptr, uq));
       }
     } else if ((s = gemm(SJ_K_WO2, Gt, ly.wo2, nullptr, X, D, F, sjb::TC_RESID, nullptr, nullptr,
                          ly.b2))) {
@@ -836,6 +850,10 @@ int sj_fast::forward(const int64_t* d_ids, const int32_t* d_cu, const int32_t* h
     }
   }
   // final norm (+ LoRA): all rows -> d_hidden, [CLS] rows -> heads
+  if (f8t) {  // the bf16 residual stream to fp32: every row, or only the [CLS] rows
+    if (d_hidden) SJ_LAUNCH(SJ_K_FINAL, sjb::widen_f32(Xh, X, (int64_t)ntok * D, st));
+    else if (d_probs && has_heads) SJ_LAUNCH(SJ_K_FINAL, sjb::widen_rows_f32(Xh, X, d_cu, B, D, st));
+  }
   if (d_hidden) {
     SJ_LAUNCH(SJ_K_FINAL, (sjb::add_ln<float, float>(X, nullptr, final_norm, final_norm_b, d_hidden, ntok,
                                                      D, eps, nullptr, st)));

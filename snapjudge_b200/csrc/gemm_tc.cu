@@ -42,8 +42,18 @@ namespace {
 using namespace tc;
 
 constexpr int BM = 128, BK = 64;
-constexpr int kEpiWarps = 8;
-constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kEpiWarps = 8;  // epilogue warps of every instance but TC_GEGLU8's
+// GEGLU with e4m3 output codes (SJ_PREC_FP8_TENSOR's Wi projection): an
+// instance of its own with 16 epilogue warps, 32 output columns each, and no
+// staging buffers.  Its epilogue is short of registers, not of work, so twice
+// the warps hide twice the TMEM-load and arithmetic latency.
+constexpr int TC_GEGLU8 = 5;
+template <int EPI>
+__host__ __device__ constexpr bool is_geglu() { return EPI == TC_GEGLU || EPI == TC_GEGLU8; }
+template <int EPI>
+__host__ __device__ constexpr int epi_warps() { return EPI == TC_GEGLU8 ? 16 : kEpiWarps; }
+template <int EPI>
+__host__ __device__ constexpr int threads_for() { return 64 + 32 * epi_warps<EPI>(); }
 
 struct EpiArgs {
   const float* bias;
@@ -73,7 +83,9 @@ struct EpiArgs {
 // TMA loads (two in flight), updated, and written back with TMA.  GEGLU on
 // 128-column tiles (32 outputs per warp) and 64-column tiles store directly.
 template <int BN, int EPI>
-__host__ __device__ constexpr bool staged() { return BN == 256 || (BN == 128 && EPI != TC_GEGLU); }
+__host__ __device__ constexpr bool staged() {
+  return EPI != TC_GEGLU8 && (BN == 256 || (BN == 128 && EPI != TC_GEGLU));
+}
 constexpr int kStageBytesPerWarp = 2 * 32 * 128;
 template <int BN, int EPI>
 __host__ __device__ constexpr int out_bytes() { return staged<BN, EPI>() ? kEpiWarps * kStageBytesPerWarp : 0; }
@@ -173,6 +185,13 @@ __device__ __forceinline__ void store_e4m3x32(uint8_t* dst, const float* v, floa
   d[0] = make_uint4(w[0], w[1], w[2], w[3]);
   d[1] = make_uint4(w[4], w[5], w[6], w[7]);
 }
+// four values to four e4m3 codes (RN, saturating) in memory order
+__device__ __forceinline__ uint32_t e4m3x4(float a, float b, float c, float d) {
+  uint16_t lo, hi;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(lo) : "f"(b), "f"(a));
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(hi) : "f"(d), "f"(c));
+  return (uint32_t)lo | ((uint32_t)hi << 16);
+}
 __device__ __forceinline__ void store_bf16x32(bf16* dst, const float* v) {
   uint4* d = reinterpret_cast<uint4*>(dst);
 #pragma unroll
@@ -232,7 +251,7 @@ __device__ __forceinline__ uint4 pack_bf16x8(const float* v) {
 }
 
 template <int BN, int EPI, bool PAIR, bool F8>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(threads_for<EPI>(), 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
                    const __grid_constant__ CUtensorMap mapC, int M, int n_tiles, int K, int up_row0,
                    EpiArgs ep) {
@@ -241,7 +260,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int STAGES = stages_for<BN, EPI, PAIR>();
   constexpr bool STAGED = staged<BN, EPI>();
   // the residual epilogue releases the accumulator as soon as it is in registers
-  constexpr bool EARLY = EPI == TC_RESID && STAGED;
+  constexpr bool EARLY = (EPI == TC_RESID || EPI == TC_RESID16) && STAGED;
   constexpr int BROWS = PAIR ? BN / 2 : BN;  // B rows this CTA loads per stage
   constexpr int A_BYTES = BM * BK * 2;
   constexpr int B_BYTES = BROWS * BK * 2;
@@ -253,7 +272,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t full_bar[STAGES], empty_bar[STAGES], tfull_bar[2], tempty_bar[2], drain_bar;
-  __shared__ uint64_t xload_bar[kEpiWarps][2];  // residual chunk loads (RESID epilogue)
+  constexpr int EPI_WARPS = epi_warps<EPI>();
+  __shared__ uint64_t xload_bar[EPI_WARPS][2];  // residual chunk loads (RESID epilogue)
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_sh;
 
@@ -273,10 +293,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull_bar[b], 1);
-      mbar_init(&tempty_bar[b], kEpiWarps * (PAIR ? 2 : 1));
+      mbar_init(&tempty_bar[b], EPI_WARPS * (PAIR ? 2 : 1));
     }
     mbar_init(&drain_bar, 1);
-    for (int w = 0; w < kEpiWarps; ++w) {
+    for (int w = 0; w < EPI_WARPS; ++w) {
       mbar_init(&xload_bar[w][0], 1);
       mbar_init(&xload_bar[w][1], 1);
     }
@@ -316,13 +336,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t bar0 = mapa_shared(smem_u32(&full_bar[stage]), 0);
           if (rank == 0) mbar_expect_tx(&full_bar[stage], 2 * STAGE_BYTES);
           tma_load_2d_pair(sa, &mapA, bar0, kb * BKE, m0);
-          const int brow = EPI == TC_GEGLU ? (rank == 0 ? nb * BROWS : up_row0 + nb * BROWS)
+          const int brow = is_geglu<EPI>() ? (rank == 0 ? nb * BROWS : up_row0 + nb * BROWS)
                                            : nb * BN + (int)rank * BROWS;
           tma_load_2d_pair(sb, &mapB, bar0, kb * BKE, brow);
         } else {
           mbar_expect_tx(&full_bar[stage], STAGE_BYTES);
           tma_load_2d(sa, &mapA, &full_bar[stage], kb * BKE, m0);
-          if (EPI == TC_GEGLU) {
+          if (is_geglu<EPI>()) {
             tma_load_2d(sb, &mapB, &full_bar[stage], kb * BKE, nb * (BN / 2));
             tma_load_2d(sb + B_BYTES / 2, &mapB, &full_bar[stage], kb * BKE,
                         up_row0 + nb * (BN / 2));
@@ -443,10 +463,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (EARLY && lane == 0) {
         // request this tile's first two X chunks while its MMAs still run
         bulk_wait_read<0>();  // the previous tile's stores have read both buffers
+        // chunks of 32 rows x 128 bytes: 32 fp32 or (TC_RESID16) 64 bf16 columns
+        constexpr int XW = EPI == TC_RESID16 ? 64 : 32;
 #pragma unroll
-        for (int k = 0; k < 2 && k < BN / 64; ++k) {
+        for (int k = 0; k < 2 && k < BN / 2 / XW; ++k) {
           mbar_expect_tx(&xb[k], 32 * 128);
-          tma_load_2d(stg + k * 4096, &mapC, &xb[k], nb * BN + hf * BN / 2 + 32 * k, m0 + q * 32);
+          tma_load_2d(stg + k * 4096, &mapC, &xb[k], nb * BN + hf * BN / 2 + XW * k, m0 + q * 32);
         }
       }
       // RoPE: this row's cos/sin (32 each, 16-byte loads), fetched before the
@@ -486,7 +508,37 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_after_sync();
       const uint32_t tacc = tmem_base + ((uint32_t)(q * 32) << 16) + b * BN;
       uint32_t r0[32], r1[32];
-      if (EPI == TC_GEGLU && STAGED) {
+      if constexpr (EPI == TC_GEGLU8) {
+        // this warp: rows q*32 .. q*32+31 of the CTA's 128, output columns
+        // hf*32 .. hf*32+31 of the tile's HALF (gate at c, up at HALF + c);
+        // codes packed as they are made, 32 bytes per row
+        constexpr int HALF = BN / 2;
+        static_assert(HALF == 4 * 32, "TC_GEGLU8 runs on 256-column tiles");
+        const int c = hf * 32, col = nb * HALF + c;
+        tmem_ld32(tacc + c, r0);
+        tmem_ld32(tacc + HALF + c, r1);
+        tmem_ld_wait();
+        release(b);  // the accumulator is in registers
+        if constexpr (F8) {
+          unscale32(r0, sa, ep.sw + col, su);
+          unscale32(r1, sa, ep.sw + up_row0 + col, su);
+        }
+        uint32_t w[8];
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          const float2 o0 = geglu_pair(__uint_as_float(r0[j]), __uint_as_float(r0[j + 1]),
+                                       __uint_as_float(r1[j]), __uint_as_float(r1[j + 1]));
+          const float2 o1 = geglu_pair(__uint_as_float(r0[j + 2]), __uint_as_float(r0[j + 3]),
+                                       __uint_as_float(r1[j + 2]), __uint_as_float(r1[j + 3]));
+          w[j / 4] = e4m3x4(o0.x * inv8, o0.y * inv8, o1.x * inv8, o1.y * inv8);
+        }
+        if (live) {
+          uint4* d = reinterpret_cast<uint4*>(ep.C8 + (int64_t)row * ep.ldc + col);
+          d[0] = make_uint4(w[0], w[1], w[2], w[3]);
+          d[1] = make_uint4(w[4], w[5], w[6], w[7]);
+          if (nb == 0 && hf == 0) ep.c8_rowscale[row] = s8;
+        }
+      } else if (EPI == TC_GEGLU && STAGED) {
         constexpr int HALF = BN / 2;    // output columns of the tile
         const int col_base = nb * HALF;
 #pragma unroll 1
@@ -695,6 +747,82 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
+      } else if constexpr (EPI == TC_RESID16) {
+        // bf16 X += acc (+ bias) through TMA, as the fp32 path above with
+        // chunks of 32 rows x 64 bf16 columns (the same 4 KB swizzled
+        // buffers); each chunk takes two 32-column accumulator pieces
+        constexpr int NCH = BN / 64;   // 32-column accumulator pieces in this warp's half
+        constexpr int NX = BN / 128;   // 64-column X chunks in this warp's half (<= 2)
+        static_assert(NX >= 1 && NX <= 2, "TC_RESID16 runs on 128- or 256-column tiles");
+        const int c0 = hf * BN / 2;
+        const int xcol = nb * BN + c0, xrow = m0 + q * 32;
+        uint32_t acc[NCH][32];
+#pragma unroll
+        for (int k = 0; k < NCH; ++k) tmem_ld32(tacc + c0 + 32 * k, acc[k]);
+        tmem_ld_wait();
+        release(b);
+#pragma unroll
+        for (int k = 0; k < NX; ++k) {
+          int okx = 1;
+          if (lane == 0) okx = mbar_wait<true>(&xb[k], (xphase >> k) & 1u) ? 1 : 0;
+          okx = __shfl_sync(0xffffffffu, okx, 0);
+          xphase ^= 1u << k;
+          if (!okx) {
+            if (lane == 0) { record_err(ep.err, 7); abort_sh = 1; }
+            break;
+          }
+          uint8_t* rowp = stg + k * 4096 + lane * 128;
+          const float* bias = ep.bias ? ep.bias + xcol + 64 * k : nullptr;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {  // 16-byte cell c: columns 8c .. 8c+7 of the chunk
+            uint4* cell = reinterpret_cast<uint4*>(rowp + ((c ^ (lane & 7)) << 4));
+            uint4 o = *cell;
+            uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+            const uint32_t* a = acc[2 * k + (c >> 2)] + 8 * (c & 3);
+            float bv[8], mul[8];
+            if constexpr (F8) {  // e4m3 operands: row x channel scales, per cell
+              if (su != 0.f) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) mul[e] = su;
+              } else {
+                const float4 w0 = __ldg(reinterpret_cast<const float4*>(ep.sw + xcol + 64 * k + 8 * c));
+                const float4 w1 = __ldg(reinterpret_cast<const float4*>(ep.sw + xcol + 64 * k + 8 * c + 4));
+                mul[0] = sa * w0.x; mul[1] = sa * w0.y; mul[2] = sa * w0.z; mul[3] = sa * w0.w;
+                mul[4] = sa * w1.x; mul[5] = sa * w1.y; mul[6] = sa * w1.z; mul[7] = sa * w1.w;
+              }
+            }
+            if (bias) {
+              const float4 b0 = *reinterpret_cast<const float4*>(bias + 8 * c);
+              const float4 b1 = *reinterpret_cast<const float4*>(bias + 8 * c + 4);
+              bv[0] = b0.x; bv[1] = b0.y; bv[2] = b0.z; bv[3] = b0.w;
+              bv[4] = b1.x; bv[5] = b1.y; bv[6] = b1.z; bv[7] = b1.w;
+            } else {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) bv[e] = 0.f;
+            }
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              __nv_bfloat162 x = *reinterpret_cast<__nv_bfloat162*>(&ow[e]);
+              const float2 xf = __bfloat1622float2(x);
+              float a0 = __uint_as_float(a[2 * e]), a1 = __uint_as_float(a[2 * e + 1]);
+              if constexpr (F8) {
+                a0 *= mul[2 * e];
+                a1 *= mul[2 * e + 1];
+              }
+              const float s0 = xf.x + (a0 + bv[2 * e]);
+              const float s1 = xf.y + (a1 + bv[2 * e + 1]);
+              __nv_bfloat162 r = __floats2bfloat162_rn(s0, s1);
+              ow[e] = *reinterpret_cast<uint32_t*>(&r);
+            }
+            *cell = o;
+          }
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&mapC, stg + k * 4096, xcol + 64 * k, xrow);
+            bulk_commit();
+          }
+        }
       } else if (EPI == TC_RESID) {
         // narrow tiles: X += acc with direct loads and stores, the next
         // chunk's residual loads in flight while the current one is added
@@ -775,7 +903,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           store_bf16x32(ep.C + (int64_t)row * ep.ldc + col_base + c, v);
         }
       }
-      if constexpr (!EARLY) release(b);
+      if constexpr (!EARLY && EPI != TC_GEGLU8) release(b);
     }
     if (STAGED && lane == 0) bulk_wait_all();  // staged stores done before the CTA exits
   }
@@ -801,7 +929,7 @@ cudaError_t launch(const void* A, const void* W, int M, int N_out, int K, int w_
   if (cudaError_t rc = ensure_smem_attr(gemm_tc_kernel<BN, EPI, PAIR, F8>, SMEM, attr_done))
     return rc;
   CUtensorMap ma, mb, mc;
-  const int b_box = PAIR ? BROWS : (EPI == TC_GEGLU ? BN / 2 : BN);
+  const int b_box = PAIR ? BROWS : (is_geglu<EPI>() ? BN / 2 : BN);
   if (F8) {
     if (!make_map_u8(&ma, A, K, M, (uint64_t)K, 2 * BK, BM) ||
         !make_map_u8(&mb, W, K, w_rows, (uint64_t)K, 2 * BK, b_box))
@@ -818,21 +946,21 @@ cudaError_t launch(const void* A, const void* W, int M, int N_out, int K, int w_
   } else {
     mc = ma;  // unused
   }
-  const int out_tile = EPI == TC_GEGLU ? BN / 2 : BN;
+  const int out_tile = is_geglu<EPI>() ? BN / 2 : BN;
   const int n_tiles = N_out / out_tile;
   const int tile_m = PAIR ? 2 * BM : BM;
   const int tiles = ((M + tile_m - 1) / tile_m) * n_tiles;
-  const int up_row0 = EPI == TC_GEGLU ? N_out : 0;
+  const int up_row0 = is_geglu<EPI>() ? N_out : 0;
   if (!PAIR) {
     const int grid = std::min(tiles, sm_count());
-    gemm_tc_kernel<BN, EPI, false, F8><<<grid, kThreads, SMEM, st>>>(ma, mb, mc, M, n_tiles, K,
+    gemm_tc_kernel<BN, EPI, false, F8><<<grid, threads_for<EPI>(), SMEM, st>>>(ma, mb, mc, M, n_tiles, K,
                                                                       up_row0, ep);
     return cudaGetLastError();
   }
   const int pairs = std::min(tiles, sm_count() / 2);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs, 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3(threads_for<EPI>(), 1, 1);
   cfg.dynamicSmemBytes = SMEM;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -852,19 +980,32 @@ constexpr int kPairMinRows = 2048;
 template <int EPI, bool F8 = false>
 cudaError_t dispatch_bn(const void* A, const void* W, int M, int N, int K, int w_rows, EpiArgs ep,
                         cudaStream_t st) {
-  if (EPI == TC_GEGLU) {
-    if (N % 128 == 0) {
+  if constexpr (EPI == TC_GEGLU8) {  // 256-column tiles only
+    if (N % 128 != 0) return cudaErrorInvalidValue;
+    if (M >= kPairMinRows) return launch<256, EPI, true, F8>(A, W, M, N, K, w_rows, ep, st);
+    return launch<256, EPI, false, F8>(A, W, M, N, K, w_rows, ep, st);
+  } else if constexpr (EPI == TC_RESID16) {  // staged tiles only: 256 or 128 columns
+    if (N % 256 == 0) {
       if (M >= kPairMinRows) return launch<256, EPI, true, F8>(A, W, M, N, K, w_rows, ep, st);
       return launch<256, EPI, false, F8>(A, W, M, N, K, w_rows, ep, st);
     }
-    return launch<128, EPI, false, F8>(A, W, M, N, K, w_rows, ep, st);
+    if (N % 128 == 0) return launch<128, EPI, false, F8>(A, W, M, N, K, w_rows, ep, st);
+    return cudaErrorInvalidValue;
+  } else {
+    if (EPI == TC_GEGLU) {
+      if (N % 128 == 0) {
+        if (M >= kPairMinRows) return launch<256, EPI, true, F8>(A, W, M, N, K, w_rows, ep, st);
+        return launch<256, EPI, false, F8>(A, W, M, N, K, w_rows, ep, st);
+      }
+      return launch<128, EPI, false, F8>(A, W, M, N, K, w_rows, ep, st);
+    }
+    if (N % 256 == 0) {
+      if (M >= kPairMinRows) return launch<256, EPI, true, F8>(A, W, M, N, K, w_rows, ep, st);
+      return launch<256, EPI, false, F8>(A, W, M, N, K, w_rows, ep, st);
+    }
+    if (N % 128 == 0) return launch<128, EPI, false, F8>(A, W, M, N, K, w_rows, ep, st);
+    return launch<64, EPI, false, F8>(A, W, M, N, K, w_rows, ep, st);
   }
-  if (N % 256 == 0) {
-    if (M >= kPairMinRows) return launch<256, EPI, true, F8>(A, W, M, N, K, w_rows, ep, st);
-    return launch<256, EPI, false, F8>(A, W, M, N, K, w_rows, ep, st);
-  }
-  if (N % 128 == 0) return launch<128, EPI, false, F8>(A, W, M, N, K, w_rows, ep, st);
-  return launch<64, EPI, false, F8>(A, W, M, N, K, w_rows, ep, st);
 }
 
 }  // namespace
@@ -894,6 +1035,9 @@ cudaError_t gemm_tc(const bf16* A, const bf16* W, const float* bias, bf16* C, fl
     case TC_RESID: return dispatch_bn<TC_RESID>(A, W, M, N, K, N, ep, st);
     case TC_GEGLU: return dispatch_bn<TC_GEGLU>(A, W, M, N, K, 2 * N, ep, st);
     case TC_ROPE: return dispatch_bn<TC_ROPE>(A, W, M, N, K, N, ep, st);
+    case TC_RESID16:
+      if (!C) return cudaErrorInvalidValue;
+      return dispatch_bn<TC_RESID16>(A, W, M, N, K, N, ep, st);
   }
   return cudaErrorInvalidValue;
 }
@@ -911,7 +1055,8 @@ cudaError_t gemm_tc_take_status(int* code) {
 
 bool gemm_tc_f8_supported(int M, int N, int K, int epi) {
   if (M <= 0 || K < 2 * BK || K % (2 * BK) != 0 || N % 64 != 0) return false;
-  return epi == TC_STORE || epi == TC_GEGLU || epi == TC_ROPE || epi == TC_RESID;
+  return epi == TC_STORE || epi == TC_GEGLU || epi == TC_ROPE || epi == TC_RESID ||
+         epi == TC_RESID16;
 }
 
 cudaError_t gemm_tc_f8(const uint8_t* A, const uint8_t* W, const float* sa, const float* sw,
@@ -937,12 +1082,15 @@ cudaError_t gemm_tc_f8(const uint8_t* A, const uint8_t* W, const float* sa, cons
   ep.c8_rowscale = q8.rowscale;
   ep.uniform = q8.uniform ? 1 : 0;
   ep.err = err;
-  if (epi == TC_RESID && !resid) return cudaErrorInvalidValue;
+  if ((epi == TC_RESID && !resid) || (epi == TC_RESID16 && !C)) return cudaErrorInvalidValue;
   if (q8.C && (epi != TC_GEGLU || !q8.scale || !q8.rowscale)) return cudaErrorInvalidValue;
   switch (epi) {
     case TC_STORE: return dispatch_bn<TC_STORE, true>(A, W, M, N, K, N, ep, st);
     case TC_RESID: return dispatch_bn<TC_RESID, true>(A, W, M, N, K, N, ep, st);
-    case TC_GEGLU: return dispatch_bn<TC_GEGLU, true>(A, W, M, N, K, 2 * N, ep, st);
+    case TC_RESID16: return dispatch_bn<TC_RESID16, true>(A, W, M, N, K, N, ep, st);
+    case TC_GEGLU:
+      if (q8.C) return dispatch_bn<TC_GEGLU8, true>(A, W, M, N, K, 2 * N, ep, st);
+      return dispatch_bn<TC_GEGLU, true>(A, W, M, N, K, 2 * N, ep, st);
     case TC_ROPE: return dispatch_bn<TC_ROPE, true>(A, W, M, N, K, N, ep, st);
   }
   return cudaErrorInvalidValue;

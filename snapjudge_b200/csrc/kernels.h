@@ -104,7 +104,10 @@ cudaError_t mean_pool(const float* h, const int32_t* cu, int B, int D, float* po
 // or, for geglu, F % 128 == 0, 16-byte aligned rows).
 bool gemm_tc_supported(int M, int N, int K, bool geglu);
 
-enum TcEpi { TC_STORE = 0, TC_RESID = 1, TC_GEGLU = 2, TC_ROPE = 3 };
+// TC_RESID: fp32 resid [M, N] += acc (+ bias).  TC_RESID16: the residual is
+// bf16 and is C itself (SJ_PREC_FP8_TENSOR's residual stream): C += acc (+
+// bias), rounded to bf16; N % 128 == 0.
+enum TcEpi { TC_STORE = 0, TC_RESID = 1, TC_GEGLU = 2, TC_ROPE = 3, TC_RESID16 = 4 };
 struct TcRope {
   const float* cos_t;
   const float* sin_t;
@@ -152,11 +155,18 @@ cudaError_t ln_e4m3(const float* X, const float* w, const float* b, uint8_t* q, 
                     int64_t rows, int D, float eps, cudaStream_t st);
 // SJ_PREC_FP8_TENSOR: one static scale per activation tensor, read from device
 // memory (*s_t): LN(X) * w (+ b) (or, quant_rows_static, X itself) quantised as
-// x / s_t, and sa[row] = s_t for the GEMM epilogue.
-cudaError_t ln_e4m3_static(const float* X, const float* w, const float* b, uint8_t* q, float* sa,
+// x / s_t, and sa[row] = s_t for the GEMM epilogue.  TX: float or bf16 (the
+// per-tensor variant's bf16 residual stream).
+template <typename TX>
+cudaError_t ln_e4m3_static(const TX* X, const float* w, const float* b, uint8_t* q, float* sa,
                            const float* s_t, int64_t rows, int D, float eps, cudaStream_t st);
-cudaError_t quant_rows_static(const float* x, int64_t rows, int cols, uint8_t* q, float* sa,
+template <typename TX>
+cudaError_t quant_rows_static(const TX* x, int64_t rows, int cols, uint8_t* q, float* sa,
                               const float* s_t, cudaStream_t st);
+// Y = fp32(X), n % 4 == 0; widen_rows_f32: only rows[0..n) of [*, D] (D % 4 == 0)
+cudaError_t widen_f32(const bf16* X, float* Y, int64_t n, cudaStream_t st);
+cudaError_t widen_rows_f32(const bf16* X, float* Y, const int32_t* rows, int n, int D,
+                           cudaStream_t st);
 // *amax = max(*amax, max |x|) (float bits in an unsigned; calibration)
 template <typename T>
 cudaError_t amax_abs(const T* x, int64_t n, unsigned* amax, cudaStream_t st);

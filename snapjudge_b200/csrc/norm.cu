@@ -276,7 +276,8 @@ __global__ void __launch_bounds__(256) ln_e4m3_warp(const float* __restrict__ X,
 __device__ __forceinline__ float static_inv(float s) { return s > 0.f ? __fdiv_rn(1.f, s) : 0.f; }
 
 // LN(X) * w (+ b) as ln_e4m3_warp, quantised with the tensor's scale
-__global__ void __launch_bounds__(256) ln_e4m3_static_warp(const float* __restrict__ X,
+template <typename TX>
+__global__ void __launch_bounds__(256) ln_e4m3_static_warp(const TX* __restrict__ X,
                                                            const float* __restrict__ w,
                                                            const float* __restrict__ b,
                                                            uint8_t* __restrict__ q,
@@ -291,7 +292,7 @@ __global__ void __launch_bounds__(256) ln_e4m3_static_warp(const float* __restri
 #pragma unroll
   for (int k = 0; k < kMaxChunks; ++k) {
     const int c = lane + 32 * k;
-    v[k] = c < nc4 ? load4<float>(X + i * D + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    v[k] = c < nc4 ? load4<TX>(X + i * D + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
   }
   float mean, invs;
   row_stats(v, lane, nc4, D, eps, mean, invs);
@@ -313,8 +314,74 @@ __global__ void __launch_bounds__(256) ln_e4m3_static_warp(const float* __restri
   if (lane == 0) sa[i] = st;
 }
 
+// ln_e4m3_static_warp for a bf16 X with D = 256 NC: each lane holds NC
+// chunks of 8 values (16-byte loads), chunk k at columns 8 (lane + 32 k), kept
+// as packed bf16 pairs and widened where used
+template <int NC>
+__global__ void __launch_bounds__(128) ln_e4m3_static_bf16x8(const bf16* __restrict__ X,
+                                                                const float* __restrict__ w,
+                                                                const float* __restrict__ b,
+                                                                uint8_t* __restrict__ q,
+                                                                float* __restrict__ sa,
+                                                                const float* __restrict__ s_t,
+                                                                int64_t M, float eps) {
+  constexpr int D = 256 * NC;
+  const int lane = threadIdx.x & 31;
+  const int64_t i = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (i >= M) return;
+  uint32_t u[NC][4];
+#pragma unroll
+  for (int k = 0; k < NC; ++k) {
+    const uint4 t = *reinterpret_cast<const uint4*>(X + i * D + 8 * (lane + 32 * k));
+    u[k][0] = t.x; u[k][1] = t.y; u[k][2] = t.z; u[k][3] = t.w;
+  }
+  auto pair = [](uint32_t p) {
+    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&p));
+  };
+  float s = 0.f;
+#pragma unroll
+  for (int k = 0; k < NC; ++k)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = pair(u[k][e]);
+      s += f.x + f.y;
+    }
+  const float mean = warp_sum(s) / (float)D;
+  float d2 = 0.f;
+#pragma unroll
+  for (int k = 0; k < NC; ++k)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = pair(u[k][e]);
+      const float d0 = f.x - mean, d1 = f.y - mean;
+      d2 += d0 * d0 + d1 * d1;
+    }
+  const float invs = 1.0f / sqrtf(warp_sum(d2) / (float)D + eps);
+  const float st = *s_t, inv = static_inv(st);
+#pragma unroll
+  for (int k = 0; k < NC; ++k) {
+    const int c = 8 * (lane + 32 * k);
+    uint32_t code[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const float2 f0 = pair(u[k][2 * h]), f1 = pair(u[k][2 * h + 1]);
+      const float4 g = load4<float>(w + c + 4 * h);
+      float4 o = make_float4((f0.x - mean) * invs * g.x, (f0.y - mean) * invs * g.y,
+                             (f1.x - mean) * invs * g.z, (f1.y - mean) * invs * g.w);
+      if (b) {
+        const float4 bb = load4<float>(b + c + 4 * h);
+        o.x += bb.x; o.y += bb.y; o.z += bb.z; o.w += bb.w;
+      }
+      code[h] = e4m3x4(o, inv);
+    }
+    *reinterpret_cast<uint2*>(q + i * D + c) = make_uint2(code[0], code[1]);
+  }
+  if (lane == 0) sa[i] = st;
+}
+
 // rows of x quantised with the tensor's scale (the identity norm of layer 0)
-__global__ void __launch_bounds__(256) quant_rows_static_kernel(const float* __restrict__ x,
+template <typename TX>
+__global__ void __launch_bounds__(256) quant_rows_static_kernel(const TX* __restrict__ x,
                                                                 int64_t rows, int cols,
                                                                 uint8_t* __restrict__ q,
                                                                 float* __restrict__ sa,
@@ -324,7 +391,7 @@ __global__ void __launch_bounds__(256) quant_rows_static_kernel(const float* __r
   if (i >= rows) return;
   const float st = *s_t, inv = static_inv(st);
   uint32_t* qrow = reinterpret_cast<uint32_t*>(q + i * cols);
-  for (int c = 4 * lane; c < cols; c += 128) qrow[c >> 2] = e4m3x4(load4<float>(x + i * cols + c), inv);
+  for (int c = 4 * lane; c < cols; c += 128) qrow[c >> 2] = e4m3x4(load4<TX>(x + i * cols + c), inv);
   if (lane == 0) sa[i] = st;
 }
 
@@ -428,6 +495,24 @@ __global__ void cast_bf16_kernel(const float* __restrict__ X, bf16* __restrict__
   if (i < n) Y[i] = __float2bfloat16(X[i]);
 }
 
+// rows[i] of X (bf16 [*, D]) -> the same rows of Y (fp32), one warp per row
+__global__ void __launch_bounds__(256) widen_rows_kernel(const bf16* __restrict__ X,
+                                                         float* __restrict__ Y,
+                                                         const int32_t* __restrict__ rows, int n,
+                                                         int D) {
+  const int lane = threadIdx.x & 31;
+  const int i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (i >= n) return;
+  const int64_t r = rows[i];
+  for (int c = 4 * lane; c < D; c += 128) store4<float>(Y + r * D + c, load4<bf16>(X + r * D + c));
+}
+
+// bf16 -> fp32, four values per thread (n % 4 == 0)
+__global__ void widen_f32_kernel(const bf16* __restrict__ X, float* __restrict__ Y, int64_t n4) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n4) store4<float>(Y + 4 * i, load4<bf16>(X + 4 * i));
+}
+
 bool warp_path(int D) { return D % 4 == 0 && D <= 4 * 32 * kMaxChunks; }
 
 }  // namespace
@@ -489,20 +574,60 @@ cudaError_t ln_e4m3(const float* X, const float* w, const float* b, uint8_t* q, 
   return cudaGetLastError();
 }
 
-cudaError_t ln_e4m3_static(const float* X, const float* w, const float* b, uint8_t* q, float* sa,
+template <typename TX>
+cudaError_t ln_e4m3_static(const TX* X, const float* w, const float* b, uint8_t* q, float* sa,
                            const float* s_t, int64_t rows, int D, float eps, cudaStream_t st) {
   if (rows <= 0) return cudaSuccess;
   if (D % 128 != 0 || D > 4 * 32 * kMaxChunks) return cudaErrorInvalidValue;
-  ln_e4m3_static_warp<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(X, w, b, q, sa, s_t, rows, D,
-                                                                  eps);
+  if constexpr (std::is_same<TX, bf16>::value) {
+    // 16-byte loads, registers for exactly the row's chunks; blocks of 4 rows
+    const unsigned g4 = (unsigned)((rows + 3) / 4);
+    switch (D) {
+      case 512: ln_e4m3_static_bf16x8<2><<<g4, 128, 0, st>>>(X, w, b, q, sa, s_t, rows, eps);
+        return cudaGetLastError();
+      case 768: ln_e4m3_static_bf16x8<3><<<g4, 128, 0, st>>>(X, w, b, q, sa, s_t, rows, eps);
+        return cudaGetLastError();
+      case 1024: ln_e4m3_static_bf16x8<4><<<g4, 128, 0, st>>>(X, w, b, q, sa, s_t, rows, eps);
+        return cudaGetLastError();
+      default: break;
+    }
+  }
+  ln_e4m3_static_warp<TX><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(X, w, b, q, sa, s_t, rows,
+                                                                      D, eps);
   return cudaGetLastError();
 }
+template cudaError_t ln_e4m3_static<float>(const float*, const float*, const float*, uint8_t*,
+                                           float*, const float*, int64_t, int, float, cudaStream_t);
+template cudaError_t ln_e4m3_static<bf16>(const bf16*, const float*, const float*, uint8_t*,
+                                          float*, const float*, int64_t, int, float, cudaStream_t);
 
-cudaError_t quant_rows_static(const float* x, int64_t rows, int cols, uint8_t* q, float* sa,
+template <typename TX>
+cudaError_t quant_rows_static(const TX* x, int64_t rows, int cols, uint8_t* q, float* sa,
                               const float* s_t, cudaStream_t st) {
   if (rows <= 0) return cudaSuccess;
   if (cols <= 0 || cols % 4 != 0) return cudaErrorInvalidValue;
-  quant_rows_static_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(x, rows, cols, q, sa, s_t);
+  quant_rows_static_kernel<TX><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(x, rows, cols, q, sa,
+                                                                           s_t);
+  return cudaGetLastError();
+}
+template cudaError_t quant_rows_static<float>(const float*, int64_t, int, uint8_t*, float*,
+                                              const float*, cudaStream_t);
+template cudaError_t quant_rows_static<bf16>(const bf16*, int64_t, int, uint8_t*, float*,
+                                             const float*, cudaStream_t);
+
+cudaError_t widen_rows_f32(const bf16* X, float* Y, const int32_t* rows, int n, int D,
+                           cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  if (D % 4 != 0) return cudaErrorInvalidValue;
+  widen_rows_kernel<<<(unsigned)((n + 7) / 8), 256, 0, st>>>(X, Y, rows, n, D);
+  return cudaGetLastError();
+}
+
+cudaError_t widen_f32(const bf16* X, float* Y, int64_t n, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  if (n % 4 != 0) return cudaErrorInvalidValue;
+  const int64_t n4 = n / 4;
+  widen_f32_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(X, Y, n4);
   return cudaGetLastError();
 }
 
