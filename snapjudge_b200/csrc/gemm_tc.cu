@@ -147,6 +147,27 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+__device__ __forceinline__ float tanh_approx(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// The GEGLU gate with the tanh form of GELU,
+//   gelu(x) ~ x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))) / 2,
+// one MUFU operation per value instead of two.  It differs from the erf form
+// by at most 4.7e-4 (at |x| ~ 2.7), far below the e4m3 rounding of the values
+// it is used for: only the GEGLU with e4m3 output (TC_GEGLU8).
+__device__ __forceinline__ float2 geglu_pair_tanh(float ga, float gb, float ua, float ub) {
+  constexpr float k0 = 0.7978845608028654f;          // sqrt(2 / pi)
+  constexpr float k1 = 0.044715f * 0.7978845608028654f;
+  const f32x2 g = pk2(ga, gb);
+  const float2 in = unpk2(mul2(g, fma2(mul2(g, g), splat2(k1), splat2(k0))));
+  const f32x2 t = pk2(tanh_approx(in.x), tanh_approx(in.y));
+  const f32x2 hg = mul2(g, splat2(0.5f));
+  return unpk2(mul2(fma2(hg, t, hg), pk2(ua, ub)));
+}
+
 // (gelu(ga) * ua, gelu(gb) * ub)
 __device__ __forceinline__ float2 geglu_pair(float ga, float gb, float ua, float ub) {
   constexpr float kP = 0.3275911f * 0.70710678118654752f;  // p / sqrt(2)
@@ -526,10 +547,10 @@ __global__ void __launch_bounds__(threads_for<EPI>(), 1)
         uint32_t w[8];
 #pragma unroll
         for (int j = 0; j < 32; j += 4) {
-          const float2 o0 = geglu_pair(__uint_as_float(r0[j]), __uint_as_float(r0[j + 1]),
-                                       __uint_as_float(r1[j]), __uint_as_float(r1[j + 1]));
-          const float2 o1 = geglu_pair(__uint_as_float(r0[j + 2]), __uint_as_float(r0[j + 3]),
-                                       __uint_as_float(r1[j + 2]), __uint_as_float(r1[j + 3]));
+          const float2 o0 = geglu_pair_tanh(__uint_as_float(r0[j]), __uint_as_float(r0[j + 1]),
+                                            __uint_as_float(r1[j]), __uint_as_float(r1[j + 1]));
+          const float2 o1 = geglu_pair_tanh(__uint_as_float(r0[j + 2]), __uint_as_float(r0[j + 3]),
+                                            __uint_as_float(r1[j + 2]), __uint_as_float(r1[j + 3]));
           w[j / 4] = e4m3x4(o0.x * inv8, o0.y * inv8, o1.x * inv8, o1.y * inv8);
         }
         if (live) {

@@ -42,3 +42,28 @@ def test_float32_far_below_bf16_step():
     want = gelu_exact(x)
     rel = np.abs(got - want) / np.maximum(np.abs(want), 1.0)
     assert rel.max() < 2.0 ** -9 / 64
+
+
+def gelu_tanh(x, dtype):
+    """The tanh form the e4m3-output GEGLU epilogue (SJ_PREC_FP8_TENSOR) uses,
+    with its constants, in the given precision (tanh itself exact here; the
+    kernel's tanh.approx.f32 adds ~2^-11 relative to the tanh)."""
+    x = np.asarray(x, dtype)
+    k0 = dtype(0.7978845608028654)
+    k1 = dtype(0.044715) * k0
+    inner = x * (x * x * k1 + k0)
+    h = dtype(0.5) * x
+    return h * np.tanh(inner) + h
+
+
+def test_tanh_form_within_e4m3_rounding():
+    """The tanh form's distance from the erf GELU: at most 4.8e-4 absolute,
+    and below 1/64 of |gelu(x)| (a quarter of e4m3's relative rounding step
+    of 2^-4) wherever |gelu(x)| >= 0.05."""
+    x = np.linspace(-12.0, 12.0, 48001)
+    want = gelu_exact(x)
+    got = gelu_tanh(x, np.float64)
+    err = np.abs(got - want)
+    assert err.max() <= 4.8e-4
+    big = np.abs(want) >= 0.05
+    assert np.all(err[big] <= np.abs(want[big]) / 64)

@@ -235,7 +235,7 @@ def test_fp8_tensor_encoder_against_fp32_forward():
     """The per-tensor variant (QKV, Wi and Wo2 on e4m3, one scale per weight
     tensor, static activation scales from a calibration pass over this same
     batch), C3 architecture, ragged batch of 8, against the fp32 forward with
-    the per-token variant's bars.  Measured on a B200: relative error 0.0375
+    the per-token variant's bars.  Measured on a B200: relative error 0.0386
     (per-token 0.0309), smallest row cosine 0.9991."""
     spec = synth.SPECS["c3"]
     t = synth.make_weights(spec)
@@ -277,7 +277,7 @@ def test_fp8_tensor_scales_fixed_after_first_pass():
 def test_fp8_tensor_c4_architecture():
     """C4 architecture (24 x 1024, F = 2816, a multiple of 128) in the
     per-tensor variant, with the per-token variant's C4 bars.  Measured on a
-    B200: relative error 0.084 (per-token 0.069), smallest row cosine 0.9953."""
+    B200: relative error 0.085 (per-token 0.069), smallest row cosine 0.9950."""
     spec = synth.SPECS["c4"]
     t = synth.make_weights(spec)
     lengths = np.array([300, 77, 129])
@@ -306,7 +306,7 @@ def test_fp8_variants_on_c5_heads():
     mode and both FP8 variants against the fp32 CPU forward and fp64 heads.
     Bars: bf16 5e-3 (the bf16 probability bar), both FP8 variants 5e-2; the
     [CLS] states within 0.06 relative.  Measured on a B200: probabilities
-    bf16 1.9e-3, fp8 2.4e-2, fp8_tensor 3.1e-2; [CLS] relative error 0.0025,
+    bf16 1.9e-3, fp8 2.4e-2, fp8_tensor 3.0e-2; [CLS] relative error 0.0025,
     0.032, 0.039."""
     spec = synth.SPECS["c5"]
     t = synth.make_weights(spec)
