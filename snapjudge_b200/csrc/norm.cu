@@ -314,49 +314,52 @@ __global__ void __launch_bounds__(256) ln_e4m3_static_warp(const TX* __restrict_
   if (lane == 0) sa[i] = st;
 }
 
-// ln_e4m3_static_warp for a bf16 X with D = 256 NC: each lane holds NC
-// chunks of 8 values (16-byte loads), chunk k at columns 8 (lane + 32 k), kept
-// as packed bf16 pairs and widened where used
+// ln_e4m3_static_warp for a bf16 X with D = 256 NC (the per-tensor FP8
+// variant's LayerNorm, whose output is rounded to e4m3): each lane holds NC
+// chunks of 8 values (16-byte loads), chunk k at columns 8 (lane + 32 k).
+// Fewer instructions per row than the generic kernel: the mean and variance
+// are multiplied by the constant 1/D and the inverse deviation is rsqrtf
+// (each within a few ulp of the division and 1/sqrtf the bf16 mode uses).
 template <int NC>
 __global__ void __launch_bounds__(128) ln_e4m3_static_bf16x8(const bf16* __restrict__ X,
-                                                                const float* __restrict__ w,
-                                                                const float* __restrict__ b,
-                                                                uint8_t* __restrict__ q,
-                                                                float* __restrict__ sa,
-                                                                const float* __restrict__ s_t,
-                                                                int64_t M, float eps) {
+                                                             const float* __restrict__ w,
+                                                             const float* __restrict__ b,
+                                                             uint8_t* __restrict__ q,
+                                                             float* __restrict__ sa,
+                                                             const float* __restrict__ s_t,
+                                                             int64_t M, float eps) {
   constexpr int D = 256 * NC;
+  constexpr float kInvD = 1.0f / (float)D;
   const int lane = threadIdx.x & 31;
   const int64_t i = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (i >= M) return;
-  uint32_t u[NC][4];
+  float v[NC][8];
 #pragma unroll
   for (int k = 0; k < NC; ++k) {
     const uint4 t = *reinterpret_cast<const uint4*>(X + i * D + 8 * (lane + 32 * k));
-    u[k][0] = t.x; u[k][1] = t.y; u[k][2] = t.z; u[k][3] = t.w;
+    const uint32_t tw[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&tw[e]));
+      v[k][2 * e] = f.x;
+      v[k][2 * e + 1] = f.y;
+    }
   }
-  auto pair = [](uint32_t p) {
-    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&p));
-  };
   float s = 0.f;
 #pragma unroll
   for (int k = 0; k < NC; ++k)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 f = pair(u[k][e]);
-      s += f.x + f.y;
-    }
-  const float mean = warp_sum(s) / (float)D;
+    for (int e = 0; e < 8; ++e) s += v[k][e];
+  const float mean = warp_sum(s) * kInvD;
   float d2 = 0.f;
 #pragma unroll
   for (int k = 0; k < NC; ++k)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 f = pair(u[k][e]);
-      const float d0 = f.x - mean, d1 = f.y - mean;
-      d2 += d0 * d0 + d1 * d1;
+    for (int e = 0; e < 8; ++e) {
+      v[k][e] -= mean;
+      d2 = fmaf(v[k][e], v[k][e], d2);
     }
-  const float invs = 1.0f / sqrtf(warp_sum(d2) / (float)D + eps);
+  const float invs = rsqrtf(warp_sum(d2) * kInvD + eps);
   const float st = *s_t, inv = static_inv(st);
 #pragma unroll
   for (int k = 0; k < NC; ++k) {
@@ -364,10 +367,9 @@ __global__ void __launch_bounds__(128) ln_e4m3_static_bf16x8(const bf16* __restr
     uint32_t code[2];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      const float2 f0 = pair(u[k][2 * h]), f1 = pair(u[k][2 * h + 1]);
       const float4 g = load4<float>(w + c + 4 * h);
-      float4 o = make_float4((f0.x - mean) * invs * g.x, (f0.y - mean) * invs * g.y,
-                             (f1.x - mean) * invs * g.z, (f1.y - mean) * invs * g.w);
+      float4 o = make_float4(v[k][4 * h] * invs * g.x, v[k][4 * h + 1] * invs * g.y,
+                             v[k][4 * h + 2] * invs * g.z, v[k][4 * h + 3] * invs * g.w);
       if (b) {
         const float4 bb = load4<float>(b + c + 4 * h);
         o.x += bb.x; o.y += bb.y; o.z += bb.z; o.w += bb.w;
