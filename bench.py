@@ -83,24 +83,40 @@ class ClockSampler:
     def __init__(self, gpu: int):
         self.gpu = gpu
         self.proc = None
-        self.lines: list[str] = []
+        self.lines: list[tuple[float, str]] = []  # (host arrival time, csv line)
+        self.t0 = self.t1 = None
 
     def start(self):
+        """Start sampling every 100 ms and wait (up to 5 s) for the first sample,
+        so that a short timed region that follows still gets samples."""
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                 "-lms", "200", "-i", str(self.gpu)],
+                 "-lms", "100", "-i", str(self.gpu)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
         except OSError:
             self.proc = None
+            return
+        end = time.monotonic() + 5.0
+        while not self.lines and time.monotonic() < end:
+            time.sleep(0.01)
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.monotonic(), line.strip()))
+
+    def mark_start(self):
+        self.t0 = time.monotonic()
+
+    def mark_end(self):
+        self.t1 = time.monotonic()
 
     def stop(self) -> dict:
+        """Median SM clock and the throttle reasons of the samples taken between
+        mark_start and mark_end (a sample arrives up to ~100 ms after it is
+        taken, so the window's end is extended by 0.15 s)."""
         if not self.proc:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         time.sleep(0.25)
@@ -112,7 +128,11 @@ class ClockSampler:
         self.t.join(timeout=2)
         sm, smax, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        t0 = self.t0 if self.t0 is not None else float("-inf")
+        t1 = self.t1 + 0.15 if self.t1 is not None else float("inf")
+        for ts, ln in self.lines:
+            if not (t0 <= ts <= t1):
+                continue
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
@@ -349,10 +369,11 @@ def main():
     eng.sync(st)
     eng.profile(reset=True)
     eng.set_profiling(True)
-    barrier()
-    torch.cuda.synchronize()
     clocks = ClockSampler(local)
     clocks.start()
+    barrier()
+    torch.cuda.synchronize()
+    clocks.mark_start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(st)
     for _ in range(a.steps):
@@ -360,6 +381,7 @@ def main():
     e1.record(st)
     eng.sync(st)
     torch.cuda.synchronize()
+    clocks.mark_end()
     ms = e0.elapsed_time(e1)
     clk = clocks.stop()
     prof = eng.profile(reset=True)

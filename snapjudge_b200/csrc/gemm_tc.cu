@@ -99,12 +99,6 @@ __device__ __forceinline__ void record_err(int* err, int code) {
   atomicCAS(err ? err : &g_gemm_tc_err, 0, code);
 }
 
-__device__ __forceinline__ float act_fn(float v, int act) {
-  if (act == ACT_GELU) return gelu_erf(v);
-  if (act == ACT_RELU) return fmaxf(v, 0.f);
-  return v;
-}
-
 // ---- GEGLU gate on column pairs, packed fp32 (fma/mul .f32x2) ----
 // erf by Abramowitz & Stegun, Handbook of Mathematical Functions, eq. 7.1.26:
 //   erfc(z) = (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-z^2),
@@ -168,8 +162,8 @@ __device__ __forceinline__ float2 geglu_pair_tanh(float ga, float gb, float ua, 
   return unpk2(mul2(fma2(hg, t, hg), pk2(ua, ub)));
 }
 
-// (gelu(ga) * ua, gelu(gb) * ub)
-__device__ __forceinline__ float2 geglu_pair(float ga, float gb, float ua, float ub) {
+// (gelu(ga), gelu(gb)), packed
+__device__ __forceinline__ f32x2 gelu2(float ga, float gb) {
   constexpr float kP = 0.3275911f * 0.70710678118654752f;  // p / sqrt(2)
   // -a_i / 2: the polynomial comes out as -erfc(z) / 2 before the exponential
   constexpr float kA1 = -0.5f * 0.254829592f, kA2 = 0.5f * 0.284496736f,
@@ -187,8 +181,44 @@ __device__ __forceinline__ float2 geglu_pair(float ga, float gb, float ua, float
   const f32x2 g = pk2(ga, gb);
   const float2 e = unpk2(mul2(mul2(g, g), splat2(kE)));
   const f32x2 h = mul2(p, pk2(ex2_approx(e.x), ex2_approx(e.y)));  // -(1 - Phi(|x|))
-  const f32x2 gelu = fma2(ax, h, pk2(fmaxf(ga, 0.f), fmaxf(gb, 0.f)));
-  return unpk2(mul2(gelu, pk2(ua, ub)));
+  return fma2(ax, h, pk2(fmaxf(ga, 0.f), fmaxf(gb, 0.f)));
+}
+
+// (gelu(ga) * ua, gelu(gb) * ub)
+__device__ __forceinline__ float2 geglu_pair(float ga, float gb, float ua, float ub) {
+  return unpk2(mul2(gelu2(ga, gb), pk2(ua, ub)));
+}
+
+// The STORE epilogue's 32 accumulator values: + bias[0..32) (when given), then
+// the activation, chosen once per call so that the unrolled loop holds one
+// activation's code; GELU is the GEGLU gate's erf approximation above.
+template <int ACT>
+__device__ __forceinline__ void bias_act32(const uint32_t (&r)[32], const float* bias, float* v) {
+#pragma unroll
+  for (int j = 0; j < 32; j += 2) {
+    float a0 = __uint_as_float(r[j]), a1 = __uint_as_float(r[j + 1]);
+    if (bias) {
+      const float2 bb = *reinterpret_cast<const float2*>(bias + j);
+      a0 += bb.x;
+      a1 += bb.y;
+    }
+    if (ACT == ACT_GELU) {
+      const float2 g = unpk2(gelu2(a0, a1));
+      a0 = g.x;
+      a1 = g.y;
+    } else if (ACT == ACT_RELU) {
+      a0 = fmaxf(a0, 0.f);
+      a1 = fmaxf(a1, 0.f);
+    }
+    v[j] = a0;
+    v[j + 1] = a1;
+  }
+}
+__device__ __forceinline__ void bias_act32(const uint32_t (&r)[32], const float* bias, int act,
+                                           float* v) {
+  if (act == ACT_GELU) bias_act32<ACT_GELU>(r, bias, v);
+  else if (act == ACT_RELU) bias_act32<ACT_RELU>(r, bias, v);
+  else bias_act32<ACT_NONE>(r, bias, v);
 }
 
 // 32 values to e4m3 codes (x * inv, RN, saturating at +-448) in memory order,
@@ -897,12 +927,8 @@ __global__ void __launch_bounds__(threads_for<EPI>(), 1)
             tmem_ld32(tacc + c + 32 * k2, r0);
             tmem_ld_wait();
             if constexpr (F8) unscale32(r0, sa, ep.sw + col_base + c + 32 * k2, su);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              float a = __uint_as_float(r0[j]);
-              if (ep.bias) a += ep.bias[col_base + c + 32 * k2 + j];
-              v[32 * k2 + j] = act_fn(a, ep.act);
-            }
+            bias_act32(r0, ep.bias ? ep.bias + col_base + c + 32 * k2 : nullptr, ep.act,
+                       v + 32 * k2);
           }
           store_chunk(v, col_base + c, m0 + q * 32);
         }
@@ -915,12 +941,7 @@ __global__ void __launch_bounds__(threads_for<EPI>(), 1)
           if (!live) continue;
           if constexpr (F8) unscale32(r0, sa, ep.sw + col_base + c, su);
           float v[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float a = __uint_as_float(r0[j]);
-            if (ep.bias) a += ep.bias[col_base + c + j];
-            v[j] = act_fn(a, ep.act);
-          }
+          bias_act32(r0, ep.bias ? ep.bias + col_base + c : nullptr, ep.act, v);
           store_bf16x32(ep.C + (int64_t)row * ep.ldc + col_base + c, v);
         }
       }
