@@ -273,6 +273,10 @@ int sj_fast_launch_count(const sj_fast* e);
 #define SJ_K_FINAL 7      /* final norm, LoRA, decision heads, positions */
 #define SJ_K_COUNT 8
 int sj_fast_set_profiling(sj_fast* e, int enable);
+/* SJ_PREC_FP8_TENSOR: forget the activation scales, so that the next forward
+ * call calibrates them again on its own batch (a bf16 pass recording each e4m3
+ * operand's amax, then the FP8 pass).  SJ_ERR_STATE for other precisions. */
+int sj_fast_reset_calibration(sj_fast* e);
 /* Accumulated since the last reset (synchronises the engine's work first):
  * ms[k] total milliseconds and launches[k] count of class k (arrays of
  * SJ_K_COUNT); reset != 0 clears the accumulators afterwards. */

@@ -32,6 +32,7 @@ EXPORTS = ["sj_b200_version", "sj_last_error", "sj_gemm", "sj_gemm_geglu", "sj_a
            "sj_fast_commit", "sj_fast_encode", "sj_fast_embed", "sj_fast_decide", "sj_fast_forward", "sj_fast_n_act",
            "sj_fast_encode_device",
            "sj_fast_sync", "sj_fast_launch_count", "sj_fast_set_profiling", "sj_fast_profile",
+           "sj_fast_reset_calibration",
            "sj_fast_last_error", "sj_fast_destroy"]
 
 # kernel classes of sj_fast_profile (SJ_K_* in the header)
@@ -93,6 +94,7 @@ def lib() -> C.CDLL:
         L.sj_fast_sync.argtypes = [_P, _P]
         L.sj_fast_launch_count.argtypes = [_P]
         L.sj_fast_set_profiling.argtypes = [_P, _I]
+        L.sj_fast_reset_calibration.argtypes = [_P]
         L.sj_fast_profile.argtypes = [_P, C.POINTER(C.c_double), C.POINTER(C.c_int64), _I]
         L.sj_fast_destroy.argtypes = [_P]
         _LIB = L

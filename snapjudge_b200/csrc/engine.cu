@@ -1313,6 +1313,13 @@ int sj_fast_sync(sj_fast* e, void* stream) {
 
 int sj_fast_launch_count(const sj_fast* e) { return e ? e->launches : 0; }
 
+int sj_fast_reset_calibration(sj_fast* e) {
+  if (!e) return SJ_ERR_INVALID;
+  if (!e->fp8_tensor) return e->fail(SJ_ERR_STATE, "sj_fast_reset_calibration: not SJ_PREC_FP8_TENSOR");
+  e->calibrated = false;
+  return SJ_OK;
+}
+
 int sj_fast_set_profiling(sj_fast* e, int enable) {
   if (!e) return SJ_ERR_INVALID;
   e->profiling = enable != 0;

@@ -234,6 +234,11 @@ class FastSnapjudge:
     def launch_count(self) -> int:
         return _lib.lib().sj_fast_launch_count(self._h)
 
+    def reset_calibration(self) -> None:
+        """fp8_tensor: the next call calibrates the activation scales again, on
+        its own batch."""
+        check(_lib.lib().sj_fast_reset_calibration(self._h), self._h)
+
     def set_profiling(self, enable: bool) -> None:
         check(_lib.lib().sj_fast_set_profiling(self._h, int(enable)), self._h)
 

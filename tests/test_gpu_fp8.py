@@ -274,6 +274,28 @@ def test_fp8_tensor_scales_fixed_after_first_pass():
     assert e <= 0.06 and c >= 0.998
 
 
+def test_fp8_tensor_reset_calibration():
+    """After sj_fast_reset_calibration the next call calibrates on its own
+    batch: the engine then gives what a fresh engine gives on that batch.
+    Other precisions refuse the call."""
+    spec = synth.SPECS["c3"]
+    t = synth.make_weights(spec)
+    rng = np.random.default_rng(23)
+    la, lb = np.array([64, 9, 200]), np.array([300, 5, 77, 128])
+    ia = rng.integers(0, spec.cfg.vocab_size, size=int(la.sum())).astype(np.int64)
+    ib = rng.integers(0, spec.cfg.vocab_size, size=int(lb.sum())).astype(np.int64)
+    eng = FastSnapjudge(spec.cfg, t, precision="fp8_tensor")
+    eng.encode_packed(ia, la)
+    at_a = eng.encode_packed(ib, lb)  # b at a's scales
+    eng.reset_calibration()
+    own = eng.encode_packed(ib, lb)   # b calibrated on b
+    fresh = FastSnapjudge(spec.cfg, t, precision="fp8_tensor").encode_packed(ib, lb)
+    assert np.array_equal(own, fresh)
+    assert not np.array_equal(own, at_a)
+    with pytest.raises(SnapjudgeError):
+        FastSnapjudge(spec.cfg, t, precision="fp8").reset_calibration()
+
+
 def test_fp8_tensor_c4_architecture():
     """C4 architecture (24 x 1024, F = 2816, a multiple of 128) in the
     per-tensor variant, with the per-token variant's C4 bars.  Measured on a
