@@ -261,6 +261,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-fp8", action="store_true", help="skip the FP8-variant section")
     ap.add_argument("--no-c4", action="store_true", help="skip the C4 encoder section")
+    ap.add_argument("--no-sjmodel", action="store_true", help="skip the SjModel encoder section")
     ap.add_argument("--ncu-case", action="store_true",
                     help="run only the small case the profiles/ summaries are captured on")
     ap.add_argument("--ncu-precision", default="bf16",
@@ -480,6 +481,8 @@ def main():
             line["fp8"] = fp8_section(spec, weights, a, local, st, pass_args, probs_d, T, value)
         if world == 1 and not a.no_c4:
             line["c4"] = c4_section(a, local, st, pk, pk_kind)
+        if world == 1 and not a.no_sjmodel:
+            line["sjmodel"] = sjmodel_section(a, local, st, pk, pk_kind)
         if world == 1 and not a.no_cpu_baseline:
             tok, sec, n, kind, cores = reference_sample(spec, weights, a.cpu_seconds, 8, 4096,
                                                         seed=spec.seed + 40000, batch=1)
@@ -550,6 +553,61 @@ def c4_section(a, local, st, pk, pk_kind):
     peak = pk.get("bf16_tflops_sustained", FALLBACK["bf16_tflops_sustained"])
     return {"config": "c4: 24 layers x 1024 (16 heads x 64, GEGLU 2816, vocab 50368), "
                       "32 x 2048 tokens, noul head, bf16",
+            "tokens_per_s": T / (ms / 1e3), "ms_per_step": ms, "steps": steps,
+            "flops_per_step": flops, "tflops": tf, "frac_of_roofline": tf / peak,
+            "peak": peak, "peak_kind": f"{pk_kind} sustained bf16",
+            "kernels_ms_per_step": {k: v[0] / steps for k, v in prof.items()}}
+
+
+def sjmodel_section(a, local, st, pk, pk_kind):
+    """The reference's second encoder family, SjModel (src/sj_model.cpp), at
+    base width: 12 pre-LN layers x 768 (12 heads x 64), learned positions,
+    biased q/k/v/o projections, a biased GELU FFN of 3072, seeded weights.
+    One pass of config-5-distributed requests (lengths within its 512
+    positions, 262,144 tokens at most) through the engine in bf16 to the
+    final hidden states, device-resident inputs, CUDA events; FLOPs per step
+    layers x [T 2 (4 D^2 + 2 D F) + 4 D sum n^2] against the measured
+    sustained bf16 peak."""
+    import torch
+    from snapjudge_b200.fast import FastSnapjudge
+    cfg, seed = synth.SJ_SPECS["sj_base"]
+    weights = synth.make_sj_weights(cfg, seed)
+    lengths = synth.make_lengths(synth.SPECS["c5"], batch=32768, seed=cfg.vocab_size + 7)
+    lengths = lengths[: int(np.searchsorted(np.cumsum(lengths), 262144, side="right"))]
+    ids = np.random.default_rng(seed + 1).integers(0, cfg.vocab_size, size=int(lengths.sum()))
+    T = int(lengths.sum())
+    D, F, L = cfg.hidden_size, cfg.intermediate_size, cfg.num_layers
+    eng = FastSnapjudge(cfg, weights, precision="bf16", device=local, max_tokens=T)
+    dev = torch.device("cuda", local)
+    cu_h = synth.cu_seqlens(lengths).astype(np.int32)
+    ids_d = torch.from_numpy(ids.astype(np.int64)).to(dev)
+    cu_d = torch.from_numpy(cu_h).to(dev)
+    hidden = torch.empty(T, D, dtype=torch.float32, device=dev)
+    steps = max(3, a.steps)
+    for _ in range(a.warmup):
+        eng.encode_device(ids_d, cu_d, cu_h, hidden=hidden, stream=st)
+    eng.sync(st)
+    eng.profile(reset=True)
+    eng.set_profiling(True)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(steps):
+        eng.encode_device(ids_d, cu_d, cu_h, hidden=hidden, stream=st)
+    e1.record(st)
+    eng.sync(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    prof = eng.profile(reset=True)
+    eng.set_profiling(False)
+    eng.close()
+    sq = float(np.sum(lengths.astype(np.float64) ** 2))
+    flops = L * (T * 2.0 * (4 * D * D + 2 * D * F) + 4.0 * D * sq)
+    tf = flops / (ms / 1e3) / 1e12
+    peak = pk.get("bf16_tflops_sustained", FALLBACK["bf16_tflops_sustained"])
+    return {"config": f"SjModel base: 12 layers x 768 (12 heads x 64, GELU FFN 3072, learned "
+                      f"positions, biased projections), {len(lengths)} requests of config 5's "
+                      f"length distribution ({T} tokens, one pass), final hidden states, bf16",
             "tokens_per_s": T / (ms / 1e3), "ms_per_step": ms, "steps": steps,
             "flops_per_step": flops, "tflops": tf, "frac_of_roofline": tf / peak,
             "peak": peak, "peak_kind": f"{pk_kind} sustained bf16",
