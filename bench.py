@@ -53,8 +53,8 @@ from snapjudge_b200 import synth  # noqa: E402
 PEAKS = os.path.join(ROOT, "MEASURED_PEAKS.json")
 FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per token of the
-# Wi+GEGLU launch, from the ncu capture summarised in profiles/gemm_geglu_c5.md
-# (56.66 MB + 83.79 MB for a 32768-token launch).  The launch's traffic grows in
+# Wi+GEGLU launch, from one ncu capture of that kernel on a 32768-token launch
+# of the C5 architecture (56.66 MB + 83.79 MB).  The launch's traffic grows in
 # proportion to its tokens (A rows read once, G rows written once, W 6.3 MB), so
 # the bench scales it to its own launch size.
 GEGLU_DRAM_BYTES_PER_TOKEN = (56.664576e6 + 83.79136e6) / 32768
@@ -511,7 +511,7 @@ def c4_section(a, local, st, pk, pk_kind):
     2048 tokens (no padding), seeded N(0, 0.02) weights, the noul head.  One
     step = the batch through the encoder and the head (one pass), device-
     resident inputs, CUDA events; the roofline is the forward's FLOPs
-    (layers x [T 2 (4 D^2 + 3 D F) + 4 D sum n^2], SURVEY 8(d)) against the
+    (layers x [T 2 (4 D^2 + 3 D F) + 4 D sum n^2]) against the
     measured sustained bf16 peak."""
     import torch
     from snapjudge_b200.fast import FastSnapjudge

@@ -1,8 +1,10 @@
 // agent_check.cpp — the reference runtime on the GPU fast path, on the
 // reference's own tiny checkpoint fixture.  TEST INFRASTRUCTURE ONLY (built by
 // oracle/Makefile into oracle/_ref/ from the reference's sources, with
-// src/agent.cpp carrying the two-line dispatch of INTEGRATION.md section 2,
-// and linked with snapjudge_b200/integration/fast.cpp).
+// src/agent.cpp carrying the maintainer's two-line dispatch: the constructor
+// builds a FastSnapjudge once the device resolves to "cuda", and the forward
+// calls it instead of DecisionModel::forward when it is there; linked with
+// snapjudge_b200/integration/fast.cpp).
 //
 // usage: agent_check <tiny checkpoint dir> <model_tiny.json>
 // 1. Agent(ckpt, "cpu").system_one equals the golden (the reference's own

@@ -6,8 +6,9 @@ layer) and the golden answer of Agent::system_one on it
 (tests/golden/model_tiny.json, checked by tests/test_model.cpp:29-45).
 oracle/Makefile copies both into oracle/_ref/ and builds, from the
 reference's sources, oracle/_ref/agent_check: the reference Agent and C API
-with the fast-path dispatch a maintainer adds,
-linked with this repository's FastSnapjudge adapter.  Checked here:
+with the fast-path dispatch a maintainer adds (a FastSnapjudge built once the
+device resolves to "cuda", called in place of DecisionModel::forward), linked
+with this repository's FastSnapjudge adapter.  Checked here:
 
 * Agent(ckpt, "cuda").system_one — the whole DecisionModel::forward of every
   question on the GPU — equals the golden in fp32 mode (numbers to the
