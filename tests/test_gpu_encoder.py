@@ -162,6 +162,15 @@ def test_c4_full_length_vs_oracle():
     assert (lengths == 2048).all()
 
 
+def test_c3_full_batch_vs_oracle():
+    """C3 at its full size: all 256 requests of the config's length
+    distribution (lognormal(128, 0.6) in [8, 512]) in one packed batch against
+    the C restatement, hidden states / logits / probabilities / labels at the
+    bf16 bars."""
+    spec = synth.SPECS["c3"]
+    _subset_check(spec, spec.batch, spec.seed + 1000)
+
+
 def test_c3_full_batch_properties():
     """Full C3 batch: finite, batch-invariant (packed batch == per-sequence), LN-shaped."""
     spec = synth.SPECS["c3"]
