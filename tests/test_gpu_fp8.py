@@ -298,6 +298,23 @@ def test_fp8_tensor_reset_calibration():
         FastSnapjudge(spec.cfg, t, precision="fp8").reset_calibration()
 
 
+def test_fp8_tensor_passes():
+    """A batch larger than max_tokens runs in several passes; the activation
+    scales come from the first pass alone and the later passes run at them:
+    within the bars against the fp32 forward."""
+    spec = synth.SPECS["c3"]
+    t = synth.make_weights(spec)
+    lengths = np.array([300, 77, 129, 250, 64, 9])
+    ids = np.random.default_rng(95).integers(0, spec.cfg.vocab_size, size=int(lengths.sum()))
+    ids = ids.astype(np.int64)
+    want = oracle.Oracle(spec.cfg, t).encode_packed(ids, lengths)
+    got = FastSnapjudge(spec.cfg, t, precision="fp8_tensor", max_tokens=320).encode_packed(
+        ids, lengths)
+    e, c = _vs(got, want)
+    print(f"fp8_tensor in passes of <= 320 tokens: relative error {e:.4f}, min cosine {c:.5f}")
+    assert np.isfinite(got).all() and e <= 0.06 and c >= 0.998
+
+
 def test_fp8_tensor_c4_architecture():
     """C4 architecture (24 x 1024, F = 2816, a multiple of 128) in the
     per-tensor variant, with the per-token variant's C4 bars.  Measured on a
