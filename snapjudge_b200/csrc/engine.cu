@@ -169,6 +169,8 @@ struct sj_fast {
   int32_t* h_cu = nullptr;
   int32_t* h_kvl = nullptr;
   cudaEvent_t staged_ev = nullptr;
+  // host_call: the last pass's h_cu / h_kvl have been copied to the device
+  cudaEvent_t inputs_ev = nullptr;
   // per-kernel CUDA-event timing (sj_fast_set_profiling)
   bool profiling = false;
   struct Mark { int cls; cudaEvent_t a, b; };
@@ -239,6 +241,7 @@ struct sj_fast {
     if (h_cu) cudaFreeHost(h_cu);
     if (h_kvl) cudaFreeHost(h_kvl);
     if (staged_ev) cudaEventDestroy(staged_ev);
+    if (inputs_ev) cudaEventDestroy(inputs_ev);
     for (const Mark& m : marks) {
       cudaEventDestroy(m.a);
       cudaEventDestroy(m.b);
@@ -519,9 +522,11 @@ int sj_fast::commit() {
       (rc = cudaMallocHost(&h_cu, (T + 1) * sizeof(int32_t))) ||
       (rc = cudaMallocHost(&h_kvl, T * sizeof(int32_t))))
     return cuda_fail(rc, "cudaMallocHost");
-  if ((rc = cudaEventCreateWithFlags(&staged_ev, cudaEventDisableTiming)))
+  if ((rc = cudaEventCreateWithFlags(&staged_ev, cudaEventDisableTiming)) ||
+      (rc = cudaEventCreateWithFlags(&inputs_ev, cudaEventDisableTiming)))
     return cuda_fail(rc, "cudaEventCreate");
-  if ((rc = cudaEventRecord(staged_ev, stream))) return cuda_fail(rc, "cudaEventRecord");
+  if ((rc = cudaEventRecord(staged_ev, stream)) || (rc = cudaEventRecord(inputs_ev, stream)))
+    return cuda_fail(rc, "cudaEventRecord");
   staged.clear();
   committed = true;
   return SJ_OK;
@@ -1032,7 +1037,10 @@ int sj_fast::host_call(const int64_t* ids_h, const int32_t* cu_h, const int32_t*
     if (b1 == b0)
       return fail(SJ_ERR_INVALID, "sequence longer than max_tokens");
     const int nb = b1 - b0, base = cu_h[b0], T = cu_h[b1] - base;
-    rc = cudaEventSynchronize(staged_ev);
+    // the host runs one pass ahead: it waits only until the previous pass's
+    // h_cu / h_kvl have reached the device (the device buffers are reused in
+    // stream order; forward() guards its own schedule upload)
+    rc = cudaEventSynchronize(inputs_ev);
     if (rc != cudaSuccess) return cuda_fail(rc, "cudaEventSynchronize");
     for (int b = 0; b <= nb; ++b) h_cu[b] = cu_h[b0 + b] - base;
     if (kvl_h) for (int b = 0; b < nb; ++b) h_kvl[b] = kvl_h[b0 + b];
@@ -1043,6 +1051,7 @@ int sj_fast::host_call(const int64_t* ids_h, const int32_t* cu_h, const int32_t*
         (kvl_h && (rc = cudaMemcpyAsync(kvl, h_kvl, nb * sizeof(int32_t),
                                         cudaMemcpyHostToDevice, stream))))
       return cuda_fail(rc, "cudaMemcpyAsync (inputs)");
+    if ((rc = cudaEventRecord(inputs_ev, stream))) return cuda_fail(rc, "cudaEventRecord");
     // h_cu is read by run() for the schedule; it is pinned host memory that
     // stays untouched until the next pass's event wait above.
     int s = run(ids, cu, h_cu, kvl_h ? kvl : nullptr, nb, (hidden_h || pooled_h) ? hid : nullptr,
@@ -1063,7 +1072,6 @@ int sj_fast::host_call(const int64_t* ids_h, const int32_t* cu_h, const int32_t*
                                          (size_t)nb * nout * sizeof(float),
                                          cudaMemcpyDeviceToHost, stream)))
       return cuda_fail(rc, "cudaMemcpyAsync (probs)");
-    if ((rc = cudaEventRecord(staged_ev, stream))) return cuda_fail(rc, "cudaEventRecord");
     b0 = b1;
   }
   return check_flags(stream);
