@@ -153,6 +153,14 @@ def test_c5_subset_vs_oracle():
     _subset_check(synth.SPECS["c5"], 24, 78)
 
 
+def test_c5_256_requests_vs_oracle():
+    """Config 5's four heads (choice-3, choice-8, score-5, noul) on 256
+    requests of its length distribution (lognormal(48, 0.8) in [4, 512]):
+    hidden states, logits, probabilities and labels at the bf16 bars."""
+    spec = synth.SPECS["c5"]
+    _subset_check(spec, 256, spec.seed + 2000)
+
+
 def test_c4_full_length_vs_oracle():
     """C4 at its full size per sequence: 24 layers x 1024, 16 heads, two
     sequences of 2048 tokens (the config's fixed length) against the C
