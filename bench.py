@@ -621,7 +621,7 @@ def ncu_case(precision: str = "bf16"):
     first call adds its bf16 calibration pass), then two launches of sj_attn on
     C4's attention shape at 16 x 2048 tokens (16 heads; attn_long).  A few GB
     on the device at most; inputs larger than L2 except where noted in the
-    summaries."""
+    summaries.  Last, two launches on the 64 x 512-token shape (12 heads)."""
     import torch
     from snapjudge_b200 import ops
     from snapjudge_b200.fast import FastSnapjudge
@@ -639,6 +639,12 @@ def ncu_case(precision: str = "bf16"):
     qkv = torch.randn(int(cu[-1]), 3 * 16 * 64, device="cuda").to(torch.bfloat16)
     for _ in range(2):
         o = ops.attn(qkv, cu, 16, 64)
+    # then two launches on the 64 x 512-token shape (12 heads; attn_long, 50 MB
+    # of Q/K/V: smaller than L2)
+    cu512 = synth.cu_seqlens(np.full(64, 512))
+    qkv512 = torch.randn(int(cu512[-1]), 3 * 12 * 64, device="cuda").to(torch.bfloat16)
+    for _ in range(2):
+        ops.attn(qkv512, cu512, 12, 64)
     torch.cuda.synchronize()
     eng.close()
     print(f"ncu case: {int(lengths.sum())} tokens, probs sum {float(probs.sum()):.3f}, "
