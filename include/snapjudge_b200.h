@@ -92,7 +92,9 @@ int sj_rope(sj_bf16* qkv, const float* cos_t, const float* sin_t, const int32_t*
  * Segment b = rows [cu_seqlens[b], cu_seqlens[b+1]); its queries attend keys
  * j < kv_lens[b] of the same segment (kv_lens NULL: the whole segment) and,
  * when window > 0, only |i - j| <= window.  softmax scale 1/sqrt(Dh), fp32
- * accumulation.  cu_seqlens_host mirrors cu_seqlens for the tile schedule.
+ * accumulation.  cu_seqlens_host mirrors cu_seqlens: the call orders the
+ * query tiles longest segment first from it (up to 2,048 tiles, passed in the
+ * launch's parameters; no allocation).
  * Replaces sj_attn (cuda/kernels.cu:351-357; lens + padded L there). */
 int sj_attn(const sj_bf16* qkv, const int32_t* cu_seqlens, const int32_t* cu_seqlens_host,
             const int32_t* kv_lens, sj_bf16* O, int B, int H, int Dh, int window, void* stream);

@@ -206,11 +206,22 @@ __device__ __forceinline__ Item decode(int w, const int2* tiles, int H, int nqt,
   return it;
 }
 
+// A query-tile list carried in the launch's own parameter block (NS > 1):
+// callers that allocate nothing still get a longest-first order, and every
+// launch has its own copy.  NS = 1: no list in the parameters.
+template <int NS>
+struct TileList {
+  int2 t[NS];
+};
+
+template <int NS>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     attn_tc_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapKV,
                    const int32_t* __restrict__ cu, const int32_t* __restrict__ kv_lens,
-                   bf16* __restrict__ O, int H, int window, const int2* __restrict__ tiles,
-                   int n_items, int nqt, int B, int* err, int inject, int long_min) {
+                   bf16* __restrict__ O, int H, int window, const int2* __restrict__ tiles_arg,
+                   int n_items, int nqt, int B, int* err, int inject, int long_min,
+                   const __grid_constant__ TileList<NS> plist) {
+  const int2* tiles = NS > 1 ? plist.t : tiles_arg;
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t q_full, kv_full[KV_STAGES], s_full, pv_done, drain;
   __shared__ Item items[2][CHUNK];  // this CTA's work items, chunk c in items[c & 1]
@@ -599,7 +610,7 @@ cudaError_t attn_tc(const bf16* qkv, const int32_t* cu, const int32_t* kv_lens, 
                     int H, int window, const int2* tiles, int n_tiles, int B, int max_seqlen,
                     int* err, cudaStream_t st, int long_min) {
   static std::atomic<uint64_t> attr_done{0};  // per device ordinal
-  if (cudaError_t rc = ensure_smem_attr(attn_tc_kernel, SMEM_BYTES, attr_done)) return rc;
+  if (cudaError_t rc = ensure_smem_attr(attn_tc_kernel<1>, SMEM_BYTES, attr_done)) return rc;
   if (T <= 0) return cudaSuccess;
   CUtensorMap mq, mkv;
   const uint64_t cols = 3ull * H * DH;
@@ -611,9 +622,34 @@ cudaError_t attn_tc(const bf16* qkv, const int32_t* cu, const int32_t* kv_lens, 
   if (items <= 0) return cudaSuccess;
   if (items > 0x7fffffff) return cudaErrorInvalidValue;
   const int grid = (int)std::min<long long>(items, (long long)kCtasPerSm * sm_count());
-  attn_tc_kernel<<<grid, kThreads, SMEM_BYTES, st>>>(mq, mkv, cu, kv_lens, O, H, window, tiles,
-                                                      (int)items, nqt, B, err,
-                                                      g_inject_timeout.load(), long_min);
+  attn_tc_kernel<1><<<grid, kThreads, SMEM_BYTES, st>>>(mq, mkv, cu, kv_lens, O, H, window,
+                                                         tiles, (int)items, nqt, B, err,
+                                                         g_inject_timeout.load(), long_min,
+                                                         TileList<1>{});
+  return cudaGetLastError();
+}
+
+cudaError_t attn_tc_host_list(const bf16* qkv, const int32_t* cu, const int32_t* kv_lens, bf16* O,
+                              int T, int H, int window, const int2* host_tiles, int n_tiles,
+                              int B, int* err, cudaStream_t st) {
+  static std::atomic<uint64_t> attr_done{0};  // per device ordinal
+  if (cudaError_t rc = ensure_smem_attr(attn_tc_kernel<kAttnTcListMax>, SMEM_BYTES, attr_done))
+    return rc;
+  if (n_tiles < 0 || n_tiles > kAttnTcListMax) return cudaErrorInvalidValue;
+  if (T <= 0 || n_tiles == 0) return cudaSuccess;
+  CUtensorMap mq, mkv;
+  const uint64_t cols = 3ull * H * DH;
+  if (!make_map_bf16(&mq, qkv, cols, T, cols * 2, DH, QT) ||
+      !make_map_bf16(&mkv, qkv, cols, T, cols * 2, DH, KT))
+    return cudaErrorInvalidValue;
+  const long long items = (long long)n_tiles * H;
+  if (items > 0x7fffffff) return cudaErrorInvalidValue;
+  static thread_local TileList<kAttnTcListMax> list;  // 16 KB: kept off the stack
+  std::copy(host_tiles, host_tiles + n_tiles, list.t);
+  const int grid = (int)std::min<long long>(items, (long long)kCtasPerSm * sm_count());
+  attn_tc_kernel<kAttnTcListMax><<<grid, kThreads, SMEM_BYTES, st>>>(
+      mq, mkv, cu, kv_lens, O, H, window, nullptr, (int)items, 0, B, err,
+      g_inject_timeout.load(), 0x7fffffff, list);
   return cudaGetLastError();
 }
 

@@ -5,7 +5,9 @@
 // same argument meaning, in packed varlen form, returning a status.  They
 // allocate nothing: every buffer is the caller's.  Shapes the tcgen05 kernels
 // take go to them; the rest run on the CUDA-core kernels (never on the host).
+#include <algorithm>
 #include <string>
+#include <vector>
 
 #include "../../include/snapjudge_b200.h"
 #include "common.cuh"
@@ -134,8 +136,37 @@ int sj_attn(const sj_bf16* qkv, const int32_t* cu_seqlens, const int32_t* cu_seq
       if (rc != SJ_OK) return rc;
       if (mn >= sjb::kAttnLongMin) return SJ_OK;  // no short segment left
     }
+    // the remaining segments' 128-row query tiles, longest segment first (the
+    // order of the engine's schedule), in the launch's parameter block when
+    // they fit; otherwise the kernel's own grid order
+    const int lmin = split ? sjb::kAttnLongMin : 0x7fffffff;
+    long long nt = 0;
+    for (int b = 0; b < B; ++b) {
+      const int n = cu_seqlens_host[b + 1] - cu_seqlens_host[b];
+      if (n < lmin) nt += (n + 127) / 128;
+    }
+    if (nt <= sjb::kAttnTcListMax) {
+      static thread_local std::vector<int> segs;
+      static thread_local std::vector<int2> tiles;
+      segs.clear();
+      tiles.clear();
+      for (int b = 0; b < B; ++b) {
+        const int n = cu_seqlens_host[b + 1] - cu_seqlens_host[b];
+        if (n > 0 && n < lmin) segs.push_back(b);
+      }
+      std::stable_sort(segs.begin(), segs.end(), [&](int x, int y) {
+        return cu_seqlens_host[x + 1] - cu_seqlens_host[x] >
+               cu_seqlens_host[y + 1] - cu_seqlens_host[y];
+      });
+      for (int b : segs)
+        for (int q0 = 0; q0 < cu_seqlens_host[b + 1] - cu_seqlens_host[b]; q0 += 128)
+          tiles.push_back(make_int2(b, q0));
+      return launched(sjb::attn_tc_host_list(q, cu_seqlens, kv_lens, o, T, H, window, tiles.data(),
+                                             (int)tiles.size(), B, nullptr, st),
+                      "attn_tc");
+    }
     return launched(sjb::attn_tc(q, cu_seqlens, kv_lens, o, T, H, window, nullptr, 0, B, ml,
-                                 nullptr, st, split ? sjb::kAttnLongMin : 0x7fffffff),
+                                 nullptr, st, lmin),
                     "attn_tc");
   }
   if (Dh != 8 && Dh != 16 && Dh != 32 && Dh != 64 && Dh != 128)

@@ -195,6 +195,13 @@ cudaError_t attn_noalloc_take_status(int* code);
 cudaError_t attn_tc(const bf16* qkv, const int32_t* cu, const int32_t* kv_lens, bf16* O, int T,
                     int H, int window, const int2* tiles, int n_tiles, int B, int max_seqlen,
                     int* err, cudaStream_t st, int long_min = 0x7fffffff);
+// The same kernel on a query-tile list given in HOST memory (at most
+// kAttnTcListMax tiles): the list travels in the launch's parameter block, so
+// the call allocates nothing and concurrent calls share no state.
+constexpr int kAttnTcListMax = 2048;
+cudaError_t attn_tc_host_list(const bf16* qkv, const int32_t* cu, const int32_t* kv_lens, bf16* O,
+                              int T, int H, int window, const int2* host_tiles, int n_tiles,
+                              int B, int* err, cudaStream_t st);
 
 // ---- tcgen05 flash attention for long segments (attn_long.cu) ----------------
 // Full-attention layers (no window) at head_dim 64 send segments of at least
