@@ -111,6 +111,9 @@ ATTN_CASES = [
     (12, 64, [300, 512, 1000, 777, 511, 64, 2], 0, [300, 100, 999, 1, 511, 64, 2]),
     (2, 64, [511, 512, 513, 639, 640, 641, 767], 0, None),
     (2, 64, [700, 600, 40], 0, [0, 37, 40]),
+    # empty segments among short ones (sj_attn's host-sorted tile list skips them)
+    (4, 64, [0, 130, 0, 5, 300, 0], 0, None),
+    (4, 64, [0, 130, 0, 5, 300, 0], 32, [0, 100, 0, 5, 299, 0]),
 ]
 
 
@@ -149,6 +152,21 @@ def test_attention_long_shapes(B, n, H):
     cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
     T = int(cu[-1])
     qkv = torch.randn(T, 3 * H * 64, generator=torch.Generator().manual_seed(B + n)).to(DEV).to(
+        torch.bfloat16)
+    O = f32(ops.attn(qkv, cu, H, 64)).reshape(T, H, 64)
+    x = f32(qkv).reshape(T, 3, H, 64)
+    want = oracle.attention_packed_np(x[:, 0], x[:, 1], x[:, 2], lens, dtype=np.float32)
+    assert_bf16_close(O, want, k=4.0)
+
+
+def test_attention_many_short_segments():
+    """More short-segment query tiles than sj_attn's parameter-block tile list
+    holds (2,048): the call falls back to the kernel's own grid order.  2,100
+    segments of 1-128 tokens, 2 heads, against the oracle."""
+    lens = np.random.default_rng(21).integers(1, 129, 2100)
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    T, H = int(cu[-1]), 2
+    qkv = torch.randn(T, 3 * H * 64, generator=torch.Generator().manual_seed(21)).to(DEV).to(
         torch.bfloat16)
     O = f32(ops.attn(qkv, cu, H, 64)).reshape(T, H, 64)
     x = f32(qkv).reshape(T, 3, H, 64)
